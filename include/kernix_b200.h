@@ -1,0 +1,215 @@
+/*
+ * kernix_b200.h -- C ABI of the B200 (sm_100a) dense-matmul path for Kernix.
+ *
+ * This is the drop-in boundary that a thin Rust FFI crate binds.  Every entry
+ * point takes plain pointers, sizes and layout descriptors (no C++ or torch
+ * types), returns an int status, and performs all validation on the host
+ * BEFORE any device work: a call that fails validation writes nothing.
+ *
+ * Reference interfaces replaced (paths inside the kernix repository):
+ *   - MatmulElement::try_dense_matmul   crates/kernix-ops/src/ops/matmul_element.rs:28-44,139-251
+ *   - MatmulElement::try_strided_matmul crates/kernix-ops/src/ops/matmul_element.rs:17-23,53-138
+ *   - MatrixInput::new                  crates/kernix-ops/src/ops/matmul_element.rs:262-300
+ *   - matmul / matmul_impl              crates/kernix-ops/src/ops/linalg.rs:31-44,68-214
+ *   - MatmulDevice<T>::matmul           crates/kernix-ops/src/execution.rs:25-36
+ *   - Device<T> upload/download/sync    crates/kernix-core/src/device.rs:22-35
+ *   - neural::conv2d / ConvGeometry     crates/kernix-ops/src/neural.rs:22-133,177-183
+ *   - softmax_temperature               crates/kernix-ops/src/ops/math_extra.rs:394-401,425-500,544-557
+ *   - CpuExecutor::matmul_into          crates/kernix-ops/src/execution.rs:149-240
+ *   - the C bridge convention           crates/kernix-ops/src/accelerate.c:15-30
+ *     (int status, caller-owned buffers, row-major output)
+ *
+ * Element units: every length, stride and origin is counted in ELEMENTS of the
+ * call's scalar type, as in kernix_core::Layout (layout/affine.rs:15-58).
+ */
+#ifndef KERNIX_B200_H
+#define KERNIX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KX_ABI_VERSION 1
+#define KX_MAX_RANK 8
+
+/* Status codes.  KX_OK: success, every output element written.
+ * KX_DECLINED mirrors a hook returning `false`: nothing was written and the
+ * caller may fall back (matmul_element.rs:17-44).  Codes 2..11 map 1:1 onto
+ * kernix OpsError / LayoutError variants (ops/error.rs:8-140). */
+typedef enum kx_status {
+    KX_OK = 0,
+    KX_DECLINED = 1,
+    KX_E_INVALID_RANK = 2,      /* OpsError::InvalidRank {operation, minimum, actual} */
+    KX_E_CONTRACT = 3,          /* OpsError::ContractDimensionMismatch {left, right} */
+    KX_E_BROADCAST = 4,         /* OpsError::BroadcastIncompatible {axis, left, right} */
+    KX_E_SHAPE_OVERFLOW = 5,    /* ShapeError::ElementCountOverflow {axis, accumulated, dim} */
+    KX_E_DIM_OVERFLOW = 6,      /* OpsError::DimensionOverflow {axis} */
+    KX_E_LAYOUT = 7,            /* LayoutError: span/storage/stride validation (values[0] = kx_layout_error) */
+    KX_E_PARAM = 8,             /* OpsError::InvalidParameter {operation, parameter} */
+    KX_E_EXACT_RANK = 9,        /* OpsError::ExactRank {operation, expected, actual} */
+    KX_E_NONFINITE = 10,        /* OpsError::NonFiniteInput {operation, indices} */
+    KX_E_AXIS = 11,             /* OpsError::AxisOutOfBounds {axis, rank} */
+    KX_E_ALIAS = 12,            /* output storage overlaps an input (Rust borrow rules forbid it) */
+    KX_E_CUDA = 13,             /* a CUDA runtime call failed (kx_error.cuda_error) */
+    KX_E_NO_DEVICE = 14,        /* no usable sm_100 device for this handle */
+    KX_E_TIMEOUT = 15,          /* a bounded device-side wait expired */
+    KX_E_UNSUPPORTED = 16       /* valid request outside this library's scope (e.g. rank > 8) */
+} kx_status;
+
+/* Sub-codes in kx_error.values[0] for KX_E_LAYOUT (layout/geometry.rs:40-80, affine.rs:186-199). */
+typedef enum kx_layout_error {
+    KX_LAYOUT_STRIDE_RANK_MISMATCH = 1,
+    KX_LAYOUT_ADDRESS_OVERFLOW = 2,
+    KX_LAYOUT_NEGATIVE_STORAGE_OFFSET = 3,
+    KX_LAYOUT_STORAGE_TOO_SMALL = 4,    /* values[1] = required, values[2] = available */
+    KX_LAYOUT_BYTE_EXTENT_OVERFLOW = 5,
+    KX_LAYOUT_OUTPUT_NOT_C_CONTIGUOUS = 6,
+    KX_LAYOUT_OUTPUT_SHAPE_MISMATCH = 7,
+    KX_LAYOUT_MISALIGNED_POINTER = 8
+} kx_layout_error;
+
+/* Structured error record (optional out-parameter, may be NULL).
+ * `values` carries the variant's integer fields in declaration order, e.g.
+ * InvalidRank -> {minimum, actual}, BroadcastIncompatible -> {axis, left, right},
+ * ElementCountOverflow -> {axis, accumulated, dim}. */
+typedef struct kx_error {
+    int32_t status;
+    int32_t cuda_error;
+    char operation[40];
+    char parameter[96];
+    uint64_t values[4];
+    uint32_t nindices;
+    uint64_t indices[KX_MAX_RANK];
+} kx_error;
+
+/* N-d strided tensor descriptor (mirror of kernix_core::Layout + storage).
+ * Element (i0..ir-1) lives at data[origin + sum_j i_j * strides[j]].
+ * `storage_len` is the number of elements addressable from `data`; the layout's
+ * reachable span must lie inside [0, storage_len) (Layout::validate_cpu_storage). */
+typedef struct kx_tensor {
+    void *data;
+    uint64_t storage_len;
+    uint64_t origin;
+    uint32_t rank;
+    uint32_t reserved;
+    uint64_t dims[KX_MAX_RANK];
+    int64_t strides[KX_MAX_RANK];
+} kx_tensor;
+
+/* Rank-2 strided matrix (mirror of MatrixInput {data, dims, strides, origin},
+ * matmul_element.rs:262-300).  Singleton strides are ignored, as MatrixInput::new
+ * normalises them to zero. */
+typedef struct kx_matrix {
+    const void *data;
+    uint64_t storage_len;
+    uint64_t dims[2];
+    int64_t strides[2];
+    uint64_t origin;
+} kx_matrix;
+
+/* Conv2dOptions (neural.rs:22-42): stride/padding/dilation per (y, x). */
+typedef struct kx_conv2d_options {
+    uint64_t stride[2];
+    uint64_t padding[2];
+    uint64_t dilation[2];
+    uint64_t groups;
+} kx_conv2d_options;
+
+/* Kernel family selection for f32 (f64 always runs on the FP64 pipe). */
+typedef enum kx_f32_variant {
+    KX_F32_AUTO = 0,    /* library chooses per shape and layout */
+    KX_F32_FFMA = 1,    /* SIMT FP32 FMA, fp32 accumulation */
+    KX_F32_3XTF32 = 2   /* split-TF32 tensor-core contraction (tcgen05 + TMEM) */
+} kx_f32_variant;
+
+typedef struct kx_handle kx_handle;
+
+/* ---- library / handle -------------------------------------------------- */
+int kx_abi_version(void);
+/* Number of CUDA devices visible (0 without a GPU).  Host only. */
+int kx_device_count(int *count);
+/* Create a handle bound to `device`.  Selects the device, checks sm_100, and
+ * creates no stream (the default stream is used until kx_set_stream). */
+int kx_create(int device, kx_handle **out, kx_error *err);
+int kx_destroy(kx_handle *h);
+/* Subsequent work on this handle is ordered on `stream` (a cudaStream_t). */
+int kx_set_stream(kx_handle *h, void *stream);
+int kx_set_f32_variant(kx_handle *h, int variant);
+/* Wait for outstanding work on the handle's stream (Device::synchronize). */
+int kx_synchronize(kx_handle *h, kx_error *err);
+
+/* ---- Device<T> buffers (device.rs:22-35) -------------------------------- */
+int kx_alloc(kx_handle *h, uint64_t bytes, void **out, kx_error *err);
+int kx_free(kx_handle *h, void *ptr);
+/* Synchronous transfers in physical order; complete before returning. */
+int kx_upload(kx_handle *h, void *dst_device, const void *src_host, uint64_t bytes, kx_error *err);
+int kx_download(kx_handle *h, void *dst_host, const void *src_device, uint64_t bytes, kx_error *err);
+
+/* ---- shape planning (host only; no device needed) ----------------------- */
+/* NumPy matmul output shape with the reference's error order
+ * (linalg.rs:77-116): rank-0 left, rank-0 right, contraction mismatch,
+ * batch broadcast, element-count overflow.  On success writes the output rank
+ * and dims (dims must hold KX_MAX_RANK entries). */
+int kx_matmul_shape(const uint64_t *a_dims, uint32_t a_rank,
+                    const uint64_t *b_dims, uint32_t b_rank,
+                    uint32_t *out_rank, uint64_t *out_dims, kx_error *err);
+/* ConvGeometry::new (neural.rs:91-125): output [n, co, oh, ow]. */
+int kx_conv2d_shape(const uint64_t *input_dims, uint32_t input_rank,
+                    const uint64_t *weight_dims, uint32_t weight_rank,
+                    const kx_conv2d_options *options, uint64_t *out_dims, kx_error *err);
+/* Validate a descriptor exactly as Layout::from_strides + validate_cpu_storage
+ * (affine.rs:43-58,186-199) for elements of `elem_bytes` bytes. */
+int kx_validate_tensor(const kx_tensor *t, uint32_t elem_bytes, kx_error *err);
+
+/* ---- device-resident operations (MatmulDevice / free functions) --------- */
+/* out = matmul(a, b) on device memory.  `out` must be C-contiguous with the
+ * dims returned by kx_matmul_shape and must not overlap a or b.  Arbitrary
+ * signed/zero strides and origins are read in place (no host copies). */
+int kx_matmul_f32(kx_handle *h, const kx_tensor *a, const kx_tensor *b, const kx_tensor *out, kx_error *err);
+int kx_matmul_f64(kx_handle *h, const kx_tensor *a, const kx_tensor *b, const kx_tensor *out, kx_error *err);
+
+/* conv2d on device memory: NCHW input (any strides), weight
+ * [out_channels, in_channels/groups, kh, kw] (any strides), C-contiguous out.
+ * im2col is fused into the operand load (no column buffer). */
+int kx_conv2d_f32(kx_handle *h, const kx_tensor *input, const kx_tensor *weight,
+                  const kx_conv2d_options *options, const kx_tensor *out, kx_error *err);
+int kx_conv2d_f64(kx_handle *h, const kx_tensor *input, const kx_tensor *weight,
+                  const kx_conv2d_options *options, const kx_tensor *out, kx_error *err);
+
+/* softmax_temperature(src, axis, temperature) into a C-contiguous `out` of the
+ * same dims.  Nonfinite input returns KX_E_NONFINITE with the C-order indices
+ * of the first nonfinite element in the reference's scan order; `out` is then
+ * unspecified (the reference returns no tensor). */
+int kx_softmax_temperature_f32(kx_handle *h, const kx_tensor *src, int64_t axis, float temperature,
+                               const kx_tensor *out, kx_error *err);
+int kx_softmax_temperature_f64(kx_handle *h, const kx_tensor *src, int64_t axis, double temperature,
+                               const kx_tensor *out, kx_error *err);
+
+/* ---- host-buffer hooks (MatmulElement) ---------------------------------- */
+/* try_dense_matmul: C-order a[m*k], b[k*n] -> out[m*n] in HOST memory.
+ * Returns KX_DECLINED (nothing written) on any length mismatch, exactly like
+ * the reference hook's `false`; KX_OK when all m*n outputs were written. */
+int kx_try_dense_matmul_f32(kx_handle *h, const float *a, uint64_t a_len, const float *b, uint64_t b_len,
+                            float *out, uint64_t out_len, uint64_t m, uint64_t k, uint64_t n);
+int kx_try_dense_matmul_f64(kx_handle *h, const double *a, uint64_t a_len, const double *b, uint64_t b_len,
+                            double *out, uint64_t out_len, uint64_t m, uint64_t k, uint64_t n);
+/* try_strided_matmul: validated signed-stride host matrices, C-order out[m*n]. */
+int kx_try_strided_matmul_f32(kx_handle *h, const kx_matrix *a, const kx_matrix *b, float *out, uint64_t out_len);
+int kx_try_strided_matmul_f64(kx_handle *h, const kx_matrix *a, const kx_matrix *b, double *out, uint64_t out_len);
+/* MatrixInput::new validation alone (host only). */
+int kx_matrix_validate(const kx_matrix *m, uint32_t elem_bytes, kx_error *err);
+
+/* ---- introspection ------------------------------------------------------ */
+/* Number of kernel launches this handle has issued since creation. */
+uint64_t kx_launch_count(const kx_handle *h);
+/* Name of the kernel family the last GEMM on this handle used. */
+const char *kx_last_kernel(const kx_handle *h);
+const char *kx_status_name(int status);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KERNIX_B200_H */

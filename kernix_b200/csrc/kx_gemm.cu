@@ -1,0 +1,132 @@
+// Kernel selection and launch for the SIMT strided GEMM (gemm_simt.cuh).
+#include "gemm_simt.cuh"
+#include "kx_internal.hpp"
+
+namespace kx {
+
+namespace {
+
+// 128x128 tiles, 8x8 outputs per thread, 256 threads (two CTAs per SM for f32).
+template <typename T> struct BigCfg;
+template <> struct BigCfg<float> : TileCfg<float, 128, 128, 16, 8, 8> {};
+template <> struct BigCfg<double> : TileCfg<double, 128, 128, 8, 8, 8> {};
+// 64x64 tiles, 4x4 per thread: more CTAs for small or split-K problems.
+template <typename T> struct SmallCfg;
+template <> struct SmallCfg<float> : TileCfg<float, 64, 64, 16, 4, 4> {};
+template <> struct SmallCfg<double> : TileCfg<double, 64, 64, 16, 4, 4> {};
+
+template <typename T, typename Cfg, int AM, int BMD>
+cudaError_t launch_one(const GemmParams<T> &p, cudaStream_t s) {
+    const int64_t tiles = (int64_t)((p.M + Cfg::BM - 1) / Cfg::BM) * ((p.N + Cfg::BN - 1) / Cfg::BN);
+    const int64_t z = p.nbatch * p.splits;
+    dim3 grid((unsigned)tiles, (unsigned)(z < 65535 ? z : 65535), 1);
+    gemm_simt_kernel<T, Cfg, AM, BMD><<<grid, Cfg::NT, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
+template <typename T, typename Cfg, int AM>
+cudaError_t launch_b(const GemmParams<T> &p, int bmode, cudaStream_t s) {
+    switch (bmode) {
+        case kVecK: return launch_one<T, Cfg, AM, kVecK>(p, s);
+        case kVecMN: return launch_one<T, Cfg, AM, kVecMN>(p, s);
+        case kGatherMN: return launch_one<T, Cfg, AM, kGatherMN>(p, s);
+        default: return launch_one<T, Cfg, AM, kGatherK>(p, s);
+    }
+}
+
+template <typename T, typename Cfg>
+cudaError_t launch_cfg(const GemmParams<T> &p, int amode, int bmode, cudaStream_t s) {
+    switch (amode) {
+        case kVecK: return launch_b<T, Cfg, kVecK>(p, bmode, s);
+        case kVecMN: return launch_b<T, Cfg, kVecMN>(p, bmode, s);
+        case kGatherMN: return launch_b<T, Cfg, kGatherMN>(p, bmode, s);
+        default: return launch_b<T, Cfg, kGatherK>(p, bmode, s);
+    }
+}
+
+inline int64_t iabs(int64_t v) { return v < 0 ? -v : v; }
+
+// Operand access mode.  `s_r` is the stride along m (A) or n (B), `s_k` along k,
+// `R` the extent along m/n.  `batch_ok` says every batch stride and the origin
+// keep vector alignment.
+template <typename T>
+int pick_mode(const T *base, int64_t s_r, int64_t s_k, int64_t R, int64_t K, bool batch_ok) {
+    constexpr int W = Vec<T>::width;
+    const bool aligned = batch_ok && (reinterpret_cast<uintptr_t>(base) % (W * sizeof(T)) == 0);
+    if (aligned && s_k == 1 && K % W == 0 && s_r % W == 0) return kVecK;
+    if (aligned && s_r == 1 && R % W == 0 && s_k % W == 0) return kVecMN;
+    return iabs(s_r) <= iabs(s_k) ? kGatherMN : kGatherK;
+}
+
+}  // namespace
+
+template <typename T>
+int run_gemm(Handle *h, GemmParams<T> p, const char **kernel_name) {
+    constexpr int W = Vec<T>::width;
+    bool a_batch_ok = true, b_batch_ok = true;
+    for (int d = 0; d < p.batch.ndims; ++d) {
+        a_batch_ok &= (p.batch.a_str[d] % W) == 0;
+        b_batch_ok &= (p.batch.b_str[d] % W) == 0;
+    }
+    const int amode = pick_mode<T>(p.A, p.a_rs, p.a_cs, p.M, p.K, a_batch_ok);
+    const int bmode = pick_mode<T>(p.B, p.b_cs, p.b_rs, p.N, p.K, b_batch_ok);
+
+    using Big = BigCfg<T>;
+    using Small = SmallCfg<T>;
+    const int64_t target = 2LL * h->sm_count;  // two resident CTAs per SM
+    const int64_t big_tiles = (int64_t)((p.M + Big::BM - 1) / Big::BM) * ((p.N + Big::BN - 1) / Big::BN);
+    const int64_t small_tiles = (int64_t)((p.M + Small::BM - 1) / Small::BM) * ((p.N + Small::BN - 1) / Small::BN);
+    if (big_tiles > INT32_MAX || small_tiles > INT32_MAX) return KX_E_UNSUPPORTED;
+
+    p.splits = 1;
+    p.k_per_split = p.K;
+    p.ws = nullptr;
+    cudaError_t ce;
+    if (big_tiles * p.nbatch >= target) {
+        *kernel_name = "simt_128x128";
+        ce = launch_cfg<T, Big>(p, amode, bmode, h->stream);
+        ++h->launches;
+    } else {
+        // Split K so that the grid fills the machine; each split keeps at least
+        // four k-tiles so the pipeline stays primed.
+        int64_t ctas = small_tiles * p.nbatch;
+        int splits = 1;
+        if (ctas < target) {
+            int64_t want = (target + ctas - 1) / ctas;
+            int64_t max_splits = p.K / (4 * Small::BK);
+            if (max_splits < 1) max_splits = 1;
+            splits = (int)(want < max_splits ? want : max_splits);
+        }
+        if (splits > 1) {
+            int64_t kps = (p.K + splits - 1) / splits;
+            kps = (kps + Small::BK - 1) / Small::BK * Small::BK;
+            splits = (int)((p.K + kps - 1) / kps);
+            p.k_per_split = (int)kps;
+        }
+        p.splits = splits;
+        if (splits > 1) {
+            const uint64_t need = (uint64_t)splits * p.nbatch * (uint64_t)p.M * p.N * sizeof(T);
+            int rc = h->workspace(need, reinterpret_cast<void **>(&p.ws));
+            if (rc) return rc;
+            *kernel_name = "simt_64x64_splitk";
+        } else {
+            *kernel_name = "simt_64x64";
+        }
+        ce = launch_cfg<T, Small>(p, amode, bmode, h->stream);
+        ++h->launches;
+        if (ce == cudaSuccess && splits > 1) {
+            const int64_t total = p.nbatch * (int64_t)p.M * p.N;
+            int64_t blocks = (total + 255) / 256;
+            if (blocks > 8LL * h->sm_count) blocks = 8LL * h->sm_count;
+            splitk_reduce_kernel<T><<<(unsigned)blocks, 256, 0, h->stream>>>(p);
+            ce = cudaGetLastError();
+            ++h->launches;
+        }
+    }
+    return ce == cudaSuccess ? KX_OK : h->cuda_fail(ce);
+}
+
+template int run_gemm<float>(Handle *, GemmParams<float>, const char **);
+template int run_gemm<double>(Handle *, GemmParams<double>, const char **);
+
+}  // namespace kx

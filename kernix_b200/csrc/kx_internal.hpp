@@ -1,0 +1,75 @@
+// Internal handle state shared by the C-ABI translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "kx_host.hpp"
+
+namespace kx {
+
+template <typename T> struct GemmParams;
+
+// One handle per (device, caller thread).  Owns a growable device workspace
+// (split-K partials, host-hook staging) and a small flag area for device-side
+// status words.  Not thread-safe: use one handle per thread/stream.
+struct Handle {
+    int device = 0;
+    int sm_count = 148;
+    cudaStream_t stream = nullptr;
+    int f32_variant = KX_F32_AUTO;
+    uint64_t launches = 0;
+    const char *last_kernel = "none";
+    int last_cuda_error = 0;
+
+    void *ws = nullptr;          // split-K partials
+    uint64_t ws_bytes = 0;
+    void *stage[3] = {nullptr, nullptr, nullptr};   // host-hook device staging (a, b, out)
+    uint64_t stage_bytes[3] = {0, 0, 0};
+    uint32_t *flags = nullptr;   // device status words (nonfinite index, timeouts)
+    static constexpr int kFlagWords = 64;
+
+    int cuda_fail(cudaError_t ce) {
+        last_cuda_error = (int)ce;
+        return KX_E_CUDA;
+    }
+    // Grow-only device buffer.  Growing synchronises the stream first so that
+    // no queued kernel still reads the old allocation.
+    int grow(void **buf, uint64_t *cap, uint64_t need) {
+        if (need <= *cap) return KX_OK;
+        if (*buf) {
+            cudaError_t ce = cudaStreamSynchronize(stream);
+            if (ce != cudaSuccess) return cuda_fail(ce);
+            cudaFree(*buf);
+            *buf = nullptr;
+            *cap = 0;
+        }
+        uint64_t bytes = need < (1u << 20) ? (1u << 20) : need;
+        cudaError_t ce = cudaMalloc(buf, bytes);
+        if (ce != cudaSuccess) {
+            *buf = nullptr;
+            return cuda_fail(ce);
+        }
+        *cap = bytes;
+        return KX_OK;
+    }
+    int workspace(uint64_t need, void **out) {
+        int rc = grow(&ws, &ws_bytes, need);
+        if (rc == KX_OK) *out = ws;
+        return rc;
+    }
+};
+
+// Error record for a failed CUDA call.
+inline int cuda_err(kx_error *e, Handle *h, const char *op) {
+    set_err(e, KX_E_CUDA, op, cudaGetErrorString((cudaError_t)h->last_cuda_error));
+    if (e) e->cuda_error = h->last_cuda_error;
+    return KX_E_CUDA;
+}
+
+template <typename T> int run_gemm(Handle *h, GemmParams<T> p, const char **kernel_name);
+
+}  // namespace kx
+
+struct kx_handle {
+    kx::Handle impl;
+};

@@ -1,0 +1,193 @@
+"""Pin the CPU oracle to the reference's own known answers (CPU only).
+
+The reference (Rust) cannot be built in this image, so the oracle is trusted
+only after it reproduces every literal known answer and exact-dyadic property
+of Kernix's matmul/conv/softmax tests (values in tests/golden/kats.json).
+"""
+import json
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+from golden import golden as G
+from kernix_b200 import rng
+
+KATS = json.loads((Path(__file__).parent / "golden" / "kats.json").read_text())
+
+
+def _view(spec, dtype):
+    if "storage" in spec:
+        return oracle.View(np.asarray(spec["storage"], dtype=dtype), spec["dims"], spec["strides"], spec["origin"])
+    return oracle.View.of(np.asarray(spec["values"], dtype=dtype).reshape(spec["dims"]))
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("case", KATS["matmul_int"], ids=lambda c: c["cite"].split()[-1])
+def test_matmul_known_answers(case, dtype):
+    out = oracle.matmul_reference(_view(case["a"], dtype), _view(case["b"], dtype))
+    assert list(out.shape) == case["out_dims"]
+    assert out.reshape(-1).tolist() == case["out"]
+
+
+@pytest.mark.parametrize("case", KATS["matmul_errors"], ids=lambda c: c["error"])
+def test_matmul_error_known_answers(case):
+    if case["error"] == "CapacityOverflow":
+        out, _, _ = oracle.matmul_shape(case["a_dims"], case["b_dims"])
+        n = math.prod(out)
+        assert n * 8 > (1 << 63) - 1 and n == case["fields"]["len"]
+        return
+    with pytest.raises(oracle.OracleError) as e:
+        oracle.matmul_shape(case["a_dims"], case["b_dims"])
+    assert e.value.kind == case["error"]
+    assert e.value.fields == case["fields"]
+
+
+def test_matmul_empty_output_shapes():
+    for case in KATS["matmul_empty_ok"]:
+        out, _, _ = oracle.matmul_shape(case["a_dims"], case["b_dims"])
+        assert out == case["out_dims"]
+
+
+@pytest.mark.parametrize("pair", KATS["batched_shapes"]["pairs"], ids=str)
+def test_batched_geometry_shapes_and_values(pair):
+    a_dims, b_dims, out_dims = pair
+    a = G.batched_values(a_dims, "left")
+    b = G.batched_values(b_dims, "right")
+    out = oracle.matmul_reference(oracle.View.of(a), oracle.View.of(b))
+    assert list(out.shape) == out_dims
+    np.testing.assert_allclose(out, np.matmul(a, b) if a.size and b.size else np.zeros(out_dims), rtol=0,
+                               atol=2e-13 * (1 + np.abs(out).max(initial=0)))
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_dyadic_boundary_grid_is_exact(dtype):
+    """small_matmul_tests.rs:59-106: dyadic data makes every sum exact."""
+    for m in G.DYADIC_M:
+        for k in G.DYADIC_K:
+            for n in G.DYADIC_N:
+                av, bv = G.dyadic_pair(m, k, n, dtype)
+                a, b = av[1:], bv[1:]
+                got = oracle.dense_matmul(a, b, m, k, n)
+                exact = (a.astype(np.float64).reshape(m, k) @ b.astype(np.float64).reshape(k, n)).reshape(-1)
+                assert np.array_equal(got.astype(np.float64), exact), (m, k, n)
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("shape", G.GAPPED_SHAPES)
+def test_gapped_positive_strides_are_exact(shape, dtype):
+    """native_kernel_tests.rs:243-294."""
+    m, k, n = shape
+    a, (ars, acs), ao, b, (brs, bcs), bo = G.gapped_strides(m, k, n, dtype)
+    va = oracle.View(a, (m, k), (ars, acs), ao)
+    vb = oracle.View(b, (k, n), (brs, bcs), bo)
+    got = oracle.matmul_reference(va, vb)
+    exact = va.to_array().astype(np.float64) @ vb.to_array().astype(np.float64)
+    assert np.array_equal(got.astype(np.float64), exact)
+
+
+@pytest.mark.parametrize("shape", G.F32_BOUNDARY_SHAPES)
+def test_f32_ordered_within_reference_bound_of_f64(shape):
+    """native_kernel_tests.rs:139-181: |f32 - f64| < 1e-5 (1 + |y|)."""
+    m, k, n = shape
+    a, b = G.f32_boundary_pair(m, k, n)
+    got = oracle.dense_matmul(a.reshape(-1), b.reshape(-1), m, k, n).reshape(m, n).astype(np.float64)
+    exp = a.astype(np.float64) @ b.astype(np.float64)
+    assert (np.abs(got - exp) < 1e-5 * (1 + np.abs(exp))).all()
+
+
+def test_dot2_oracle_matches_exact_rational_sum():
+    """The compensated oracle reproduces a hard cancellation exactly."""
+    a = np.array([[1e16, 1.0, -1e16]], dtype=np.float64)
+    b = np.array([[1.0], [1.0], [1.0]], dtype=np.float64)
+    out, ab = oracle.gemm_dot2(oracle.View.of(a), oracle.View.of(b), threads=1)
+    assert out[0, 0] == 1.0 and ab[0, 0] == 2e16 + 1.0
+
+
+def test_conv_hand_oracle():
+    """neural_vision_tests.rs:29-46 (and its reversed view)."""
+    c = KATS["conv_hand"]
+    x = np.asarray(c["x"]["values"], dtype=np.float64).reshape(c["x"]["dims"])
+    w = np.asarray(c["w"]["values"], dtype=np.float64).reshape(c["w"]["dims"])
+    assert oracle.conv2d_reference(oracle.View.of(x), oracle.View.of(w)).reshape(-1).tolist() == c["out"]
+    # reverse_axis(3): stride -1 on the last axis, origin at the last column.
+    xr = oracle.View(x.reshape(-1), (1, 1, 3, 3), (9, 3, 3, -1), 2)
+    assert oracle.conv2d_reference(xr, oracle.View.of(w)).reshape(-1).tolist() == c["out_x_reversed_axis3"]
+
+
+def test_conv_geometry_errors():
+    c = KATS["conv_errors"]
+    for case in c["cases"]:
+        opts = dict(stride=(1, 1), padding=(0, 0), dilation=(1, 1), groups=1)
+        for k, v in case["options"].items():
+            opts[k] = tuple(v) if isinstance(v, list) else v
+        if "error" in case:
+            with pytest.raises(oracle.OracleError) as e:
+                oracle.conv_shape(c["x_dims"], c["w_dims"], **opts)
+            assert e.value.kind == case["error"]
+        else:
+            assert oracle.conv_shape(c["x_dims"], c["w_dims"], **opts) == case["out_dims"]
+
+
+@pytest.mark.parametrize("options", G.CONV_OPTIONS, ids=["default", "grouped_dilated_padded"])
+def test_conv_reference_matches_compensated(options):
+    """native_kernel_tests.rs:201-241 tolerance 1e-13 (1 + |y|)."""
+    x, w = G.conv_inputs(4, options["groups"])
+    ref = oracle.conv2d_reference(oracle.View.of(x), oracle.View.of(w), **options)
+    d2, _ = oracle.conv2d_dot2(oracle.View.of(x), oracle.View.of(w), **options)
+    assert (np.abs(ref - d2) < 1e-13 * (1 + np.abs(d2))).all()
+
+
+def test_softmax_known_answers():
+    s = KATS["softmax"]
+    x = np.array([[1000.0, 1001.0]])
+    y = oracle.softmax_temperature(x, -1, 2.0)
+    assert abs(y[0, 1] - 1.0 / (1.0 + math.exp(-0.5))) < 1e-15
+    huge = np.array([2.0e38, 2.0e38], dtype=np.float32)
+    assert oracle.softmax_temperature(huge, -1, 0.001).tolist() == s[1]["out"]
+    mx = np.finfo(np.float64).max
+    y = oracle.softmax_temperature(np.array([mx, -mx]), 0, mx)
+    e = 1.0 / (1.0 + math.exp(-2.0))
+    assert abs(y[0] - e) < 1e-14 and abs(y[1] - (1 - e)) < 1e-14
+    for t in (0.0, -1.0, float("nan"), float("inf")):
+        with pytest.raises(oracle.OracleError):
+            oracle.softmax_temperature(x, 1, t)
+
+
+def test_softmax_first_nonfinite_in_scan_order():
+    x = np.zeros((3, 4, 5))
+    x[2, 1, 3] = np.inf
+    x[1, 3, 0] = np.nan
+    with pytest.raises(oracle.OracleError) as e:
+        oracle.softmax_temperature(x, 1, 1.0)
+    # rows are the (axis-0, axis-2) pairs in C order; (1, *, 0) precedes (2, *, 3)
+    assert e.value.fields["indices"] == [1, 3, 0]
+
+
+def test_splitmix64_published_vector_and_numpy_generator():
+    hexes = KATS["splitmix64_seed0"]["first_outputs_hex"]
+    state = 0
+    for h in hexes:
+        v, state = oracle.splitmix_next(state)
+        assert v == int(h, 16)
+    assert np.array_equal(rng.splitmix_block(0, 0, 3), np.array([int(h, 16) for h in hexes], dtype=np.uint64))
+    for seed in (0, 5, 2**63 + 11):
+        assert np.array_equal(rng.uniform(seed, 4099, -1.0, 1.0), oracle.uniform(seed, 4099, -1.0, 1.0))
+        assert np.array_equal(rng.uniform(seed, 777, -3.0, 2.0, np.float64),
+                              oracle.uniform(seed, 777, -3.0, 2.0, np.float64))
+
+
+def test_normal_generator_moments():
+    z = rng.normal(1, 200001)
+    assert abs(z.mean()) < 0.01 and abs(z.std() - 1) < 0.01
+    assert np.isfinite(z).all()
+
+
+def test_parallel_ordered_equals_serial():
+    a = rng.uniform(3, 129 * 67, -1, 1).reshape(129, 67)
+    b = rng.uniform(4, 67 * 33, -1, 1).reshape(67, 33)
+    ser = oracle.dense_matmul(a.reshape(-1), b.reshape(-1), 129, 67, 33).reshape(129, 33)
+    par = oracle.gemm_ordered_par(oracle.View.of(a), oracle.View.of(b), threads=4)
+    assert np.array_equal(ser, par)
