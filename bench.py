@@ -1,0 +1,472 @@
+#!/usr/bin/env python3
+"""Benchmark of Kernix's dense matmul path on B200.
+
+Default workload (the headline configuration): f32 GEMM M=N=K=8192 where A is a
+non-contiguous strided slice (row stride 8704) of an 8192 x 8704 buffer, entries
+uniform[-1,1] from SplitMix64 seeds 5 (A buffer) and 6 (B).  Rows of M are
+sharded block-cyclically over the GPUs and the output is all-gathered over
+NVLink, so ``scaling`` is strong (fixed total work).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under ``python -m torch.distributed.run --nproc-per-node N``.  Rank 0
+prints one JSON line.  ``--config c1..c5`` selects the other configurations
+(parity-test cases, reported in the design notes, not bench lines).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SEEDS = {"c1": (0,), "c2": (1,), "c3": (2,), "c4": (3, 4), "c5": (5, 6)}
+CONFIG_TEXT = {
+    "c1": "f32 GEMM 512^3, row-major contiguous",
+    "c2": "f64 GEMM 4096^3, B a transposed (column-major) view",
+    "c3": "batched f32 attention products 16x32 heads, seq 2048, d 128: S=QK^T, softmax(S/sqrt(128)), PV",
+    "c4": "f32 conv2d NCHW 64x128x56x56, 3x3, 256 out, stride 1, pad 1 (implicit GEMM)",
+    "c5": "f32 GEMM 8192^3, A strided slice (row stride 8704), rows sharded, output all-gathered",
+}
+METRIC = "GEMM TFLOP/s (f32, f64) at 1/2/4/8 B200 and % of pipe peak vs host-CPU ref"
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "sm_max_mhz": 1965.0}, \
+        "fallback"
+
+
+def pipe_peak(pipe: str, peaks: dict, sm_mhz: float) -> tuple[float, str]:
+    """Peak of the pipe the dominant kernel runs on, in TFLOP/s.
+
+    FP32 SIMT and FP64 are derived from the SM clock (148 SMs x 128 FP32 or 64
+    FP64 lanes x 2 flops); TF32 tensor is half the measured dense bf16 rate and
+    3xTF32 a third of that."""
+    if pipe == "fp32-simt":
+        return 148 * 128 * 2 * sm_mhz * 1e6 / 1e12, f"derived: 148 SM x 128 FP32 lanes x 2 x {sm_mhz:.0f} MHz"
+    if pipe == "fp64":
+        return 148 * 64 * 2 * sm_mhz * 1e6 / 1e12, f"derived: 148 SM x 64 FP64 lanes x 2 x {sm_mhz:.0f} MHz"
+    if pipe == "3xtf32":
+        return peaks["bf16_tflops"] / 2 / 3, "measured bf16 dense / 2 (tf32) / 3 (three products)"
+    raise ValueError(pipe)
+
+
+# ---------------------------------------------------------------------------
+# clocks (NVML reads only; no setting is changed)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, index: int, period: float = 0.1):
+        self.samples, self.reasons = [], set()
+        self.period = period
+        self._stop = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.dev = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.dev, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.dev, self.nv.NVML_CLOCK_SM))
+                mask = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.dev)
+                for name, bit in self.REASONS.items():
+                    if mask & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons)}
+        return {"sm_mhz": float(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# workload: c5 (headline)
+# ---------------------------------------------------------------------------
+M = N = K = 8192
+ROW_STRIDE = 8704
+
+
+def a_rows(rows: list[int], out: np.ndarray) -> np.ndarray:
+    """Rows of the seed-5 8192 x 8704 buffer, in the given order, written into
+    ``out`` (the stream is counter-based: runs of rows generate directly)."""
+    from kernix_b200 import rng
+    i = 0
+    while i < len(rows):
+        j = i
+        while j + 1 < len(rows) and rows[j + 1] == rows[j] + 1:
+            j += 1
+        r0, cnt = rows[i], j - i + 1
+        rng.uniform(SEEDS["c5"][0], cnt * ROW_STRIDE, -1.0, 1.0, np.float32,
+                    out=out[i * ROW_STRIDE:(i + cnt) * ROW_STRIDE], start=r0 * ROW_STRIDE)
+        i = j + 1
+    return out
+
+
+def run_ours(args, rank, world, local):
+    import torch
+    import torch.distributed as dist
+    import kernix_b200 as kx
+    from kernix_b200 import rng
+    from kernix_b200.sharded import plan_rows, sharded_matmul
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    h = kx.handle(local)
+    plan = plan_rows(M, world, target_piece=args.piece if world > 1 else M)
+    my_rows = plan.local_rows(rank)
+    # Host inputs (pinned): this rank's rows of the A buffer, and B.
+    a_host = torch.empty(len(my_rows) * ROW_STRIDE, dtype=torch.float32, pin_memory=True)
+    a_rows(my_rows, a_host.numpy())
+    b_host = torch.empty(K * N, dtype=torch.float32, pin_memory=True)
+    rng.uniform(SEEDS["c5"][1], K * N, -1.0, 1.0, np.float32, out=b_host.numpy())
+    a_buf = a_host.to(dev)
+    b = b_host.to(dev).view(K, N)
+    c = torch.empty(M, N, dtype=torch.float32, device=dev)
+    # piece i of this rank: rows [i*piece, (i+1)*piece) of the local buffer,
+    # viewed with the 8704 row stride (first 8192 columns)
+    pieces = [kx.TensorView(a_buf, (plan.piece, K), (ROW_STRIDE, 1), i * plan.piece * ROW_STRIDE)
+              for i in range(plan.pieces)]
+    scratch = [torch.empty(plan.piece, N, dtype=torch.float32, device=dev) for _ in range(plan.pieces)] \
+        if world > 1 else None
+    streams = (torch.cuda.current_stream(dev), torch.cuda.Stream(dev)) if world > 1 else None
+    group = dist.group.WORLD if world > 1 else None
+
+    def step():
+        sharded_matmul(pieces, b, c, plan, rank, group, streams=streams, scratch=scratch)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    # warm-up
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    # kernel-only timing of one GEMM launch (dominant kernel) for the roofline
+    kern_ms = time_dominant_kernel(h, pieces, b, c, plan, dev)
+    barrier()
+    launches0 = h.launches
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        barrier()
+    launches = h.launches - launches0
+    elapsed = start.elapsed_time(end) / 1e3
+    t = torch.tensor([elapsed], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed = float(t.item())
+    flops = 2.0 * M * N * K
+    value = flops * args.steps / elapsed / 1e12
+
+    # end-to-end through the public API with host buffers
+    e2e = None if args.no_e2e else e2e_run(args, rank, world, local, a_host, b_host, plan, kx, dist, group)
+    # correctness spot check of the timed output: a checksum of rows
+    check = spot_check(c, a_host, b_host, plan, rank) if rank == 0 else None
+
+    result = None
+    if rank == 0:
+        peaks, peak_src = measured_peaks()
+        clocks = clk.summary()
+        pipe = "fp32-simt"
+        kname = h.last_kernel
+        if "tf32" in kname:
+            pipe = "3xtf32"
+        sm_max = clocks.get("sm_max_mhz") or peaks.get("sm_max_mhz", 1965.0)
+        peak, basis = pipe_peak(pipe, peaks, float(sm_max))
+        per_launch_flops = 2.0 * plan.piece * N * K
+        achieved = per_launch_flops / (kern_ms / 1e3) / 1e12
+        traffic = load_traffic(kname, plan.piece)
+        result = {
+            "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(elapsed * 1e3 / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (SplitMix64 seeds 5, 6)",
+            "config": {"workload": "c5: " + CONFIG_TEXT["c5"], "M": M, "N": N, "K": K, "a_row_stride": ROW_STRIDE,
+                       "parallelism": f"rows{world} block-cyclic piece={plan.piece} + all-gather",
+                       "l2": "inputs larger than L2 (A span 285 MB, B 268 MB)", "kernel": kname},
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "roofline": {"bound": "tensor", "pipe": pipe, "achieved": round(achieved, 3), "peak": round(peak, 3),
+                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "peak_basis": basis + (" (of measured)" if pipe == "3xtf32" and peak_src == "measured"
+                                                else ""),
+                         "kernel": kname, "kernel_ms": round(kern_ms, 4),
+                         "launch_flops": per_launch_flops},
+            "clocks": clocks,
+            "check": check,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_seconds)
+    return result
+
+
+def time_dominant_kernel(h, pieces, b, c, plan, dev, reps=5):
+    """Average duration of one GEMM launch (one piece) with CUDA events on the
+    stream the kernel runs on."""
+    import torch
+    import kernix_b200 as kx
+    out = c[:plan.piece]
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kx.matmul_into(pieces[0], b, out)
+    torch.cuda.synchronize(dev)
+    s.record()
+    for _ in range(reps):
+        kx.matmul_into(pieces[0], b, out)
+    e.record()
+    e.synchronize()
+    return s.elapsed_time(e) / reps
+
+
+def e2e_run(args, rank, world, local, a_host, b_host, plan, kx, dist, group):
+    """Same metric measured through the public API from pinned host buffers.
+
+    N=1: ``try_strided_matmul`` -- the reference-facing MatmulElement hook --
+    on the host A view (row stride 8704) and B, result read back to host.
+    N>1: host->device copy of this rank's A rows and B, the sharded matmul with
+    its all-gather, and rank 0 reads C back."""
+    import torch
+    from kernix_b200.sharded import sharded_matmul
+    dev = torch.device("cuda", local)
+    steps = max(1, min(args.steps, 5))
+    if world == 1:
+        a_np, b_np = a_host.numpy(), b_host.numpy()
+        out = torch.empty(M * N, dtype=torch.float32, pin_memory=True).numpy()
+        ma = kx.MatrixInput(a_np, [M, K], [ROW_STRIDE, 1], 0)
+        mb = kx.MatrixInput(b_np, [K, N], [N, 1], 0)
+        assert kx.try_strided_matmul(ma, mb, out)   # warm (allocates staging)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            ok = kx.try_strided_matmul(ma, mb, out)
+            assert ok
+        dt = (time.perf_counter() - t0) / steps
+        h2d = ((M - 1) * ROW_STRIDE + K) * 4 + K * N * 4
+        d2h = M * N * 4
+    else:
+        a_dev = torch.empty_like(a_host, device=dev)
+        b_dev = torch.empty(K, N, dtype=torch.float32, device=dev)
+        c = torch.empty(M, N, dtype=torch.float32, device=dev)
+        c_host = torch.empty(M, N, dtype=torch.float32, pin_memory=True) if rank == 0 else None
+        pieces = [kx.TensorView(a_dev, (plan.piece, K), (ROW_STRIDE, 1), i * plan.piece * ROW_STRIDE)
+                  for i in range(plan.pieces)]
+
+        def one():
+            a_dev.copy_(a_host, non_blocking=True)
+            b_dev.view(-1).copy_(b_host, non_blocking=True)
+            sharded_matmul(pieces, b_dev, c, plan, rank, group)
+            if rank == 0:
+                c_host.copy_(c, non_blocking=True)
+            torch.cuda.synchronize(dev)
+        one()
+        dist.barrier(device_ids=[local])
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            one()
+        dist.barrier(device_ids=[local])
+        dt = (time.perf_counter() - t0) / steps
+        t = torch.tensor([dt], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+        h2d = (a_host.numel() * 4 + K * N * 4) * world
+        d2h = M * N * 4
+    return {"value": round(2.0 * M * N * K / dt / 1e12, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "ms_per_step": round(dt * 1e3, 3), "steps": steps,
+            "api": "try_strided_matmul (C-ABI hook)" if world == 1 else "sharded_matmul + torch H2D/D2H"}
+
+
+def spot_check(c, a_host, b_host, plan, rank):
+    """Check of the timed (gathered) output: four rows this rank holds in its A
+    buffer must match the compensated oracle within the f32 scaled bound
+    |x - y| <= 2e-6 sum|a b| (small_matmul_tests.rs:153-186)."""
+    import oracle
+    a = a_host.numpy()
+    b = b_host.numpy().reshape(K, N)
+    local = plan.local_rows(rank)
+    picks = sorted({0, 1, len(local) // 2 + 3, len(local) - 1})
+    worst = 0.0
+    for li in picks:
+        r = local[li]
+        va = oracle.View(a, (1, K), (ROW_STRIDE, 1), li * ROW_STRIDE)
+        want, ab = oracle.gemm_dot2(va, oracle.View.of(b))
+        got = c[r].cpu().numpy().astype(np.float64)
+        worst = max(worst, float(np.max(np.abs(got - want[0]) / ab[0])))
+    return {"rows_checked": len(picks), "max_err_over_sum_abs": worst, "bound": 2e-6, "pass": worst <= 2e-6}
+
+
+def load_traffic(kernel: str, piece_rows: int):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu
+    summary (scaled to this launch's rows when captured on a smaller case)."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    e = d.get(kernel)
+    if not e:
+        return None
+    return int(e["dram_bytes_per_row"] * piece_rows) if "dram_bytes_per_row" in e else e.get("dram_bytes")
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle's port of Kernix's ordered matmul on host cores
+# ---------------------------------------------------------------------------
+def cpu_baseline(budget_s: float = 15.0, threads: int | None = None):
+    import oracle
+    threads = threads or oracle.THREADS
+    b = np.empty(K * N, dtype=np.float32)
+    from kernix_b200 import rng
+    rng.uniform(SEEDS["c5"][1], K * N, -1.0, 1.0, np.float32, out=b)
+    b = b.reshape(K, N)
+
+    def run(rows):
+        a = np.empty(rows * ROW_STRIDE, dtype=np.float32)
+        a_rows(list(range(rows)), a)
+        va = oracle.View(a, (rows, K), (ROW_STRIDE, 1))
+        t0 = time.perf_counter()
+        oracle.gemm_ordered_par(va, oracle.View.of(b), threads=threads)
+        return time.perf_counter() - t0
+
+    probe_rows = max(threads, 8)
+    t = run(probe_rows)
+    rows = int(min(M, max(probe_rows, probe_rows * budget_s / max(t, 1e-3))))
+    rows = max(threads, rows // threads * threads)
+    t = run(rows)
+    flops = 2.0 * rows * N * K
+    return {"value": round(flops / t / 1e12, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} of 8192 rows of the c5 GEMM (strided A, K=N=8192), {t:.1f} s; oracle port of "
+                      "Kernix's ordered matmul (linalg.rs:236-316) row-split like CpuExecutor::matmul_into"}
+
+
+def run_reference(args, rank, world):
+    """Reference arm: the oracle port of Kernix's CPU path timed on host cores."""
+    if rank != 0:
+        return None
+    import oracle
+    threads = oracle.THREADS
+    per_step = max(2.0, min(20.0, 150.0 / max(1, args.steps + args.warmup)))
+    b = np.empty(K * N, dtype=np.float32)
+    from kernix_b200 import rng
+    rng.uniform(SEEDS["c5"][1], K * N, -1.0, 1.0, np.float32, out=b)
+    b = b.reshape(K, N)
+    probe = max(threads, 8)
+    a = np.empty(M * ROW_STRIDE // 16, dtype=np.float32)
+
+    def run(rows):
+        buf = a[:rows * ROW_STRIDE]
+        a_rows(list(range(rows)), buf)
+        va = oracle.View(buf, (rows, K), (ROW_STRIDE, 1))
+        t0 = time.perf_counter()
+        oracle.gemm_ordered_par(va, oracle.View.of(b), threads=threads)
+        return time.perf_counter() - t0
+
+    t = run(probe)
+    rows = int(max(probe, min(M // 16, probe * per_step / max(t, 1e-3))))
+    rows = max(threads, rows // threads * threads)
+    for _ in range(args.warmup):
+        run(rows)
+    times = [run(rows) for _ in range(args.steps)]
+    tot = sum(times)
+    value = 2.0 * rows * N * K * args.steps / tot / 1e12
+    return {"metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(tot / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (SplitMix64 seeds 5, 6)",
+            "config": {"workload": "c5: " + CONFIG_TEXT["c5"], "M": M, "N": N, "K": K, "a_row_stride": ROW_STRIDE,
+                       "parallelism": "host threads"},
+            "impl": "reference",
+            "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                             "sample": f"{rows} of 8192 rows per step; oracle port of Kernix's ordered matmul "
+                                       "(linalg.rs:236-316), row-split over host threads"},
+            "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--piece", type=int, default=1024, help="rows per sharded piece")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
+    ap.add_argument("--size", type=int, default=8192,
+                    help="profiling aid: M=N=K=size with row stride size+512 (8192 is the workload)")
+    args = ap.parse_args()
+    global M, N, K, ROW_STRIDE
+    if args.size != 8192:
+        M = N = K = args.size
+        ROW_STRIDE = args.size + 512
+    rank, world, local = env_rank()
+    if world != args.gpus:
+        print(f"warning: WORLD_SIZE={world} but --gpus {args.gpus}", file=sys.stderr)
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    try:
+        res = run_ours(args, rank, world, local)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            dist.barrier(device_ids=[local])
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

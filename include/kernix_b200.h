@@ -138,6 +138,12 @@ int kx_destroy(kx_handle *h);
 /* Subsequent work on this handle is ordered on `stream` (a cudaStream_t). */
 int kx_set_stream(kx_handle *h, void *stream);
 int kx_set_f32_variant(kx_handle *h, int variant);
+/* Ordered mode (CpuExecutor::with_ordered_matmul, execution.rs:76-84): every
+ * output is accumulated in increasing k with separately rounded multiply and
+ * add, so device matmul results equal matmul_reference (linalg.rs:57-64,
+ * 236-316) bit for bit.  Slower: no FMA, no split-K. */
+int kx_set_ordered_matmul(kx_handle *h, int ordered);
+int kx_ordered_matmul(const kx_handle *h);
 /* Wait for outstanding work on the handle's stream (Device::synchronize). */
 int kx_synchronize(kx_handle *h, kx_error *err);
 

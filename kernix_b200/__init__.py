@@ -34,7 +34,8 @@ lib = _abi.lib
 MAX_RANK = _abi.MAX_RANK
 
 __all__ = [
-    "matmul", "matmul_shape", "matmul_into", "conv2d", "conv2d_shape", "Conv2dOptions", "softmax_temperature",
+    "matmul", "matmul_reference", "matmul_shape", "matmul_into", "conv2d", "conv2d_reference", "conv2d_shape",
+    "Conv2dOptions", "softmax_temperature",
     "MatrixInput", "try_dense_matmul", "try_strided_matmul", "TensorView", "CudaExecutor", "Handle",
     "handle", "OpsError", "InvalidRank", "ContractDimensionMismatch", "BroadcastIncompatible",
     "ElementCountOverflow", "DimensionOverflow", "LayoutError", "InvalidParameter", "ExactRank",
@@ -78,6 +79,15 @@ class Handle:
 
     def set_f32_variant(self, variant: int) -> None:
         raise_for(lib.kx_set_f32_variant(self._h, int(variant)), None)
+
+    def set_ordered_matmul(self, ordered: bool) -> None:
+        """Increasing-k, separately rounded accumulation (bitwise equal to
+        matmul_reference); see CpuExecutor::with_ordered_matmul."""
+        raise_for(lib.kx_set_ordered_matmul(self._h, int(bool(ordered))), None)
+
+    @property
+    def ordered_matmul(self) -> bool:
+        return bool(lib.kx_ordered_matmul(self._h))
 
     def synchronize(self) -> None:
         err = KxError()
@@ -231,6 +241,30 @@ def matmul_into(a, b, out) -> None:
     raise_for(fn(h.ptr, C.byref(da), C.byref(db), C.byref(do), C.byref(err)), err)
 
 
+class _Ordered:
+    """Run the enclosed device calls of ``h`` in ordered mode."""
+
+    def __init__(self, h: Handle):
+        self.h = h
+
+    def __enter__(self):
+        self.prev = self.h.ordered_matmul
+        self.h.set_ordered_matmul(True)
+        return self.h
+
+    def __exit__(self, *exc):
+        self.h.set_ordered_matmul(self.prev)
+        return False
+
+
+def matmul_reference(a, b):
+    """``matmul_reference`` on the device: every output accumulated in
+    increasing k with separately rounded multiply and add (linalg.rs:57-64),
+    so the bits equal Kernix's ordered CPU result."""
+    with _Ordered(_bind(a)):
+        return matmul(a, b)
+
+
 # ---------------------------------------------------------------------------
 # conv2d
 # ---------------------------------------------------------------------------
@@ -276,6 +310,13 @@ def conv2d(x, w, options: Conv2dOptions = Conv2dOptions()):
     dx, dw, do = _descriptor(x), _descriptor(w), _descriptor(out)
     raise_for(fn(h.ptr, C.byref(dx), C.byref(dw), C.byref(o), C.byref(do), C.byref(err)), err)
     return out
+
+
+def conv2d_reference(x, w, options: Conv2dOptions = Conv2dOptions()):
+    """``conv2d_reference`` on the device: the ordered scalar loop
+    (neural.rs:188-198, 341-357), bitwise equal to Kernix's CPU result."""
+    with _Ordered(_bind(x)):
+        return conv2d(x, w, options)
 
 
 # ---------------------------------------------------------------------------

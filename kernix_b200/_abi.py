@@ -98,6 +98,8 @@ _SIGNATURES = {
     "kx_destroy": (C.c_int, [_vp]),
     "kx_set_stream": (C.c_int, [_vp, _vp]),
     "kx_set_f32_variant": (C.c_int, [_vp, C.c_int]),
+    "kx_set_ordered_matmul": (C.c_int, [_vp, C.c_int]),
+    "kx_ordered_matmul": (C.c_int, [_vp]),
     "kx_synchronize": (C.c_int, [_vp, _P(KxError)]),
     "kx_alloc": (C.c_int, [_vp, _u64, _P(_vp), _P(KxError)]),
     "kx_free": (C.c_int, [_vp, _vp]),
@@ -129,7 +131,7 @@ def load_library(path: Path = LIB_PATH) -> C.CDLL:
     if not path.exists():
         raise ImportError(
             f"kernix_b200: native library {path} is missing; run "
-            "`python -m kernix_b200._build` (needs nvcc). There is no CPU fallback.")
+            "`python kernix_b200/_build.py` (needs nvcc). There is no CPU fallback.")
     lib = C.CDLL(str(path))
     for name, (res, args) in _SIGNATURES.items():
         fn = getattr(lib, name)

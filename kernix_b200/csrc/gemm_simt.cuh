@@ -16,6 +16,19 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+// Compile-time tuning knobs of the f32 SIMT tiles (defaults are the shipped
+// configuration): packed FP32 FMA, k depth of the 128x128 tile, and its
+// resident-CTA target per SM.
+#ifndef KX_FFMA2
+#define KX_FFMA2 1
+#endif
+#ifndef KX_F32_BK
+#define KX_F32_BK 8
+#endif
+#ifndef KX_F32_MINB
+#define KX_F32_MINB 2
+#endif
+
 namespace kx {
 
 constexpr int kMaxBatchDims = 6;
@@ -73,6 +86,15 @@ __device__ __forceinline__ void batch_offsets(const BatchGeom &g, int64_t b,
 // Tile loader for one operand.  `Rows` is the extent along m (A) or n (B) of the
 // tile, `BK` the k extent.  The operand element (r, p) (r along m/n, p along k)
 // lives at ptr[r*s_r + p*s_k].  Shared layout: sm[p][r] with row pitch Pitch.
+//
+// The thread -> element map is fixed for the whole k loop, so init() resolves
+// the thread's row (or column) once and load() only adds the k offset; this
+// keeps 64-bit address arithmetic out of the inner loop and the register
+// budget small enough for two resident CTAs per SM.
+//   kVecK     vector of W along k; threads walk rows fastest (transposing store)
+//   kVecMN    vector of W along m/n; straight store
+//   kGatherMN scalar; threads walk rows fastest
+//   kGatherK  scalar; threads walk k fastest
 // ---------------------------------------------------------------------------
 template <typename T, int Rows, int BK, int NT, int Mode, int Pitch>
 struct TileLoader {
@@ -82,95 +104,91 @@ struct TileLoader {
     static constexpr int kCount = kVector ? (Rows * BK) / (W * NT) : (Rows * BK) / NT;
     static_assert(kCount >= 1, "tile too small for thread count");
     static_assert(kVector ? (Rows * BK) % (W * NT) == 0 : (Rows * BK) % NT == 0, "tile/thread mismatch");
+    // Threads per "row" of the walk and the fixed stride between a thread's slots.
+    static constexpr int kLanesR = (Mode == kVecK || Mode == kGatherMN) ? Rows : (Mode == kVecMN ? Rows / W : BK);
+    static_assert(NT % kLanesR == 0, "thread count must tile the fast axis");
+    static constexpr int kStep = NT / kLanesR;
 
     T reg[kVector ? kCount * W : kCount];
+    const T *base;      // element (row of this thread, k = 0)
+    int64_t s_k;        // stride along k (gathers, kVecMN)
+    int64_t s_rstep;    // kGatherK: stride between this thread's rows
+    int fast, slow0;    // thread position on the fast / slow axis
+    int rlim;           // rows remaining from this thread's first row (validity)
 
-    // Load tile rows [r0, r0+Rows), k [k0, k0+BK) with zero fill outside
-    // [0,R) x [0,kend).
-    __device__ __forceinline__ void load(const T *__restrict__ ptr, int64_t s_r, int64_t s_k,
-                                         int r0, int R, int k0, int kend, int tid) {
-        if constexpr (Mode == kVecK) {
-            // vector index v: r = v % Rows, kv = v / Rows (threads walk r fastest)
-#pragma unroll
-            for (int i = 0; i < kCount; ++i) {
-                int v = tid + i * NT;
-                int r = v % Rows, kv = v / Rows;
-                int gr = r0 + r, gk = k0 + kv * W;
-                V val;
-                if (gr < R && gk < kend) {
-                    val = __ldg(reinterpret_cast<const V *>(ptr + (int64_t)gr * s_r + gk));
-                } else {
-                    val = zero_vec();
-                }
-                store_vec(&reg[i * W], val);
-            }
+    __device__ __forceinline__ void init(const T *__restrict__ ptr, int64_t s_r, int64_t sk, int r0, int R,
+                                         int tid) {
+        fast = tid % kLanesR;
+        slow0 = tid / kLanesR;
+        s_k = sk;
+        if constexpr (Mode == kVecK || Mode == kGatherMN) {
+            base = ptr + (int64_t)(r0 + fast) * s_r;
+            rlim = R - (r0 + fast);
         } else if constexpr (Mode == kVecMN) {
-            constexpr int RV = Rows / W;
-#pragma unroll
-            for (int i = 0; i < kCount; ++i) {
-                int v = tid + i * NT;
-                int rv = v % RV, kk = v / RV;
-                int gr = r0 + rv * W, gk = k0 + kk;
-                V val;
-                if (gr < R && gk < kend) {
-                    val = __ldg(reinterpret_cast<const V *>(ptr + (int64_t)gk * s_k + gr));
-                } else {
-                    val = zero_vec();
-                }
-                store_vec(&reg[i * W], val);
-            }
-        } else if constexpr (Mode == kGatherMN) {
-#pragma unroll
-            for (int i = 0; i < kCount; ++i) {
-                int v = tid + i * NT;
-                int r = v % Rows, kk = v / Rows;
-                int gr = r0 + r, gk = k0 + kk;
-                reg[i] = (gr < R && gk < kend) ? __ldg(ptr + (int64_t)gr * s_r + (int64_t)gk * s_k) : T(0);
-            }
+            base = ptr + (r0 + fast * W);
+            rlim = R - (r0 + fast * W);
         } else {
-#pragma unroll
-            for (int i = 0; i < kCount; ++i) {
-                int v = tid + i * NT;
-                int kk = v % BK, r = v / BK;
-                int gr = r0 + r, gk = k0 + kk;
-                reg[i] = (gr < R && gk < kend) ? __ldg(ptr + (int64_t)gr * s_r + (int64_t)gk * s_k) : T(0);
-            }
+            base = ptr + (int64_t)(r0 + slow0) * s_r;
+            s_rstep = (int64_t)kStep * s_r;
+            rlim = R - (r0 + slow0);
         }
     }
 
-    __device__ __forceinline__ void store(T *sm, int tid) const {
+    // Load k [k0, k0 + BK), zero filled outside the row range and [.., kend).
+    __device__ __forceinline__ void load(int k0, int kend) {
         if constexpr (Mode == kVecK) {
 #pragma unroll
             for (int i = 0; i < kCount; ++i) {
-                int v = tid + i * NT;
-                int r = v % Rows, kv = v / Rows;
-#pragma unroll
-                for (int j = 0; j < W; ++j) sm[(kv * W + j) * Pitch + r] = reg[i * W + j];
+                const int gk = k0 + (slow0 + i * kStep) * W;
+                V val = zero_vec();
+                if (rlim > 0 && gk < kend) val = __ldg(reinterpret_cast<const V *>(base + gk));
+                store_vec(&reg[i * W], val);
             }
         } else if constexpr (Mode == kVecMN) {
-            constexpr int RV = Rows / W;
 #pragma unroll
             for (int i = 0; i < kCount; ++i) {
-                int v = tid + i * NT;
-                int rv = v % RV, kk = v / RV;
-                V val;
-                load_vec(&reg[i * W], val);
-                *reinterpret_cast<V *>(&sm[kk * Pitch + rv * W]) = val;
+                const int gk = k0 + slow0 + i * kStep;
+                V val = zero_vec();
+                if (rlim > 0 && gk < kend) val = __ldg(reinterpret_cast<const V *>(base + (int64_t)gk * s_k));
+                store_vec(&reg[i * W], val);
             }
         } else if constexpr (Mode == kGatherMN) {
 #pragma unroll
             for (int i = 0; i < kCount; ++i) {
-                int v = tid + i * NT;
-                int r = v % Rows, kk = v / Rows;
-                sm[kk * Pitch + r] = reg[i];
+                const int gk = k0 + slow0 + i * kStep;
+                reg[i] = (rlim > 0 && gk < kend) ? __ldg(base + (int64_t)gk * s_k) : T(0);
             }
         } else {
+            const int gk = k0 + fast;
+            const bool kok = gk < kend;
+            const T *p = base + (int64_t)gk * s_k;
+#pragma unroll
+            for (int i = 0; i < kCount; ++i)
+                reg[i] = (kok && rlim > i * kStep) ? __ldg(p + i * s_rstep) : T(0);
+        }
+    }
+
+    __device__ __forceinline__ void store(T *sm) const {
+        if constexpr (Mode == kVecK) {
 #pragma unroll
             for (int i = 0; i < kCount; ++i) {
-                int v = tid + i * NT;
-                int kk = v % BK, r = v / BK;
-                sm[kk * Pitch + r] = reg[i];
+                const int kv = slow0 + i * kStep;
+#pragma unroll
+                for (int j = 0; j < W; ++j) sm[(kv * W + j) * Pitch + fast] = reg[i * W + j];
             }
+        } else if constexpr (Mode == kVecMN) {
+#pragma unroll
+            for (int i = 0; i < kCount; ++i) {
+                V val;
+                load_vec(&reg[i * W], val);
+                *reinterpret_cast<V *>(&sm[(slow0 + i * kStep) * Pitch + fast * W]) = val;
+            }
+        } else if constexpr (Mode == kGatherMN) {
+#pragma unroll
+            for (int i = 0; i < kCount; ++i) sm[(slow0 + i * kStep) * Pitch + fast] = reg[i];
+        } else {
+#pragma unroll
+            for (int i = 0; i < kCount; ++i) sm[fast * Pitch + slow0 + i * kStep] = reg[i];
         }
     }
 
@@ -199,14 +217,24 @@ struct TileLoader {
 // (TM/2)x(TN/2), the blocks BM/2 (resp. BN/2) apart.  A warp covers 4 rows x 8
 // columns of thread positions so each shared read is at most one wavefront.
 // ---------------------------------------------------------------------------
+template <typename T> struct Pair;
+template <> struct Pair<float> { using type = float2; };
+template <> struct Pair<double> { using type = double2; };
+
 template <typename T, int BM, int BN, int TM, int TN>
 struct MicroTile {
     static constexpr int HM = TM / 2, HN = TN / 2;
     static constexpr int TY = BM / TM, TX = BN / TN;   // thread grid
     static constexpr int NT = TY * TX;
     static_assert(TX % 8 == 0 && TY % 4 == 0, "warp shape 4x8 requires TX%8==0, TY%4==0");
-    T acc[TM][TN];
+    static_assert(TN % 2 == 0, "columns are held in pairs");
+    using P = typename Pair<T>::type;
+    // Accumulators in column pairs: acc(i, j) = accp[i][j/2].{x,y}.  Pairs sit in
+    // adjacent registers, the operand shape of the packed FP32 FMA.
+    P accp[TM][TN / 2];
     int ty, tx;
+
+    __device__ __forceinline__ T acc(int i, int j) const { return (j & 1) ? accp[i][j >> 1].y : accp[i][j >> 1].x; }
 
     __device__ __forceinline__ void init(int tid) {
         int warp = tid >> 5, lane = tid & 31;
@@ -217,42 +245,94 @@ struct MicroTile {
 #pragma unroll
         for (int i = 0; i < TM; ++i)
 #pragma unroll
-            for (int j = 0; j < TN; ++j) acc[i][j] = T(0);
+            for (int j = 0; j < TN / 2; ++j) {
+                accp[i][j].x = T(0);
+                accp[i][j].y = T(0);
+            }
     }
-    __device__ __forceinline__ int row(int i) const {  // tile-local row of acc[i][*]
+    __device__ __forceinline__ int row(int i) const {  // tile-local row of acc(i, *)
         return (i < HM) ? ty * HM + i : BM / 2 + ty * HM + (i - HM);
     }
     __device__ __forceinline__ int col(int j) const {
         return (j < HN) ? tx * HN + j : BN / 2 + tx * HN + (j - HN);
     }
 
-    template <int BK, int PA, int PB>
+    // ORD: separately rounded multiply and add (no FMA), which together with the
+    // increasing-k order reproduces the reference's ordered recurrence
+    // `acc += a * b` (linalg.rs:236-316) bit for bit.
+    template <int BK, int PA, int PB, bool ORD = false>
     __device__ __forceinline__ void mma(const T *__restrict__ sa, const T *__restrict__ sb) {
 #pragma unroll
         for (int k = 0; k < BK; ++k) {
-            T a[TM], b[TN];
+            T a[TM];
+            P b[TN / 2];
+            load_frag<HM>(sa + k * PA + ty * HM, a);
+            load_frag<HM>(sa + k * PA + BM / 2 + ty * HM, a + HM);
+            load_frag<HN>(sb + k * PB + tx * HN, reinterpret_cast<T *>(b));
+            load_frag<HN>(sb + k * PB + BN / 2 + tx * HN, reinterpret_cast<T *>(b) + HN);
 #pragma unroll
-            for (int i = 0; i < HM; ++i) {
-                a[i] = sa[k * PA + ty * HM + i];
-                a[HM + i] = sa[k * PA + BM / 2 + ty * HM + i];
+            for (int i = 0; i < TM; ++i) {
+#pragma unroll
+                for (int j = 0; j < TN / 2; ++j) {
+                    if constexpr (ORD) {
+                        accp[i][j].x = add_rn(accp[i][j].x, mul_rn(a[i], b[j].x));
+                        accp[i][j].y = add_rn(accp[i][j].y, mul_rn(a[i], b[j].y));
+                    } else {
+                        fma2(accp[i][j], a[i], b[j]);
+                    }
+                }
             }
-#pragma unroll
-            for (int j = 0; j < HN; ++j) {
-                b[j] = sb[k * PB + tx * HN + j];
-                b[HN + j] = sb[k * PB + BN / 2 + tx * HN + j];
-            }
-#pragma unroll
-            for (int i = 0; i < TM; ++i)
-#pragma unroll
-                for (int j = 0; j < TN; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
         }
     }
+
+  private:
+    // Blackwell's packed FP32 FMA: one issue slot for both lanes of a pair,
+    // which leaves issue bandwidth for the shared-memory fragment loads.
+    __device__ __forceinline__ static void fma2(float2 &c, float a, const float2 &b) {
+#if KX_FFMA2
+        c = __ffma2_rn(make_float2(a, a), b, c);
+#else
+        c.x = fmaf(a, b.x, c.x);
+        c.y = fmaf(a, b.y, c.y);
+#endif
+    }
+    __device__ __forceinline__ static void fma2(double2 &c, double a, const double2 &b) {
+        c.x = fma(a, b.x, c.x);
+        c.y = fma(a, b.y, c.y);
+    }
+    // H consecutive shared elements with the widest aligned vector loads.
+    template <int H>
+    __device__ __forceinline__ static void load_frag(const T *__restrict__ src, T *dst) {
+        constexpr int bytes = H * (int)sizeof(T);
+        if constexpr (bytes % 16 == 0) {
+#pragma unroll
+            for (int v = 0; v < bytes / 16; ++v) {
+                const uint4 q = *reinterpret_cast<const uint4 *>(reinterpret_cast<const char *>(src) + 16 * v);
+                *reinterpret_cast<uint4 *>(reinterpret_cast<char *>(dst) + 16 * v) = q;
+            }
+        } else if constexpr (bytes % 8 == 0) {
+#pragma unroll
+            for (int v = 0; v < bytes / 8; ++v) {
+                const uint2 q = *reinterpret_cast<const uint2 *>(reinterpret_cast<const char *>(src) + 8 * v);
+                *reinterpret_cast<uint2 *>(reinterpret_cast<char *>(dst) + 8 * v) = q;
+            }
+        } else {
+#pragma unroll
+            for (int v = 0; v < H; ++v) dst[v] = src[v];
+        }
+    }
+    __device__ __forceinline__ static float mul_rn(float x, float y) { return __fmul_rn(x, y); }
+    __device__ __forceinline__ static double mul_rn(double x, double y) { return __dmul_rn(x, y); }
+    __device__ __forceinline__ static float add_rn(float x, float y) { return __fadd_rn(x, y); }
+    __device__ __forceinline__ static double add_rn(double x, double y) { return __dadd_rn(x, y); }
 };
 
-// Tile configuration.
-template <typename T, int BM_, int BN_, int BK_, int TM_, int TN_>
+// Tile configuration.  MinBlocks is the resident-CTA target per SM that bounds
+// registers per thread (65536 / (NT * MinBlocks)).
+template <typename T, int BM_, int BN_, int BK_, int TM_, int TN_, int MinBlocks_ = 1>
 struct TileCfg {
     static constexpr int BM = BM_, BN = BN_, BK = BK_, TM = TM_, TN = TN_;
+    static constexpr int MinBlocks = MinBlocks_;
     static constexpr int NT = (BM / TM) * (BN / TN);
     // Pitch keeps 16-byte alignment of every shared row (float4 / double2 reads).
     static constexpr int PA = BM + 16 / (int)sizeof(T);
@@ -272,8 +352,8 @@ __device__ __forceinline__ void raster(int lin, int tiles_m, int tiles_n, int gr
     tn = in / gm;
 }
 
-template <typename T, typename Cfg, int AM, int BMODE>
-__global__ void __launch_bounds__(Cfg::NT)
+template <typename T, typename Cfg, int AM, int BMODE, bool ORD = false>
+__global__ void __launch_bounds__(Cfg::NT, Cfg::MinBlocks)
 gemm_simt_kernel(const __grid_constant__ GemmParams<T> p) {
     constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, NT = Cfg::NT;
     constexpr int PA = Cfg::PA, PB = Cfg::PB;
@@ -303,24 +383,26 @@ gemm_simt_kernel(const __grid_constant__ GemmParams<T> p) {
         mt.init(tid);
 
         const int ktiles = (kend - kbeg + BK - 1) / BK;
+        la.init(A, p.a_rs, p.a_cs, m0, p.M, tid);
+        lb.init(B, p.b_cs, p.b_rs, n0, p.N, tid);
         if (ktiles > 0) {
-            la.load(A, p.a_rs, p.a_cs, m0, p.M, kbeg, kend, tid);
-            lb.load(B, p.b_cs, p.b_rs, n0, p.N, kbeg, kend, tid);
-            la.store(sa[0], tid);
-            lb.store(sb[0], tid);
+            la.load(kbeg, kend);
+            lb.load(kbeg, kend);
+            la.store(sa[0]);
+            lb.store(sb[0]);
         }
         __syncthreads();
         for (int kt = 0; kt < ktiles; ++kt) {
             const int cur = kt & 1;
             if (kt + 1 < ktiles) {
                 const int k0 = kbeg + (kt + 1) * BK;
-                la.load(A, p.a_rs, p.a_cs, m0, p.M, k0, kend, tid);
-                lb.load(B, p.b_cs, p.b_rs, n0, p.N, k0, kend, tid);
+                la.load(k0, kend);
+                lb.load(k0, kend);
             }
-            mt.template mma<BK, PA, PB>(sa[cur], sb[cur]);
+            mt.template mma<BK, PA, PB, ORD>(sa[cur], sb[cur]);
             if (kt + 1 < ktiles) {
-                la.store(sa[cur ^ 1], tid);
-                lb.store(sb[cur ^ 1], tid);
+                la.store(sa[cur ^ 1]);
+                lb.store(sb[cur ^ 1]);
             }
             __syncthreads();
         }
@@ -357,13 +439,13 @@ gemm_simt_kernel(const __grid_constant__ GemmParams<T> p) {
                         typename Vec<T>::type val;
                         T *pv = reinterpret_cast<T *>(&val);
 #pragma unroll
-                        for (int w = 0; w < W; ++w) pv[w] = mt.acc[i][h * HN + v + w];
+                        for (int w = 0; w < W; ++w) pv[w] = mt.acc(i, h * HN + v + w);
                         *reinterpret_cast<typename Vec<T>::type *>(crow + gc + v) = val;
                     }
                 } else {
 #pragma unroll
                     for (int j = 0; j < HN; ++j) {
-                        if (gc + j < p.N) crow[(int64_t)(gc + j) * ccs] = mt.acc[i][h * HN + j];
+                        if (gc + j < p.N) crow[(int64_t)(gc + j) * ccs] = mt.acc(i, h * HN + j);
                     }
                 }
             }

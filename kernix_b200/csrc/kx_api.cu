@@ -318,6 +318,14 @@ int kx_set_f32_variant(kx_handle *hh, int variant) {
     return KX_OK;
 }
 
+int kx_set_ordered_matmul(kx_handle *hh, int ordered) {
+    if (!hh) return KX_E_PARAM;
+    hh->impl.ordered = ordered != 0;
+    return KX_OK;
+}
+
+int kx_ordered_matmul(const kx_handle *hh) { return hh && hh->impl.ordered ? 1 : 0; }
+
 int kx_synchronize(kx_handle *hh, kx_error *err) {
     if (!hh) return set_err(err, KX_E_PARAM, "synchronize", "null handle");
     DeviceGuard g(hh->impl.device);

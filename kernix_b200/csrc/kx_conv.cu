@@ -54,7 +54,7 @@ __device__ __forceinline__ KEntry make_entry(const ConvGeom &g, int64_t kk) {
 }
 
 template <typename T, typename Cfg, bool kTable>
-__global__ void __launch_bounds__(Cfg::NT) conv_igemm_kernel(const T *__restrict__ x, const T *__restrict__ wt,
+__global__ void __launch_bounds__(Cfg::NT, Cfg::MinBlocks) conv_igemm_kernel(const T *__restrict__ x, const T *__restrict__ wt,
                                                               T *__restrict__ y, const __grid_constant__ ConvGeom g) {
     constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, NT = Cfg::NT;
     constexpr int PA = Cfg::PA, PB = Cfg::PB;
@@ -84,14 +84,17 @@ __global__ void __launch_bounds__(Cfg::NT) conv_igemm_kernel(const T *__restrict
     const int krow0 = tid / BN;
     const int64_t gcol = n0 + col;
     const bool col_ok = gcol < g.ncols;
-    int64_t iy0 = 0, ix0 = 0, xbase = 0;
+    // Input coordinates fit int32 (the host bounds padding, stride and extents).
+    int iy0 = 0, ix0 = 0;
+    int64_t xbase = 0;
+    const int ih = (int)g.h, iw = (int)g.w;
     if (col_ok) {
         const int64_t hw = g.oh * g.ow;
         const int64_t img = gcol / hw, p = gcol % hw;
         const int64_t oy = p / g.ow, ox = p % g.ow;
-        iy0 = oy * g.sy - g.py;
-        ix0 = ox * g.sx - g.px;
-        xbase = img * g.xs[0] + grp * g.cg * g.xs[1] + iy0 * g.xs[2] + ix0 * g.xs[3];
+        iy0 = (int)(oy * g.sy - g.py);
+        ix0 = (int)(ox * g.sx - g.px);
+        xbase = img * g.xs[0] + grp * g.cg * g.xs[1] + (int64_t)iy0 * g.xs[2] + (int64_t)ix0 * g.xs[3];
     }
     // Weight rows: thread walks k fastest.
     const int a_k = tid % BK;
@@ -108,8 +111,8 @@ __global__ void __launch_bounds__(Cfg::NT) conv_igemm_kernel(const T *__restrict
                 KEntry e;
                 if constexpr (kTable) e = table[kk];
                 else e = make_entry(g, kk);
-                const int64_t iy = iy0 + e.ry, ix = ix0 + e.rx;
-                if (iy >= 0 && iy < g.h && ix >= 0 && ix < g.w) v = __ldg(x + xbase + e.x_off);
+                const int iy = iy0 + e.ry, ix = ix0 + e.rx;
+                if (iy >= 0 && iy < ih && ix >= 0 && ix < iw) v = __ldg(x + xbase + e.x_off);
             }
             rb[i] = v;
         }
@@ -167,7 +170,7 @@ __global__ void __launch_bounds__(Cfg::NT) conv_igemm_kernel(const T *__restrict
                     float4 v;
                     float *pv = reinterpret_cast<float *>(&v);
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) pv[j] = (float)mt.acc[i][h2 * HN + j];
+                    for (int j = 0; j < 4; ++j) pv[j] = (float)mt.acc(i, h2 * HN + j);
                     *reinterpret_cast<float4 *>(y + (img * g.co + grp * g.cog + co) * hw + p) = v;
                 }
             }
@@ -181,7 +184,7 @@ __global__ void __launch_bounds__(Cfg::NT) conv_igemm_kernel(const T *__restrict
 #pragma unroll
             for (int i = 0; i < Cfg::TM; ++i) {
                 const int64_t co = m0 + mt.row(i);
-                if (co < g.cog) y[(img * g.co + grp * g.cog + co) * hw + p] = mt.acc[i][h2 * HN + j];
+                if (co < g.cog) y[(img * g.co + grp * g.cog + co) * hw + p] = mt.acc(i, h2 * HN + j);
             }
         }
     }
@@ -204,11 +207,13 @@ __global__ void conv_weight_scan(const T *__restrict__ wt, const __grid_constant
 }
 
 // Ordered scalar convolution (neural.rs:341-357 order: ci, ky, kx increasing,
-// padded taps skipped, separate multiply and add).  Runs only when *flag is set.
+// padded taps skipped, separate multiply and add).  With a flag it runs only
+// when *flag is set (nonfinite-weight fixup); without one it always runs (the
+// conv2d_reference mode of an ordered handle).
 template <typename T>
 __global__ void conv_direct_fixup(const T *__restrict__ x, const T *__restrict__ wt, T *__restrict__ y,
                                   const __grid_constant__ ConvGeom g, const uint32_t *flag) {
-    if (*flag == 0) return;
+    if (flag && *flag == 0) return;
     const int64_t total = g.n * g.co * g.oh * g.ow;
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
          e += (int64_t)gridDim.x * blockDim.x) {
@@ -238,11 +243,11 @@ __global__ void conv_direct_fixup(const T *__restrict__ x, const T *__restrict__
 }
 
 template <typename T> struct ConvCfg;
-template <> struct ConvCfg<float> : TileCfg<float, 128, 128, 16, 8, 8> {};
+template <> struct ConvCfg<float> : TileCfg<float, 128, 128, 8, 8, 8, 2> {};
 template <> struct ConvCfg<double> : TileCfg<double, 128, 128, 8, 8, 8> {};
 template <typename T> struct ConvSmallCfg;
-template <> struct ConvSmallCfg<float> : TileCfg<float, 64, 64, 16, 4, 4> {};
-template <> struct ConvSmallCfg<double> : TileCfg<double, 64, 64, 16, 4, 4> {};
+template <> struct ConvSmallCfg<float> : TileCfg<float, 64, 64, 16, 4, 4, 2> {};
+template <> struct ConvSmallCfg<double> : TileCfg<double, 64, 64, 16, 4, 4, 2> {};
 
 template <typename T, typename Cfg>
 cudaError_t launch_igemm(Handle *h, const T *x, const T *w, T *y, const ConvGeom &g) {
@@ -316,8 +321,9 @@ int conv_impl(kx_handle *hh, const kx_tensor *in, const kx_tensor *wt, const kx_
     g.ncols = g.n * g.oh * g.ow;
     // Geometry that reaches int32 limits in the tile loops is outside this
     // kernel's envelope (the validated span keeps every address in range).
-    if (g.kh * g.dy > INT32_MAX || g.kw * g.dx > INT32_MAX || g.groups > 65535 || g.py > INT32_MAX / 2 ||
-        g.px > INT32_MAX / 2 || g.sy > INT32_MAX || g.sx > INT32_MAX)
+    if (g.kh * g.dy > INT32_MAX / 4 || g.kw * g.dx > INT32_MAX / 4 || g.groups > 65535 || g.py > INT32_MAX / 4 ||
+        g.px > INT32_MAX / 4 || g.h > INT32_MAX / 4 || g.w > INT32_MAX / 4 || g.oh * g.sy > INT32_MAX / 4 ||
+        g.ow * g.sx > INT32_MAX / 4)
         return set_err(err, KX_E_UNSUPPORTED, kOp, "geometry outside kernel limits");
 
     int dev_prev = -1;
@@ -327,6 +333,20 @@ int conv_impl(kx_handle *hh, const kx_tensor *in, const kx_tensor *wt, const kx_
     const T *wp = static_cast<const T *>(wt->data) + wt->origin;
     T *yp = static_cast<T *>(out->data) + out->origin;
     cudaError_t ce = cudaSuccess;
+    if (h->ordered) {
+        int64_t blocks = ((int64_t)total + 255) / 256;
+        if (blocks > 16LL * h->sm_count) blocks = 16LL * h->sm_count;
+        conv_direct_fixup<T><<<(unsigned)blocks, 256, 0, h->stream>>>(xp, wp, yp, g, nullptr);
+        ce = cudaGetLastError();
+        ++h->launches;
+        h->last_kernel = "conv_direct_ordered";
+        if (dev_prev >= 0 && dev_prev != h->device) cudaSetDevice(dev_prev);
+        if (ce != cudaSuccess) {
+            h->cuda_fail(ce);
+            return cuda_err(err, h, kOp);
+        }
+        return KX_OK;
+    }
     const bool padded = g.py != 0 || g.px != 0;
     if (padded) {
         ce = cudaMemsetAsync(h->flags, 0, sizeof(uint32_t), h->stream);

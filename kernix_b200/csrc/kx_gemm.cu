@@ -8,39 +8,39 @@ namespace {
 
 // 128x128 tiles, 8x8 outputs per thread, 256 threads (two CTAs per SM for f32).
 template <typename T> struct BigCfg;
-template <> struct BigCfg<float> : TileCfg<float, 128, 128, 16, 8, 8> {};
-template <> struct BigCfg<double> : TileCfg<double, 128, 128, 8, 8, 8> {};
+template <> struct BigCfg<float> : TileCfg<float, 128, 128, KX_F32_BK, 8, 8, KX_F32_MINB> {};
+template <> struct BigCfg<double> : TileCfg<double, 128, 128, 8, 8, 8, 1> {};
 // 64x64 tiles, 4x4 per thread: more CTAs for small or split-K problems.
 template <typename T> struct SmallCfg;
-template <> struct SmallCfg<float> : TileCfg<float, 64, 64, 16, 4, 4> {};
-template <> struct SmallCfg<double> : TileCfg<double, 64, 64, 16, 4, 4> {};
+template <> struct SmallCfg<float> : TileCfg<float, 64, 64, 16, 4, 4, 2> {};
+template <> struct SmallCfg<double> : TileCfg<double, 64, 64, 16, 4, 4, 2> {};
 
-template <typename T, typename Cfg, int AM, int BMD>
+template <typename T, typename Cfg, int AM, int BMD, bool ORD>
 cudaError_t launch_one(const GemmParams<T> &p, cudaStream_t s) {
     const int64_t tiles = (int64_t)((p.M + Cfg::BM - 1) / Cfg::BM) * ((p.N + Cfg::BN - 1) / Cfg::BN);
     const int64_t z = p.nbatch * p.splits;
     dim3 grid((unsigned)tiles, (unsigned)(z < 65535 ? z : 65535), 1);
-    gemm_simt_kernel<T, Cfg, AM, BMD><<<grid, Cfg::NT, 0, s>>>(p);
+    gemm_simt_kernel<T, Cfg, AM, BMD, ORD><<<grid, Cfg::NT, 0, s>>>(p);
     return cudaGetLastError();
 }
 
-template <typename T, typename Cfg, int AM>
+template <typename T, typename Cfg, int AM, bool ORD>
 cudaError_t launch_b(const GemmParams<T> &p, int bmode, cudaStream_t s) {
     switch (bmode) {
-        case kVecK: return launch_one<T, Cfg, AM, kVecK>(p, s);
-        case kVecMN: return launch_one<T, Cfg, AM, kVecMN>(p, s);
-        case kGatherMN: return launch_one<T, Cfg, AM, kGatherMN>(p, s);
-        default: return launch_one<T, Cfg, AM, kGatherK>(p, s);
+        case kVecK: return launch_one<T, Cfg, AM, kVecK, ORD>(p, s);
+        case kVecMN: return launch_one<T, Cfg, AM, kVecMN, ORD>(p, s);
+        case kGatherMN: return launch_one<T, Cfg, AM, kGatherMN, ORD>(p, s);
+        default: return launch_one<T, Cfg, AM, kGatherK, ORD>(p, s);
     }
 }
 
-template <typename T, typename Cfg>
+template <typename T, typename Cfg, bool ORD = false>
 cudaError_t launch_cfg(const GemmParams<T> &p, int amode, int bmode, cudaStream_t s) {
     switch (amode) {
-        case kVecK: return launch_b<T, Cfg, kVecK>(p, bmode, s);
-        case kVecMN: return launch_b<T, Cfg, kVecMN>(p, bmode, s);
-        case kGatherMN: return launch_b<T, Cfg, kGatherMN>(p, bmode, s);
-        default: return launch_b<T, Cfg, kGatherK>(p, bmode, s);
+        case kVecK: return launch_b<T, Cfg, kVecK, ORD>(p, bmode, s);
+        case kVecMN: return launch_b<T, Cfg, kVecMN, ORD>(p, bmode, s);
+        case kGatherMN: return launch_b<T, Cfg, kGatherMN, ORD>(p, bmode, s);
+        default: return launch_b<T, Cfg, kGatherK, ORD>(p, bmode, s);
     }
 }
 
@@ -82,7 +82,13 @@ int run_gemm(Handle *h, GemmParams<T> p, const char **kernel_name) {
     p.k_per_split = p.K;
     p.ws = nullptr;
     cudaError_t ce;
-    if (big_tiles * p.nbatch >= target) {
+    if (h->ordered) {
+        // Ordered mode: one pass over k per output, separately rounded
+        // multiply and add -- bitwise equal to the reference's ordered path.
+        *kernel_name = "simt_64x64_ordered";
+        ce = launch_cfg<T, Small, true>(p, amode, bmode, h->stream);
+        ++h->launches;
+    } else if (big_tiles * p.nbatch >= target) {
         *kernel_name = "simt_128x128";
         ce = launch_cfg<T, Big>(p, amode, bmode, h->stream);
         ++h->launches;

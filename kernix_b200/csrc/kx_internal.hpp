@@ -17,6 +17,7 @@ struct Handle {
     int sm_count = 148;
     cudaStream_t stream = nullptr;
     int f32_variant = KX_F32_AUTO;
+    bool ordered = false;        // CpuExecutor::with_ordered_matmul equivalent
     uint64_t launches = 0;
     const char *last_kernel = "none";
     int last_cuda_error = 0;

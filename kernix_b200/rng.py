@@ -34,14 +34,16 @@ def fractions(seed: int, start: int, count: int) -> np.ndarray:
     return (splitmix_block(seed, start, count) >> np.uint64(11)).astype(np.float64) * (1.0 / 9007199254740992.0)
 
 
-def uniform(seed: int, n: int, low: float, high: float, dtype=np.float32, out: np.ndarray | None = None) -> np.ndarray:
-    """``SeededRng::new(seed).uniform([n], low, high)`` as a flat array."""
+def uniform(seed: int, n: int, low: float, high: float, dtype=np.float32, out: np.ndarray | None = None,
+            start: int = 0) -> np.ndarray:
+    """``SeededRng::new(seed).uniform([start + n], low, high)[start:]`` as a
+    flat array (the stream is counter-based, so any window is direct)."""
     if out is None:
         out = np.empty(n, dtype=dtype)
     width = float(high) - float(low)
     for s in range(0, n, _CHUNK):
         c = min(_CHUNK, n - s)
-        out[s:s + c] = float(low) + width * fractions(seed, s, c)
+        out[s:s + c] = float(low) + width * fractions(seed, start + s, c)
     return out
 
 

@@ -1,0 +1,99 @@
+// Exercises the C++ host mirror (include/kernix_b200.hpp) the way Kernix's own
+// tests exercise the Rust API.  `--host` needs no GPU; `--gpu` runs on device 0.
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <vector>
+
+#include "kernix_b200.hpp"
+
+static int failures = 0;
+#define EXPECT(c)                                                        \
+    do {                                                                 \
+        if (!(c)) {                                                      \
+            std::fprintf(stderr, "FAIL %s:%d: %s\n", __FILE__, __LINE__, #c); \
+            ++failures;                                                  \
+        }                                                                \
+    } while (0)
+
+static void host_checks() {
+    // native_kernel_tests.rs:17-28: invalid span rejected, isize::MIN singleton accepted
+    double one = 1.0;
+    bool threw = false;
+    try {
+        kernix::MatrixInput<double>::create(&one, 1, {2, 2}, {2, 1}, 0);
+    } catch (const kernix::OpsError &e) {
+        threw = e.status() == KX_E_LAYOUT;
+    }
+    EXPECT(threw);
+    auto m = kernix::MatrixInput<double>::create(&one, 1, {1, 1}, {INT64_MIN, INT64_MIN}, 0);
+    EXPECT(m.strides()[0] == 0 && m.strides()[1] == 0);
+    // ops_tests.rs:304-320: contraction mismatch carries (left, right)
+    uint64_t a[2] = {2, 3}, b[2] = {4, 2}, od[KX_MAX_RANK];
+    uint32_t r = 0;
+    kx_error e{};
+    EXPECT(kx_matmul_shape(a, 2, b, 2, &r, od, &e) == KX_E_CONTRACT && e.values[0] == 3 && e.values[1] == 4);
+    // small_matmul_tests.rs:137-151: malformed extents decline without writes
+    std::vector<float> out(64, 7.0f), x(16, 1.0f), y(63, 2.0f);
+    EXPECT(kx_try_dense_matmul_f32(nullptr, x.data(), 16, y.data(), 63, out.data(), 64, 4, 4, 16) == KX_DECLINED);
+    for (float v : out) EXPECT(v == 7.0f);
+}
+
+static void gpu_checks() {
+    kernix::CudaExecutor cuda(0);
+    // ops_tests.rs:286-293: transpose view times F-order view
+    auto x = cuda.upload<double>({1, 2, 3, 4}, {2, 2});
+    auto yf = cuda.upload<double>({5, 7, 6, 8}, {2, 2}).transpose();   // F-order [[5,6],[7,8]]
+    auto z = cuda.matmul(x.transpose(), yf);
+    auto zv = cuda.download(z);
+    EXPECT(zv.size() == 4 && zv[0] == 26 && zv[1] == 30 && zv[2] == 38 && zv[3] == 44);
+    // batched_matmul_tests.rs:49-65: swapped then reversed batch view, ordered == exact
+    std::vector<double> base(24);
+    for (int i = 0; i < 24; ++i) base[i] = i / 16.0;
+    auto t = cuda.upload<double>(base, {2, 3, 4}).swap_axes(1, 2).reverse_axis(2);
+    auto bm = cuda.upload<double>(std::vector<double>(6, 0.75), {3, 2});
+    auto p = cuda.matmul(t, bm);
+    auto pv = cuda.download(p);
+    EXPECT(pv.size() == 16);
+    for (int bi = 0; bi < 2; ++bi)
+        for (int i = 0; i < 4; ++i) {
+            double s = 0;
+            for (int k = 0; k < 3; ++k) s += base[bi * 12 + (2 - k) * 4 + i] * 0.75;   // dyadic: exact
+            EXPECT(pv[(bi * 4 + i) * 2] == s && pv[(bi * 4 + i) * 2 + 1] == s);
+        }
+    // MatmulElement hooks on host buffers (small_matmul_tests.rs dyadic data, exact)
+    kernix::Handle h(0);
+    const size_t m = 17, k = 33, n = 9;
+    std::vector<float> av(m * k), bv(k * n), ov(m * n + 2, NAN);
+    for (size_t i = 0; i < av.size(); ++i) av[i] = ((i * 7 % 29) - 14.0f) / 8.0f;
+    for (size_t i = 0; i < bv.size(); ++i) bv[i] = ((i * 11 % 37) - 18.0f) / 16.0f;
+    EXPECT(kernix::MatmulElement<float>::try_dense_matmul(h, av.data(), av.size(), bv.data(), bv.size(),
+                                                          ov.data() + 1, m * n, m, k, n));
+    for (size_t i = 0; i < m; ++i)
+        for (size_t j = 0; j < n; ++j) {
+            double s = 0;
+            for (size_t q = 0; q < k; ++q) s += (double)av[i * k + q] * bv[q * n + j];
+            EXPECT((double)ov[1 + i * n + j] == s);
+        }
+    EXPECT(std::isnan(ov[0]) && std::isnan(ov[m * n + 1]));
+    auto ma = kernix::MatrixInput<float>::create(av.data(), av.size(), {m, k}, {(std::ptrdiff_t)k, 1}, 0);
+    auto mb = kernix::MatrixInput<float>::create(bv.data(), bv.size(), {k, n}, {(std::ptrdiff_t)n, 1}, 0);
+    std::vector<float> o2(m * n);
+    EXPECT(kernix::MatmulElement<float>::try_strided_matmul(h, ma, mb, o2.data(), o2.size()));
+    for (size_t i = 0; i < m * n; ++i) EXPECT(o2[i] == ov[1 + i]);
+    // ordered mode is available and reported
+    cuda.with_ordered_matmul(true);
+    EXPECT(cuda.ordered_matmul());
+}
+
+int main(int argc, char **argv) {
+    bool gpu = argc > 1 && std::string(argv[1]) == "--gpu";
+    host_checks();
+    if (gpu) gpu_checks();
+    if (failures) {
+        std::fprintf(stderr, "%d failure(s)\n", failures);
+        return 1;
+    }
+    std::printf("mirror_test ok (%s)\n", gpu ? "host+gpu" : "host");
+    return 0;
+}

@@ -54,6 +54,18 @@ def test_conv_matches_reference_across_geometry(kx, torch_cuda, options, dtype):
     assert (np.abs(got_r - ref_r) < tol * (1 + np.abs(ref_r))).all()
 
 
+@pytest.mark.parametrize("options", G.CONV_OPTIONS, ids=["default", "grouped_dilated_padded"])
+@pytest.mark.parametrize("dtype", [np.float64, np.float32])
+def test_conv_reference_mode_is_bitwise(kx, torch_cuda, options, dtype):
+    """conv2d_reference on the device reproduces the ordered scalar path exactly
+    (native_kernel_tests.rs:237-239 asserts this equality for reversed inputs)."""
+    x, w = G.conv_inputs(4, options["groups"], dtype)
+    opts = kx.Conv2dOptions(**options)
+    ref = oracle.conv2d_reference(oracle.View.of(x), oracle.View.of(w), **options)
+    got = kx.conv2d_reference(to_dev(x, torch_cuda), to_dev(w, torch_cuda), opts).cpu().numpy()
+    assert np.array_equal(got, ref)
+
+
 def test_conv_errors_and_empty(kx, torch_cuda):
     x = torch_cuda.zeros(1, 2, 2, 3, device="cuda")
     w = torch_cuda.zeros(2, 2, 3, 3, device="cuda")

@@ -85,8 +85,38 @@ def test_strided_batches_swapped_and_reversed(kx, torch_cuda):
     va = oracle.View(base, (2, 4, 3), (12, 1, -4), 8)
     b = np.full((3, 2), 0.7)
     exp = oracle.matmul_reference(va, oracle.View.of(b))
-    got = kx.matmul(view(kx, torch_cuda, base, (2, 4, 3), (12, 1, -4), 8), to_dev(b, torch_cuda)).cpu().numpy()
+    dv = view(kx, torch_cuda, base, (2, 4, 3), (12, 1, -4), 8)
+    # The reference's matmul sends this view to its ordered fallback, so it
+    # equals matmul_reference exactly; the device's ordered mode does the same.
+    assert np.array_equal(kx.matmul_reference(dv, to_dev(b, torch_cuda)).cpu().numpy(), exp)
+    got = kx.matmul(dv, to_dev(b, torch_cuda)).cpu().numpy()
+    assert (np.abs(got - exp) < 2e-13 * (1 + np.abs(exp))).all()
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_ordered_mode_is_bitwise_matmul_reference(kx, torch_cuda, dtype):
+    """execution_tests.rs:23-32 / native_kernel_tests.rs:51-69: the ordered
+    path equals matmul_reference bit for bit, for any layout and batch."""
+    rng = np.random.default_rng(3)
+    cases = [
+        ((7, 11), (11, 5)), ((65, 67), (67, 69)), ((17, 31), (31, 19)), ((3, 1, 9, 40), (5, 40, 12)),
+        ((40,), (40, 9)), ((9, 40), (40,)), ((40,), (40,)), ((129, 300), (300, 131)),
+    ]
+    for a_dims, b_dims in cases:
+        a = rng.uniform(-1, 1, a_dims).astype(dtype)
+        b = rng.uniform(-1, 1, b_dims).astype(dtype)
+        exp = oracle.matmul_reference(oracle.View.of(a), oracle.View.of(b))
+        got = kx.matmul_reference(to_dev(a, torch_cuda), to_dev(b, torch_cuda)).cpu().numpy()
+        assert np.array_equal(got, exp), (a_dims, b_dims)
+    # transpose (a.T) times reversed rows, through views
+    a = rng.uniform(-1, 1, (33, 21)).astype(dtype)
+    b = rng.uniform(-1, 1, (33, 14)).astype(dtype)
+    va, vb = oracle.View(a, (21, 33), (1, 21), 0), oracle.View(b, (33, 14), (-14, 1), 32 * 14)
+    exp = oracle.matmul_reference(va, vb)
+    got = kx.matmul_reference(view(kx, torch_cuda, a, (21, 33), (1, 21)),
+                              view(kx, torch_cuda, b, (33, 14), (-14, 1), 32 * 14)).cpu().numpy()
     assert np.array_equal(got, exp)
+    assert not kx.handle(0).ordered_matmul
 
 
 @pytest.mark.parametrize("dtype", [np.float32, np.float64])
