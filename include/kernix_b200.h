@@ -208,6 +208,23 @@ int kx_try_strided_matmul_f64(kx_handle *h, const kx_matrix *a, const kx_matrix 
 /* MatrixInput::new validation alone (host only). */
 int kx_matrix_validate(const kx_matrix *m, uint32_t elem_bytes, kx_error *err);
 
+/* ---- allocation-free variant -------------------------------------------- */
+/* No counterpart in the reference.  Split-K f32 GEMM out = a x b for callers
+ * that may not call cudaMalloc while they run (a process whose device memory is
+ * owned up front by its own pool, or a latency-critical loop where cudaMalloc /
+ * cudaFree would synchronise the device).  It takes no handle and allocates
+ * nothing: the split-K partial sums live in a file-scope 16 MiB static device
+ * array that every GPU loading this library keeps until exit.
+ *   - rank-two a [m,k] and b [k,n], any signed strides, device memory of the
+ *     calling thread's current device; out C-contiguous [m,n], not overlapping;
+ *   - rejects m*n > 2,097,152 (two splits must fit) with KX_E_UNSUPPORTED;
+ *   - the first call on a device resolves the array's address on that device
+ *     (and loads the module there): make it before any stream capture;
+ *   - all calls share the array: calls whose kernels overlap on the GPU race,
+ *     so order them on one stream.  Nothing in it needs to start at zero. */
+int kx_matmul_splitk_f32_static(const kx_tensor *a, const kx_tensor *b, const kx_tensor *out, void *stream,
+                                kx_error *err);
+
 /* ---- introspection ------------------------------------------------------ */
 /* Number of kernel launches this handle has issued since creation. */
 uint64_t kx_launch_count(const kx_handle *h);

@@ -121,6 +121,7 @@ _SIGNATURES = {
     "kx_try_strided_matmul_f32": (C.c_int, [_vp, _P(KxMatrix), _P(KxMatrix), _vp, _u64]),
     "kx_try_strided_matmul_f64": (C.c_int, [_vp, _P(KxMatrix), _P(KxMatrix), _vp, _u64]),
     "kx_matrix_validate": (C.c_int, [_P(KxMatrix), C.c_uint32, _P(KxError)]),
+    "kx_matmul_splitk_f32_static": (C.c_int, [_P(KxTensor), _P(KxTensor), _P(KxTensor), _vp, _P(KxError)]),
     "kx_launch_count": (C.c_uint64, [_vp]),
     "kx_last_kernel": (C.c_char_p, [_vp]),
     "kx_status_name": (C.c_char_p, [C.c_int]),
