@@ -87,7 +87,30 @@ int build_params(const MatmulPlan &pl, const kx_tensor *a, const T *a_ptr, const
         nbatch *= (int64_t)dim;
         ++nd;
     }
-    p->batch.ndims = nd;
+    // Merge adjacent batch axes that every operand walks as one (stride of the
+    // outer axis = stride x extent of the inner one): [16, 32] heads become a
+    // single axis of 512 with the same element offsets.
+    int w = 0;
+    for (int d = 0; d < nd; ++d) {
+        if (w > 0) {
+            BatchGeom &g = p->batch;
+            const int64_t e = g.dims[d];
+            if (g.a_str[w - 1] == g.a_str[d] * e && g.b_str[w - 1] == g.b_str[d] * e &&
+                g.c_str[w - 1] == g.c_str[d] * e) {
+                g.dims[w - 1] *= e;
+                g.a_str[w - 1] = g.a_str[d];
+                g.b_str[w - 1] = g.b_str[d];
+                g.c_str[w - 1] = g.c_str[d];
+                continue;
+            }
+        }
+        p->batch.dims[w] = p->batch.dims[d];
+        p->batch.a_str[w] = p->batch.a_str[d];
+        p->batch.b_str[w] = p->batch.b_str[d];
+        p->batch.c_str[w] = p->batch.c_str[d];
+        ++w;
+    }
+    p->batch.ndims = w;
     p->nbatch = nbatch;
     p->splits = 1;
     p->k_per_split = p->K;
@@ -283,6 +306,7 @@ int kx_create(int device, kx_handle **out, kx_error *err) {
     hh->impl.sm_count = prop.multiProcessorCount;
     DeviceGuard g(device);
     cudaError_t ce = cudaMalloc(&hh->impl.flags, Handle::kFlagWords * sizeof(uint32_t));
+    if (ce == cudaSuccess) ce = cudaMemset(hh->impl.flags, 0, Handle::kFlagWords * sizeof(uint32_t));
     if (ce != cudaSuccess) {
         delete hh;
         return set_err(err, KX_E_CUDA, "kx_create", cudaGetErrorString(ce));
@@ -333,6 +357,18 @@ int kx_synchronize(kx_handle *hh, kx_error *err) {
     if (ce != cudaSuccess) {
         hh->impl.cuda_fail(ce);
         return cuda_err(err, &hh->impl, "synchronize");
+    }
+    // Device status word: a kernel whose bounded wait expired leaves a flag
+    // here instead of hanging; report it once and clear it.
+    uint32_t status = 0;
+    ce = cudaMemcpy(&status, hh->impl.flags + kStatusWord, sizeof(status), cudaMemcpyDeviceToHost);
+    if (ce != cudaSuccess) {
+        hh->impl.cuda_fail(ce);
+        return cuda_err(err, &hh->impl, "synchronize");
+    }
+    if (status) {
+        cudaMemset(hh->impl.flags + kStatusWord, 0, sizeof(status));
+        return set_err(err, KX_E_TIMEOUT, "synchronize", "a device-side wait expired", status);
     }
     return KX_OK;
 }

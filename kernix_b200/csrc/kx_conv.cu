@@ -349,12 +349,12 @@ int conv_impl(kx_handle *hh, const kx_tensor *in, const kx_tensor *wt, const kx_
     }
     const bool padded = g.py != 0 || g.px != 0;
     if (padded) {
-        ce = cudaMemsetAsync(h->flags, 0, sizeof(uint32_t), h->stream);
+        ce = cudaMemsetAsync(h->flags + kConvFlagWord, 0, sizeof(uint32_t), h->stream);
         if (ce == cudaSuccess) {
             const int64_t wtotal = g.co * g.kk;
             int64_t blocks = (wtotal + 255) / 256;
             if (blocks > 4LL * h->sm_count) blocks = 4LL * h->sm_count;
-            conv_weight_scan<T><<<(unsigned)blocks, 256, 0, h->stream>>>(wp, g, h->flags);
+            conv_weight_scan<T><<<(unsigned)blocks, 256, 0, h->stream>>>(wp, g, h->flags + kConvFlagWord);
             ce = cudaGetLastError();
             ++h->launches;
         }
@@ -373,7 +373,7 @@ int conv_impl(kx_handle *hh, const kx_tensor *in, const kx_tensor *wt, const kx_
     if (ce == cudaSuccess && padded) {
         int64_t blocks = ((int64_t)total + 255) / 256;
         if (blocks > 8LL * h->sm_count) blocks = 8LL * h->sm_count;
-        conv_direct_fixup<T><<<(unsigned)blocks, 256, 0, h->stream>>>(xp, wp, yp, g, h->flags);
+        conv_direct_fixup<T><<<(unsigned)blocks, 256, 0, h->stream>>>(xp, wp, yp, g, h->flags + kConvFlagWord);
         ce = cudaGetLastError();
         ++h->launches;
     }

@@ -82,6 +82,18 @@ int run_gemm(Handle *h, GemmParams<T> p, const char **kernel_name) {
     p.k_per_split = p.K;
     p.ws = nullptr;
     cudaError_t ce;
+    if constexpr (std::is_same<T, float>::value) {
+        // Split-TF32 tensor-core path: eligible layouts, enough 128x256 tiles to
+        // fill the machine, and not the ordered (bitwise reference) mode.
+        if (!h->ordered && h->f32_variant != KX_F32_FFMA && tc_eligible(p)) {
+            const int64_t tc_tiles = (int64_t)((p.M + 127) / 128) * ((p.N + 255) / 256) * p.nbatch;
+            const bool big = tc_tiles >= h->sm_count / 2 && p.K >= 64;
+            if (h->f32_variant == KX_F32_3XTF32 || big) {
+                int rc = run_gemm_tc(h, p, kernel_name);
+                if (rc != KX_DECLINED) return rc;
+            }
+        }
+    }
     if (h->ordered) {
         // Ordered mode: one pass over k per output, separately rounded
         // multiply and add -- bitwise equal to the reference's ordered path.

@@ -1,0 +1,522 @@
+// Split-TF32 ("3xTF32") f32 GEMM on the 5th-generation tensor cores (tcgen05).
+//
+// Each f32 operand x is split into hi = rna_tf32(x) and lo = rna_tf32(x - hi)
+// (x - hi is exact in f32), and C = A_hi B_hi + A_hi B_lo + A_lo B_hi is
+// accumulated in f32 in tensor memory.  Representation error per product is at
+// most 3 * 2^-22 |a b| (hi, lo each carry 11 significant bits; the dropped
+// lo*lo term is below 2^-22 |a b|), inside the f32 bound the reference's tests
+// use, |x - y| <= 2e-6 sum|a b| (small_matmul_tests.rs:153-186).
+//
+// Pipeline per CTA (one 128 x 256 output tile, 256 threads):
+//   warp 0      TMA producer: raw f32 tiles of A and B into stage s (k depth 16)
+//   warp 1      TMEM owner and MMA issuer: 3 x 2 tcgen05.mma (kind::tf32) per stage
+//   warps 2..7  converters: rewrite the raw tile as hi in place, write lo beside it
+//   warps 4..7  epilogue: tcgen05.ld the 128 x 256 f32 accumulator, store to C
+// Stages: 4 x (A hi 8 KB, A lo 8 KB, B hi 16 KB, B lo 16 KB) = 192 KB.
+// A is read K-major (unit stride along k; SWIZZLE_64B), B either MN-major (unit
+// stride along n; 128-byte swizzle on 32-byte atoms, 32-column boxes) or K-major
+// (SWIZZLE_64B).
+// Loads are plain (non-cluster) TMA, one per CTA, from this GPU's memory only.
+//
+// Every mbarrier wait is bounded by a %globaltimer deadline; on expiry the
+// kernel records KX_TIMEOUT_FLAG in the handle's status word, lets its own
+// copies drain (bounded again), frees its tensor memory and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "gemm_simt.cuh"
+#include "kx_internal.hpp"
+
+namespace kx {
+namespace tc {
+
+constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4;
+constexpr int A_TILE = BM * BK * 4;                   // 8 KB
+constexpr int B_TILE = BN * BK * 4;                   // 16 KB
+constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 48 KB
+constexpr int BAR_BYTES = 256;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+constexpr int NTHREADS = 256;
+constexpr int CONV_WARP0 = 2, CONV_WARPS = 6;
+constexpr uint32_t TMEM_COLS = 512;   // main (hi*hi) + cross (hi*lo + lo*hi) accumulators
+constexpr uint64_t WAIT_NS = 2000000000ull;           // 2 s per wait
+constexpr uint32_t KX_TIMEOUT_FLAG = 1u;
+
+struct TcParams {
+    // Raw operand views, used only to recompute a tile on the CUDA cores when
+    // its inputs hold inf/NaN (see the epilogue).
+    const float *A;
+    int64_t a_rs, a_bs;
+    const float *B;
+    int64_t b_rs, b_cs, b_bs;
+    float *C;
+    int64_t c_rs;     // row stride of C (elements)
+    int64_t c_bs;     // batch stride of C
+    int M, N, K;
+    int nbatch;
+    int a_batched, b_batched;   // 1 if the operand has its own batch coordinate
+    uint32_t *status;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+// Bounded wait for the phase with the given parity; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    uint64_t deadline = 0;
+    while (true) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+        const uint64_t now = globaltimer();
+        if (deadline == 0) deadline = now + WAIT_NS;
+        else if (now > deadline) return false;
+    }
+}
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int c0, int c1, int c2,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptors (tcgen05 canonical layouts, version 1).
+//   K-major, 64-byte swizzle: 8-row groups 512 B apart (SBO), LBO unused (1).
+//   MN-major 32-bit data uses the 128-byte swizzle on 32-byte atoms
+//   (layout type 1, TMA CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B): atoms of 4 k-rows
+//   x 128 B, 32-element MN blocks LBO apart, 4-row k groups SBO apart.
+__device__ __forceinline__ uint64_t desc_k_sw64(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
+}
+__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46) | ((uint64_t)1 << 61);
+}
+// Instruction descriptor: f32 accumulate, tf32 A and B, M = 128, N = 256.
+__host__ __device__ constexpr uint32_t idesc_tf32(bool b_mn_major) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | (0u << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+           ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    const uint32_t z = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+// 32 consecutive f32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+// x = hi + lo with hi, lo exact tf32 values; nonfinite x keeps lo = 0 so the
+// single hi*hi product reproduces the f32 result's inf/NaN behaviour.
+__device__ __forceinline__ void split(float x, float &hi, float &lo) {
+    hi = tf32_rna(x);
+    if (!isfinite(hi)) hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);   // rounding overflowed
+    lo = isfinite(x) ? tf32_rna(x - hi) : 0.0f;
+}
+
+template <bool B_MN>
+__global__ void __launch_bounds__(NTHREADS, 1)
+gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+    uint64_t *conv = full + STAGES;
+    uint64_t *empty = conv + STAGES;
+    uint64_t *accf = empty + STAGES;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accf + 1);
+    __shared__ int s_fail_storage, s_nonfinite_storage;
+    volatile int &s_fail = s_fail_storage;
+    volatile int &s_nonfinite = s_nonfinite_storage;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_m = (p.M + BM - 1) / BM, tiles_n = (p.N + BN - 1) / BN;
+    int tm, tn;
+    raster(blockIdx.x, tiles_m, tiles_n, 8, tm, tn);
+    const int m0 = tm * BM, n0 = tn * BN;
+    const int batch = blockIdx.y;
+    const int ab = p.a_batched ? batch : 0, bb = p.b_batched ? batch : 0;
+    const int ktiles = (p.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&conv[s], CONV_WARPS);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accf, 1);
+        s_fail = 0;
+        s_nonfinite = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    auto stage_a = [&](int s) { return smem + s * STAGE_BYTES; };
+    auto stage_alo = [&](int s) { return smem + s * STAGE_BYTES + A_TILE; };
+    auto stage_b = [&](int s) { return smem + s * STAGE_BYTES + 2 * A_TILE; };
+    auto stage_blo = [&](int s) { return smem + s * STAGE_BYTES + 2 * A_TILE + B_TILE; };
+
+    if (warp == 0) {
+        // ---- TMA producer ------------------------------------------------
+        if (lane == 0) {
+            int last_issued[STAGES];
+            for (int s = 0; s < STAGES; ++s) last_issued[s] = -1;
+            for (int kt = 0; kt < ktiles && !s_fail; ++kt) {
+                const int s = kt % STAGES;
+                if (kt >= STAGES && !mbar_wait(&empty[s], ((kt / STAGES) - 1) & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                mbar_expect_tx(&full[s], A_TILE + B_TILE);
+                const int k0 = kt * BK;
+                tma_load_3d(stage_a(s), &tmA, k0, m0, ab, &full[s]);
+                if constexpr (B_MN) {
+#pragma unroll
+                    for (int j = 0; j < BN / 32; ++j) tma_load_3d(stage_b(s) + j * 2048, &tmB, n0 + 32 * j, k0, bb, &full[s]);
+                } else {
+                    tma_load_3d(stage_b(s), &tmB, k0, n0, bb, &full[s]);
+                }
+                last_issued[s] = kt;
+            }
+            // Drain: every issued copy must have landed before the CTA exits.
+            for (int s = 0; s < STAGES; ++s)
+                if (last_issued[s] >= 0) mbar_wait(&full[s], (last_issued[s] / STAGES) & 1);
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer ------------------------------------------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_tf32(B_MN);
+            for (int kt = 0; kt < ktiles; ++kt) {
+                const int s = kt % STAGES;
+                if (s_fail || !mbar_wait(&conv[s], (kt / STAGES) & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_hi = smem_u32(stage_a(s)), a_lo = smem_u32(stage_alo(s));
+                const uint32_t b_hi = smem_u32(stage_b(s)), b_lo = smem_u32(stage_blo(s));
+#pragma unroll
+                for (int ks = 0; ks < BK / 8; ++ks) {
+                    const uint64_t dah = desc_k_sw64(a_hi + ks * 32), dal = desc_k_sw64(a_lo + ks * 32);
+                    uint64_t dbh, dbl;
+                    if constexpr (B_MN) {
+                        dbh = desc_mn_sw128(b_hi + ks * 1024, 2048, 512);
+                        dbl = desc_mn_sw128(b_lo + ks * 1024, 2048, 512);
+                    } else {
+                        dbh = desc_k_sw64(b_hi + ks * 32);
+                        dbl = desc_k_sw64(b_lo + ks * 32);
+                    }
+                    // hi*hi accumulates in columns [0, 256); the two cross terms,
+                    // 2^-11 smaller, in [256, 512).  The tensor core's f32
+                    // accumulation rounds toward zero, so keeping the large
+                    // running sum to one addition per k-step (instead of three)
+                    // cuts its accumulated bias threefold.
+                    const uint32_t acc0 = (kt > 0 || ks > 0) ? 1u : 0u;
+                    mma_tf32(tmem, dah, dbh, idesc, acc0);
+                    mma_tf32(tmem + BN, dah, dbl, idesc, acc0);
+                    mma_tf32(tmem + BN, dal, dbh, idesc, 1u);
+                }
+                mma_commit(&empty[s]);
+            }
+            mma_commit(accf);   // arrives once every issued MMA has completed
+        }
+    } else {
+        // ---- converters (warps 2..7) -------------------------------------
+        const int ct = threadIdx.x - CONV_WARP0 * 32;
+        constexpr int NCT = CONV_WARPS * 32;
+        for (int kt = 0; kt < ktiles; ++kt) {
+            const int s = kt % STAGES;
+            if (s_fail || !mbar_wait(&full[s], (kt / STAGES) & 1)) {
+                s_fail = 1;
+                break;
+            }
+            bool bad = false;
+            float4 *a = reinterpret_cast<float4 *>(stage_a(s));
+            float4 *alo = reinterpret_cast<float4 *>(stage_alo(s));
+            for (int i = ct; i < A_TILE / 16; i += NCT) {
+                float4 v = a[i], h, l;
+                bad |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
+                split(v.x, h.x, l.x);
+                split(v.y, h.y, l.y);
+                split(v.z, h.z, l.z);
+                split(v.w, h.w, l.w);
+                a[i] = h;
+                alo[i] = l;
+            }
+            float4 *b = reinterpret_cast<float4 *>(stage_b(s));
+            float4 *blo = reinterpret_cast<float4 *>(stage_blo(s));
+            for (int i = ct; i < B_TILE / 16; i += NCT) {
+                float4 v = b[i], h, l;
+                bad |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
+                split(v.x, h.x, l.x);
+                split(v.y, h.y, l.y);
+                split(v.z, h.z, l.z);
+                split(v.w, h.w, l.w);
+                b[i] = h;
+                blo[i] = l;
+            }
+            if (bad) s_nonfinite = 1;
+            fence_proxy_async();   // generic-proxy writes -> visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&conv[s]);
+        }
+        // ---- epilogue (warps 4..7; warp w reads TMEM lanes 32*(w%4)..) ----
+        if (warp >= 4) {
+            const bool ok = mbar_wait(accf, 0);
+            if (!ok) s_fail = 1;
+            tc_fence_after();
+            if (ok && s_nonfinite) {
+                // inf/NaN in this tile's operands: a cross term such as inf * 0
+                // (lo of an exact tf32 value) would turn inf into NaN, so the
+                // tile is recomputed with plain f32 FMA in increasing k, which
+                // keeps IEEE propagation of the CUDA-core path.
+                const int q = warp - 4;
+                const int row = m0 + q * 32 + lane;
+                if (row < p.M) {
+                    const float *arow = p.A + (int64_t)ab * p.a_bs + (int64_t)row * p.a_rs;
+                    const float *bbat = p.B + (int64_t)bb * p.b_bs;
+                    float *crow = p.C + (int64_t)batch * p.c_bs + (int64_t)row * p.c_rs;
+                    for (int j = 0; j < BN && n0 + j < p.N; ++j) {
+                        const float *bcol = bbat + (int64_t)(n0 + j) * p.b_cs;
+                        float acc = 0.0f;
+                        for (int k = 0; k < p.K; ++k) acc = fmaf(arow[k], bcol[(int64_t)k * p.b_rs], acc);
+                        crow[n0 + j] = acc;
+                    }
+                }
+            } else if (ok) {
+                const int q = warp - 4;
+                const int row = m0 + q * 32 + lane;
+                float *crow = p.C + (int64_t)batch * p.c_bs + (int64_t)row * p.c_rs;
+                const bool vec = (p.c_rs % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
+                                 (p.c_bs % 4 == 0);
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t r[32], x[32];
+                    const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32);
+                    tmem_ld32(taddr + BN, x);
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+                          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+                          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+                          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                        : "r"(taddr));
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(x[j]));
+                    if (row < p.M) {
+                        const int col0 = n0 + c * 32;
+                        if (vec && col0 + 32 <= p.N) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<float4 *>(crow + col0 + j) =
+                                    make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (col0 + j < p.N) crow[col0 + j] = __uint_as_float(r[j]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+    if (threadIdx.x == 0 && s_fail) atomicOr(p.status, KX_TIMEOUT_FLAG);
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+// 3-d f32 tensor map: dims innermost first, strides (bytes) of dims 1 and 2.
+bool make_map(CUtensorMap *map, const float *base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,
+              uint64_t s2_bytes, uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {s1_bytes, s2_bytes};
+    cuuint32_t box[3] = {b0, b1, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+}  // namespace tc
+
+// Layout test for the tensor-core path: A unit stride along k, B unit stride
+// along n or k, 16-byte aligned rows, at most one batch axis.
+bool tc_eligible(const GemmParams<float> &p) {
+    auto a16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+    if (p.M < 1 || p.N < 1 || p.K < 32) return false;
+    if (p.batch.ndims > 1) return false;
+    if (!(p.a_cs == 1 && p.a_rs > 0 && (p.a_rs * 4) % 16 == 0) && !(p.M == 1)) return false;
+    if (p.M == 1 && p.a_cs != 1) return false;
+    const bool b_mn = p.b_cs == 1 && (p.b_rs * 4) % 16 == 0 && p.b_rs > 0;
+    const bool b_k = p.b_rs == 1 && (p.b_cs * 4) % 16 == 0 && p.b_cs > 0;
+    if (!b_mn && !b_k) return false;
+    if (!a16(p.A) || !a16(p.B) || !a16(p.C)) return false;
+    if (p.c_cs != 1 || p.c_rs % 4 != 0) return false;
+    if (p.batch.ndims == 1) {
+        const int64_t as = p.batch.a_str[0], bs = p.batch.b_str[0];
+        if (as < 0 || bs < 0 || (as * 4) % 16 || (bs * 4) % 16) return false;
+        if (p.batch.dims[0] > 65535) return false;
+    }
+    return true;
+}
+
+int run_gemm_tc(Handle *h, const GemmParams<float> &p, const char **kernel_name) {
+    using namespace tc;
+    const bool b_mn = p.b_cs == 1 && (p.b_rs * 4) % 16 == 0 && p.b_rs > 0;
+    const int nb = (int)p.nbatch;
+    const int64_t a_bs = p.batch.ndims == 1 ? p.batch.a_str[0] : 0;
+    const int64_t b_bs = p.batch.ndims == 1 ? p.batch.b_str[0] : 0;
+    const int64_t c_bs = p.batch.ndims == 1 ? p.batch.c_str[0] : 0;
+    const int a_batched = (nb > 1 && a_bs > 0) ? 1 : 0;
+    const int b_batched = (nb > 1 && b_bs > 0) ? 1 : 0;
+    const int64_t a_rs = p.M == 1 ? 16 : p.a_rs;   // a single row: any aligned stride
+    CUtensorMap ma, mb;
+    const uint64_t a_s2 = a_batched ? (uint64_t)a_bs * 4 : (uint64_t)((a_rs * 4 * (int64_t)p.M + 15) / 16 * 16);
+    if (!make_map(&ma, p.A, (uint64_t)p.K, (uint64_t)p.M, a_batched ? (uint64_t)nb : 1, (uint64_t)a_rs * 4, a_s2, BK,
+                  BM, CU_TENSOR_MAP_SWIZZLE_64B))
+        return KX_DECLINED;
+    bool okb;
+    if (b_mn) {
+        const uint64_t s2 = b_batched ? (uint64_t)b_bs * 4 : (uint64_t)((p.b_rs * 4 * (int64_t)p.K + 15) / 16 * 16);
+        okb = make_map(&mb, p.B, (uint64_t)p.N, (uint64_t)p.K, b_batched ? (uint64_t)nb : 1, (uint64_t)p.b_rs * 4, s2,
+                       32, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    } else {
+        const uint64_t s2 = b_batched ? (uint64_t)b_bs * 4 : (uint64_t)((p.b_cs * 4 * (int64_t)p.N + 15) / 16 * 16);
+        okb = make_map(&mb, p.B, (uint64_t)p.K, (uint64_t)p.N, b_batched ? (uint64_t)nb : 1, (uint64_t)p.b_cs * 4, s2,
+                       BK, BN, CU_TENSOR_MAP_SWIZZLE_64B);
+    }
+    if (!okb) return KX_DECLINED;
+    TcParams tp;
+    tp.A = p.A;
+    tp.a_rs = p.a_rs;
+    tp.a_bs = a_bs;
+    tp.B = p.B;
+    tp.b_rs = p.b_rs;
+    tp.b_cs = p.b_cs;
+    tp.b_bs = b_bs;
+    tp.C = p.C;
+    tp.c_rs = p.M == 1 ? 0 : p.c_rs;
+    tp.c_bs = c_bs;
+    tp.M = p.M;
+    tp.N = p.N;
+    tp.K = p.K;
+    tp.nbatch = nb;
+    tp.a_batched = a_batched;
+    tp.b_batched = b_batched;
+    tp.status = h->flags + kStatusWord;
+    const int64_t tiles = (int64_t)((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+    dim3 grid((unsigned)tiles, (unsigned)nb, 1);
+    cudaError_t ce;
+    if (b_mn) {
+        auto k = gemm_3xtf32_kernel<true>;
+        ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (ce == cudaSuccess) {
+            k<<<grid, NTHREADS, SMEM_BYTES, h->stream>>>(ma, mb, tp);
+            ce = cudaGetLastError();
+        }
+        *kernel_name = "tc_3xtf32_128x256_bmn";
+    } else {
+        auto k = gemm_3xtf32_kernel<false>;
+        ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (ce == cudaSuccess) {
+            k<<<grid, NTHREADS, SMEM_BYTES, h->stream>>>(ma, mb, tp);
+            ce = cudaGetLastError();
+        }
+        *kernel_name = "tc_3xtf32_128x256_bk";
+    }
+    ++h->launches;
+    return ce == cudaSuccess ? KX_OK : h->cuda_fail(ce);
+}
+
+}  // namespace kx

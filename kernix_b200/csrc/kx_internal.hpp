@@ -68,6 +68,17 @@ inline int cuda_err(kx_error *e, Handle *h, const char *op) {
 }
 
 template <typename T> int run_gemm(Handle *h, GemmParams<T> p, const char **kernel_name);
+// Split-TF32 tensor-core GEMM (kx_gemm_tc.cu).  KX_DECLINED when a tensor map
+// cannot describe the operands (the caller then uses the SIMT kernel).
+bool tc_eligible(const GemmParams<float> &p);
+int run_gemm_tc(Handle *h, const GemmParams<float> &p, const char **kernel_name);
+// Layout of the handle's device flag area (32-bit words), one owner per word:
+//   [1]     status written by device code: bit 0 = a bounded wait expired
+//   [2..3]  softmax: 64-bit key of the first nonfinite element (8-byte aligned)
+//   [4]     conv2d: some weight is NaN or infinite
+constexpr int kStatusWord = 1;
+constexpr int kSoftmaxWord = 2;
+constexpr int kConvFlagWord = 4;
 
 }  // namespace kx
 

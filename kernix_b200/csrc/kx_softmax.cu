@@ -315,7 +315,7 @@ int softmax_impl(kx_handle *hh, const kx_tensor *src, int64_t axis, T temperatur
     if (dev_prev != h->device) cudaSetDevice(h->device);
     const T *sp = static_cast<const T *>(src->data) + src->origin;
     T *op = static_cast<T *>(out->data) + out->origin;
-    unsigned long long *flag = reinterpret_cast<unsigned long long *>(h->flags);
+    unsigned long long *flag = reinterpret_cast<unsigned long long *>(h->flags + kSoftmaxWord);
     cudaError_t ce = cudaMemsetAsync(flag, 0xff, sizeof(unsigned long long), h->stream);
     if (ce == cudaSuccess) {
         const int64_t blocks_cap = 16LL * h->sm_count;

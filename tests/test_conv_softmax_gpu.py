@@ -176,3 +176,21 @@ def test_softmax_first_nonfinite_indices(kx, torch_cuda):
     with pytest.raises(kx.NonFiniteInput) as ge:
         kx.softmax_temperature(to_dev(y, torch_cuda), -1, 1.0)
     assert ge.value.indices == [1, 5]
+
+
+def test_status_words_do_not_alias(kx, torch_cuda):
+    """softmax's nonfinite record, conv's weight flag and the device status word
+    live in separate words: neither operation reads as an expired wait."""
+    h = kx.handle(0)
+    x = to_dev(np.zeros((4, 8), dtype=np.float32), torch_cuda)
+    kx.softmax_temperature(x, -1, 1.0)
+    h.synchronize()
+    bad = x.clone()
+    bad[1, 2] = float("inf")
+    with pytest.raises(kx.NonFiniteInput):
+        kx.softmax_temperature(bad, -1, 1.0)
+    h.synchronize()
+    w = torch_cuda.ones(2, 1, 3, 3, device="cuda")
+    w[0, 0, 0, 0] = float("nan")
+    kx.conv2d(torch_cuda.ones(1, 1, 5, 5, device="cuda"), w, kx.Conv2dOptions(padding=(1, 1)))
+    h.synchronize()

@@ -1,0 +1,109 @@
+"""Split-TF32 tensor-core GEMM (tcgen05 + TMEM, TMA-fed) against the oracle.
+
+The f32 bound is the reference's scaled form |x - y| <= 2e-6 * sum|a b|
+(small_matmul_tests.rs:153-186); the kernel's representation error per product
+is at most 3 * 2^-22 |a b|.
+"""
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture
+def tc_handle(kx, torch_cuda):
+    h = kx.handle(0)
+    h.set_f32_variant(2)    # KX_F32_3XTF32
+    yield h
+    h.set_f32_variant(0)
+
+
+def _view(kx, torch, arr, dims, strides, origin=0):
+    buf = torch.from_numpy(np.ascontiguousarray(arr).reshape(-1)).cuda()
+    return kx.TensorView(buf, list(dims), list(strides), origin)
+
+
+def _check(got, a, b):
+    exp, ab = oracle.gemm_dot2(a, b)
+    g = got.astype(np.float64)
+    assert np.isfinite(g).all()
+    ratio = np.abs(g - exp) / np.maximum(ab, 1e-300)
+    assert (np.abs(g - exp) <= 2e-6 * ab + 1e-30).all(), float(ratio.max())
+    return float(ratio.max())
+
+
+@pytest.mark.parametrize("m,k,n", [(128, 64, 256), (300, 1000, 260), (1, 64, 256), (520, 48, 1028)])
+@pytest.mark.parametrize("b_layout", ["row", "col"])
+def test_tc_2d_layouts(kx, torch_cuda, tc_handle, m, k, n, b_layout):
+    rng = np.random.default_rng(m * 7 + k)
+    pad = 8
+    abuf = rng.uniform(-1, 1, (m, k + pad)).astype(np.float32)
+    va = oracle.View(abuf, (m, k), (k + pad, 1))
+    if b_layout == "row":
+        bbuf = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+        vb = oracle.View(bbuf, (k, n), (n, 1))
+    else:
+        bbuf = rng.uniform(-1, 1, (n, k)).astype(np.float32)     # B = bbuf^T, unit stride along k
+        vb = oracle.View(bbuf, (k, n), (1, k))
+    got = kx.matmul(_view(kx, torch_cuda, abuf, (m, k), (k + pad, 1)),
+                    _view(kx, torch_cuda, bbuf, vb.dims, vb.strides)).cpu().numpy()
+    assert tc_handle.last_kernel.startswith("tc_3xtf32"), tc_handle.last_kernel
+    tc_handle.synchronize()
+    _check(got, va, vb)
+
+
+def test_tc_batched_and_broadcast(kx, torch_cuda, tc_handle):
+    torch = torch_cuda
+    rng = np.random.default_rng(5)
+    a = rng.uniform(-1, 1, (4, 256, 96)).astype(np.float32)
+    b = rng.uniform(-1, 1, (4, 96, 512)).astype(np.float32)
+    bb = rng.uniform(-1, 1, (1, 96, 512)).astype(np.float32)
+    for bm in (b, bb):
+        got = kx.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(bm).cuda()).cpu().numpy()
+        assert tc_handle.last_kernel.startswith("tc_3xtf32")
+        for i in range(4):
+            _check(got[i], oracle.View.of(a[i]), oracle.View.of(bm[min(i, bm.shape[0] - 1)]))
+    # attention-shaped: Q [2,4,256,128] x K^T (K [2,4,256,128] viewed transposed): batch axes merge
+    q = rng.uniform(-1, 1, (2, 4, 256, 128)).astype(np.float32)
+    kk = rng.uniform(-1, 1, (2, 4, 256, 128)).astype(np.float32)
+    s = kx.matmul(torch.from_numpy(q).cuda(), torch.from_numpy(kk).cuda().transpose(2, 3)).cpu().numpy()
+    assert tc_handle.last_kernel == "tc_3xtf32_128x256_bk"
+    for i, j in [(0, 0), (1, 3)]:
+        _check(s[i, j], oracle.View.of(q[i, j]), oracle.View(kk[i, j], (128, 256), (1, 128)))
+    tc_handle.synchronize()
+
+
+def test_tc_nonfinite_keeps_ieee_propagation(kx, torch_cuda, tc_handle):
+    """An inf in A must give inf (not NaN from inf * 0 in a cross term)."""
+    torch = torch_cuda
+    a = np.full((128, 64), 0.5, dtype=np.float32)
+    b = np.ones((64, 256), dtype=np.float32)
+    a[3, 7] = np.inf
+    a[5, 2] = np.nan
+    got = kx.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()).cpu().numpy()
+    tc_handle.set_f32_variant(1)
+    ref = kx.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()).cpu().numpy()
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    assert np.array_equal(np.isinf(got), np.isinf(ref))
+    assert np.isinf(got[3]).all() and np.isnan(got[5]).all()
+    fin = np.isfinite(ref)
+    assert np.array_equal(got[fin], ref[fin])
+
+
+def test_auto_selects_tensor_cores_for_large_products(kx, torch_cuda):
+    torch = torch_cuda
+    h = kx.handle(0)
+    h.set_f32_variant(0)
+    a = torch.rand(2048, 512, device="cuda") * 2 - 1
+    b = torch.rand(512, 2048, device="cuda") * 2 - 1
+    c = kx.matmul(a, b)
+    assert h.last_kernel.startswith("tc_3xtf32"), h.last_kernel
+    exp, ab = oracle.gemm_dot2(oracle.View.of(a.cpu().numpy()[:64]), oracle.View.of(b.cpu().numpy()))
+    assert (np.abs(c[:64].cpu().numpy().astype(np.float64) - exp) <= 2e-6 * ab).all()
+    h.set_f32_variant(1)
+    kx.matmul(a, b)
+    assert h.last_kernel.startswith("simt"), h.last_kernel
+    h.set_f32_variant(0)
+    h.synchronize()
