@@ -79,7 +79,7 @@ class ClockSampler:
         "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
     }
 
-    def __init__(self, index: int, period: float = 0.1):
+    def __init__(self, index: int, period: float = 0.02):
         self.samples, self.reasons = [], set()
         self.period = period
         self._stop = threading.Event()

@@ -1,22 +1,26 @@
 // Split-TF32 ("3xTF32") f32 GEMM on the 5th-generation tensor cores (tcgen05).
 //
-// Each f32 operand x is split into hi = rna_tf32(x) and lo = rna_tf32(x - hi)
-// (x - hi is exact in f32), and C = A_hi B_hi + A_hi B_lo + A_lo B_hi is
-// accumulated in f32 in tensor memory.  Representation error per product is at
-// most 3 * 2^-22 |a b| (hi, lo each carry 11 significant bits; the dropped
-// lo*lo term is below 2^-22 |a b|), inside the f32 bound the reference's tests
-// use, |x - y| <= 2e-6 sum|a b| (small_matmul_tests.rs:153-186).
+// Each f32 operand x is split into hi = rna_tf32(x) and lo = x - hi (exact in
+// f32), and C = A_hi B_hi + A_hi B_lo + A_lo B_hi is accumulated in f32 in
+// tensor memory.  Representation error per product is at most ~1.2e-6 |a b|
+// (see split below), inside the f32 bound the reference's tests use,
+// |x - y| <= 2e-6 sum|a b| (small_matmul_tests.rs:153-186).
 //
-// Pipeline per CTA (one 128 x 256 output tile, 256 threads):
-//   warp 0      TMA producer: raw f32 tiles of A and B into stage s (k depth 16)
-//   warp 1      TMEM owner and MMA issuer: 3 x 2 tcgen05.mma (kind::tf32) per stage
-//   warps 2..7  converters: rewrite the raw tile as hi in place, write lo beside it
-//   warps 4..7  epilogue: tcgen05.ld the 128 x 256 f32 accumulator, store to C
+// Pipeline per CTA (one 128 x 256 output tile, 384 threads):
+//   warp 0       TMA producer: raw f32 tiles of A and B into stage s (k depth 16)
+//   warp 1       TMEM owner and MMA issuer: 3 x 2 tcgen05.mma (kind::tf32) per stage
+//   warps 4..11  workers: rewrite each raw tile as hi in place and write lo beside
+//                it; every 64 k-tiles fold the hi*hi accumulator into f32
+//                registers (128 columns of one row per thread); at the end add
+//                the cross-term accumulator and store C
 // Stages: 4 x (A hi 8 KB, A lo 8 KB, B hi 16 KB, B lo 16 KB) = 192 KB.
+// The tensor core's f32 accumulation truncates, so the large hi*hi sum is
+// restarted every 1024 k and summed with round-to-nearest adds on the CUDA
+// cores; the small cross terms keep one TMEM accumulator over all of K.
 // A is read K-major (unit stride along k; SWIZZLE_64B), B either MN-major (unit
 // stride along n; 128-byte swizzle on 32-byte atoms, 32-column boxes) or K-major
-// (SWIZZLE_64B).
-// Loads are plain (non-cluster) TMA, one per CTA, from this GPU's memory only.
+// (SWIZZLE_64B).  Loads are plain (non-cluster) TMA, one per CTA, from this
+// GPU's memory only.
 //
 // Every mbarrier wait is bounded by a %globaltimer deadline; on expiry the
 // kernel records KX_TIMEOUT_FLAG in the handle's status word, lets its own
@@ -37,10 +41,14 @@ constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4;
 constexpr int A_TILE = BM * BK * 4;                   // 8 KB
 constexpr int B_TILE = BN * BK * 4;                   // 16 KB
 constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 48 KB
-constexpr int BAR_BYTES = 256;
+constexpr int BAR_BYTES = 256;   // 3 x STAGES + 2 mbarriers and the TMEM address
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
-constexpr int NTHREADS = 256;
-constexpr int CONV_WARP0 = 2, CONV_WARPS = 6;
+constexpr int NTHREADS = 384;                        // 12 warps
+constexpr int WORK_WARP0 = 4, WORK_WARPS = 8, WORK_THREADS = WORK_WARPS * 32;
+constexpr int HALF_COLS = BN / 2;                     // accumulator columns per worker thread
+constexpr int KC = 64;                                // k-tiles (1024 k) per hi*hi chunk
+constexpr int CONV_CHUNKS = (A_TILE + B_TILE) / 16;   // 1536 chunks = 6 per worker thread
+static_assert(CONV_CHUNKS % WORK_THREADS == 0, "converter work must divide evenly");
 constexpr uint32_t TMEM_COLS = 512;   // main (hi*hi) + cross (hi*lo + lo*hi) accumulators
 constexpr uint64_t WAIT_NS = 2000000000ull;           // 2 s per wait
 constexpr uint32_t KX_TIMEOUT_FLAG = 1u;
@@ -160,12 +168,42 @@ __device__ __forceinline__ float tf32_rna(float x) {
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
     return __uint_as_float(r);
 }
-// x = hi + lo with hi, lo exact tf32 values; nonfinite x keeps lo = 0 so the
-// single hi*hi product reproduces the f32 result's inf/NaN behaviour.
-__device__ __forceinline__ void split(float x, float &hi, float &lo) {
-    hi = tf32_rna(x);
-    if (!isfinite(hi)) hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);   // rounding overflowed
-    lo = isfinite(x) ? tf32_rna(x - hi) : 0.0f;
+// Split x = hi + lo: hi = rna_tf32(x) and lo = x - hi (exact in f32).  The MMA
+// reads lo with tf32 precision, so per product the error is at most
+// 2^-21 (hi x lo_b) + 2^-21 (lo_a x hi) + 2^-22 (dropped lo x lo), about
+// 1.2e-6 |a b|.  A nonzero result marks an exponent of all ones: an inf/NaN
+// input, or a finite input whose rounding overflowed.
+__device__ __forceinline__ uint32_t nonfinite_bits(float h) {
+    return (__float_as_uint(h) & 0x7F800000u) == 0x7F800000u ? 1u : 0u;
+}
+
+// 16 consecutive f32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Add this thread's half row (128 columns starting at col0) of the TMEM
+// accumulator at `tcol` into the register running sum.
+__device__ __forceinline__ void tmem_accumulate(uint32_t tmem, int quarter, int col0, float (&sum)[HALF_COLS]) {
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col0;
+#pragma unroll
+    for (int c = 0; c < HALF_COLS / 32; ++c) {
+        uint32_t r0[16], r1[16];   // two loads in flight per wait
+        tmem_ld16(lane_base + (uint32_t)(c * 32), r0);
+        tmem_ld16(lane_base + (uint32_t)(c * 32 + 16), r1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            sum[c * 32 + j] += __uint_as_float(r0[j]);
+            sum[c * 32 + 16 + j] += __uint_as_float(r1[j]);
+        }
+    }
 }
 
 template <bool B_MN>
@@ -177,8 +215,9 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
     uint64_t *conv = full + STAGES;
     uint64_t *empty = conv + STAGES;
-    uint64_t *accf = empty + STAGES;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accf + 1);
+    uint64_t *chunk_full = empty + STAGES;
+    uint64_t *chunk_empty = chunk_full + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(chunk_empty + 1);
     __shared__ int s_fail_storage, s_nonfinite_storage;
     volatile int &s_fail = s_fail_storage;
     volatile int &s_nonfinite = s_nonfinite_storage;
@@ -191,14 +230,16 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     const int batch = blockIdx.y;
     const int ab = p.a_batched ? batch : 0, bb = p.b_batched ? batch : 0;
     const int ktiles = (p.K + BK - 1) / BK;
+    const int nchunks = (ktiles + KC - 1) / KC;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&conv[s], CONV_WARPS);
+            mbar_init(&conv[s], WORK_WARPS);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(accf, 1);
+        mbar_init(chunk_full, 1);
+        mbar_init(chunk_empty, WORK_WARPS);
         s_fail = 0;
         s_nonfinite = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -222,8 +263,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     if (warp == 0) {
         // ---- TMA producer ------------------------------------------------
         if (lane == 0) {
-            int last_issued[STAGES];
-            for (int s = 0; s < STAGES; ++s) last_issued[s] = -1;
+            int issued = 0;   // k-tiles whose copies were issued
             for (int kt = 0; kt < ktiles && !s_fail; ++kt) {
                 const int s = kt % STAGES;
                 if (kt >= STAGES && !mbar_wait(&empty[s], ((kt / STAGES) - 1) & 1)) {
@@ -239,18 +279,29 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 } else {
                     tma_load_3d(stage_b(s), &tmB, k0, n0, bb, &full[s]);
                 }
-                last_issued[s] = kt;
+                issued = kt + 1;
             }
-            // Drain: every issued copy must have landed before the CTA exits.
-            for (int s = 0; s < STAGES; ++s)
-                if (last_issued[s] >= 0) mbar_wait(&full[s], (last_issued[s] / STAGES) & 1);
+            // Drain: every issued copy must have landed before the CTA exits
+            // (the last k-tile issued into each stage).
+            for (int s = 0; s < STAGES && s < issued; ++s) {
+                const int last = s + STAGES * ((issued - 1 - s) / STAGES);
+                mbar_wait(&full[s], (last / STAGES) & 1);
+            }
         }
     } else if (warp == 1) {
         // ---- MMA issuer ------------------------------------------------
+        // hi*hi accumulates per chunk of KC k-tiles in columns [0, 256) (the
+        // workers fold each chunk into f32 registers); the two cross terms,
+        // 2^-11 smaller, accumulate over all of K in [256, 512).
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_tf32(B_MN);
             for (int kt = 0; kt < ktiles; ++kt) {
                 const int s = kt % STAGES;
+                const int chunk = kt / KC, kin = kt % KC;
+                if (kin == 0 && chunk > 0 && (s_fail || !mbar_wait(chunk_empty, (chunk - 1) & 1))) {
+                    s_fail = 1;
+                    break;
+                }
                 if (s_fail || !mbar_wait(&conv[s], (kt / STAGES) & 1)) {
                     s_fail = 1;
                     break;
@@ -269,120 +320,118 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                         dbh = desc_k_sw64(b_hi + ks * 32);
                         dbl = desc_k_sw64(b_lo + ks * 32);
                     }
-                    // hi*hi accumulates in columns [0, 256); the two cross terms,
-                    // 2^-11 smaller, in [256, 512).  The tensor core's f32
-                    // accumulation rounds toward zero, so keeping the large
-                    // running sum to one addition per k-step (instead of three)
-                    // cuts its accumulated bias threefold.
-                    const uint32_t acc0 = (kt > 0 || ks > 0) ? 1u : 0u;
-                    mma_tf32(tmem, dah, dbh, idesc, acc0);
-                    mma_tf32(tmem + BN, dah, dbl, idesc, acc0);
+                    mma_tf32(tmem, dah, dbh, idesc, (kin > 0 || ks > 0) ? 1u : 0u);
+                    mma_tf32(tmem + BN, dah, dbl, idesc, (kt > 0 || ks > 0) ? 1u : 0u);
                     mma_tf32(tmem + BN, dal, dbh, idesc, 1u);
                 }
                 mma_commit(&empty[s]);
+                if (kin == KC - 1 || kt == ktiles - 1) mma_commit(chunk_full);   // chunk done (and all before it)
             }
-            mma_commit(accf);   // arrives once every issued MMA has completed
+            if (s_fail) mma_commit(chunk_full);   // release workers waiting on a chunk
         }
-    } else {
-        // ---- converters (warps 2..7) -------------------------------------
-        const int ct = threadIdx.x - CONV_WARP0 * 32;
-        constexpr int NCT = CONV_WARPS * 32;
+    } else if (warp >= WORK_WARP0) {
+        // ---- workers (warps 4..11): convert, fold chunks, epilogue -------
+        const int wt = threadIdx.x - WORK_WARP0 * 32;           // 0..255
+        const int quarter = warp & 3;                           // TMEM lanes 32*quarter..
+        const int col0 = ((warp - WORK_WARP0) >> 2) * HALF_COLS; // this warp's column half
+        float sum[HALF_COLS];
+#pragma unroll
+        for (int j = 0; j < HALF_COLS; ++j) sum[j] = 0.0f;
+        int chunk = 0;
         for (int kt = 0; kt < ktiles; ++kt) {
             const int s = kt % STAGES;
             if (s_fail || !mbar_wait(&full[s], (kt / STAGES) & 1)) {
                 s_fail = 1;
                 break;
             }
-            bool bad = false;
-            float4 *a = reinterpret_cast<float4 *>(stage_a(s));
-            float4 *alo = reinterpret_cast<float4 *>(stage_alo(s));
-            for (int i = ct; i < A_TILE / 16; i += NCT) {
-                float4 v = a[i], h, l;
-                bad |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
-                split(v.x, h.x, l.x);
-                split(v.y, h.y, l.y);
-                split(v.z, h.z, l.z);
-                split(v.w, h.w, l.w);
-                a[i] = h;
-                alo[i] = l;
+            // The A and B tiles of the stage are 1536 16-byte chunks (A hi: 512
+            // at offset 0, B hi: 1024 at 16 KB); each of the 256 worker threads
+            // splits 6 of them, lo going to the buffer beside its hi.
+            uint32_t bad = 0;
+            uint8_t *base = stage_a(s);
+#pragma unroll
+            for (int j = 0; j < CONV_CHUNKS / WORK_THREADS; ++j) {
+                const int c = wt + j * WORK_THREADS;
+                const bool in_a = c < A_TILE / 16;
+                float4 *hp = reinterpret_cast<float4 *>(base + (in_a ? c * 16 : 2 * A_TILE + (c - A_TILE / 16) * 16));
+                float4 *lp = reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(hp) + (in_a ? A_TILE : B_TILE));
+                const float4 v = *hp;
+                float4 h, l;
+                h.x = tf32_rna(v.x);
+                h.y = tf32_rna(v.y);
+                h.z = tf32_rna(v.z);
+                h.w = tf32_rna(v.w);
+                l.x = v.x - h.x;
+                l.y = v.y - h.y;
+                l.z = v.z - h.z;
+                l.w = v.w - h.w;
+                bad |= nonfinite_bits(h.x) | nonfinite_bits(h.y) | nonfinite_bits(h.z) | nonfinite_bits(h.w);
+                *hp = h;
+                *lp = l;
             }
-            float4 *b = reinterpret_cast<float4 *>(stage_b(s));
-            float4 *blo = reinterpret_cast<float4 *>(stage_blo(s));
-            for (int i = ct; i < B_TILE / 16; i += NCT) {
-                float4 v = b[i], h, l;
-                bad |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
-                split(v.x, h.x, l.x);
-                split(v.y, h.y, l.y);
-                split(v.z, h.z, l.z);
-                split(v.w, h.w, l.w);
-                b[i] = h;
-                blo[i] = l;
-            }
-            if (bad) s_nonfinite = 1;
-            fence_proxy_async();   // generic-proxy writes -> visible to the tensor core
+            if (bad) s_nonfinite = 1;   // inf/NaN input or a rounding overflow: FMA fallback
+            fence_proxy_async();        // generic-proxy writes -> visible to the tensor core
             __syncwarp();
             if (lane == 0) mbar_arrive(&conv[s]);
+            if (kt % KC == KC - 1 || kt == ktiles - 1) {
+                // Fold the finished chunk of hi*hi into the register sum.
+                if (!mbar_wait(chunk_full, chunk & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                if (s_fail) break;
+                tmem_accumulate(tmem, quarter, col0, sum);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(chunk_empty);
+                ++chunk;
+            }
         }
-        // ---- epilogue (warps 4..7; warp w reads TMEM lanes 32*(w%4)..) ----
-        if (warp >= 4) {
-            const bool ok = mbar_wait(accf, 0);
-            if (!ok) s_fail = 1;
-            tc_fence_after();
-            if (ok && s_nonfinite) {
+        // ---- epilogue ------------------------------------------------------
+        const int row = m0 + quarter * 32 + lane;
+        if (!s_fail && chunk == nchunks) {
+            if (s_nonfinite) {
                 // inf/NaN in this tile's operands: a cross term such as inf * 0
                 // (lo of an exact tf32 value) would turn inf into NaN, so the
                 // tile is recomputed with plain f32 FMA in increasing k, which
                 // keeps IEEE propagation of the CUDA-core path.
-                const int q = warp - 4;
-                const int row = m0 + q * 32 + lane;
                 if (row < p.M) {
                     const float *arow = p.A + (int64_t)ab * p.a_bs + (int64_t)row * p.a_rs;
                     const float *bbat = p.B + (int64_t)bb * p.b_bs;
                     float *crow = p.C + (int64_t)batch * p.c_bs + (int64_t)row * p.c_rs;
-                    for (int j = 0; j < BN && n0 + j < p.N; ++j) {
-                        const float *bcol = bbat + (int64_t)(n0 + j) * p.b_cs;
+                    for (int j = 0; j < HALF_COLS && n0 + col0 + j < p.N; ++j) {
+                        const float *bcol = bbat + (int64_t)(n0 + col0 + j) * p.b_cs;
                         float acc = 0.0f;
                         for (int k = 0; k < p.K; ++k) acc = fmaf(arow[k], bcol[(int64_t)k * p.b_rs], acc);
-                        crow[n0 + j] = acc;
+                        crow[n0 + col0 + j] = acc;
                     }
                 }
-            } else if (ok) {
-                const int q = warp - 4;
-                const int row = m0 + q * 32 + lane;
-                float *crow = p.C + (int64_t)batch * p.c_bs + (int64_t)row * p.c_rs;
+            } else {
+                // Stream out: 16 columns of cross terms at a time, added to the
+                // running sum and stored straight away.
+                const bool in_rows = row < p.M;
+                float *crow = p.C + (int64_t)batch * p.c_bs + (int64_t)(in_rows ? row : 0) * p.c_rs + n0 + col0;
                 const bool vec = (p.c_rs % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
                                  (p.c_bs % 4 == 0);
-#pragma unroll 1
-                for (int c = 0; c < BN / 32; ++c) {
-                    uint32_t r[32], x[32];
-                    const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32);
-                    tmem_ld32(taddr + BN, x);
-                    asm volatile(
-                        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-                        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-                          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-                          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-                          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-                          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-                        : "r"(taddr));
-                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(x[j]));
-                    if (row < p.M) {
-                        const int col0 = n0 + c * 32;
-                        if (vec && col0 + 32 <= p.N) {
+                for (int c = 0; c < HALF_COLS / 16; ++c) {
+                    uint32_t r[16];
+                    tmem_ld16(tmem + BN + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(col0 + c * 16), r);
+                    tmem_wait_ld();
+                    if (!in_rows) continue;
+                    float v[16];
 #pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                *reinterpret_cast<float4 *>(crow + col0 + j) =
-                                    make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-                        } else {
+                    for (int j = 0; j < 16; ++j) v[j] = sum[c * 16 + j] + __uint_as_float(r[j]);
+                    const int gcol = n0 + col0 + c * 16;
+                    if (vec && gcol + 16 <= p.N) {
 #pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (col0 + j < p.N) crow[col0 + j] = __uint_as_float(r[j]);
-                        }
+                        for (int j = 0; j < 16; j += 4)
+                            *reinterpret_cast<float4 *>(crow + c * 16 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (gcol + j < p.N) crow[c * 16 + j] = v[j];
                     }
                 }
             }
