@@ -201,6 +201,7 @@ def run_ours(args, rank, world, local):
         end.record()
         barrier()
     launches = h.launches - launches0
+    h.synchronize()   # raises DeviceTimeout if any bounded device wait expired
     elapsed = start.elapsed_time(end) / 1e3
     t = torch.tensor([elapsed], dtype=torch.float64, device=dev)
     if world > 1:

@@ -1,16 +1,16 @@
 // Split-TF32 ("3xTF32") f32 GEMM on the 5th-generation tensor cores (tcgen05).
 //
-// Each f32 operand x is split into hi = rna_tf32(x) and lo = x - hi (exact in
-// f32), and C = A_hi B_hi + A_hi B_lo + A_lo B_hi is accumulated in f32 in
-// tensor memory.  Representation error per product is at most ~1.2e-6 |a b|
-// (see split below), inside the f32 bound the reference's tests use,
-// |x - y| <= 2e-6 sum|a b| (small_matmul_tests.rs:153-186).
+// Each f32 operand x is split into hi = x truncated to tf32 and lo = x - hi
+// (exact in f32), and C = A_hi B_hi + A_hi B_lo + A_lo B_hi is accumulated in
+// f32 in tensor memory.  Representation error per product stays below
+// ~1.7e-6 |a b| (see tf32_trunc below), inside the f32 bound the reference's
+// tests use, |x - y| <= 2e-6 sum|a b| (small_matmul_tests.rs:153-186).
 //
 // Pipeline per CTA (one 128 x 256 output tile, 384 threads):
 //   warp 0       TMA producer: raw f32 tiles of A and B into stage s (k depth 16)
 //   warp 1       TMEM owner and MMA issuer: 3 x 2 tcgen05.mma (kind::tf32) per stage
-//   warps 4..11  workers: rewrite each raw tile as hi in place and write lo beside
-//                it; every 64 k-tiles fold the hi*hi accumulator into f32
+//   warps 4..11  workers: write lo beside each raw tile (the raw tile is hi);
+//                every 64 k-tiles fold the hi*hi accumulator into f32
 //                registers (128 columns of one row per thread); at the end add
 //                the cross-term accumulator and store C
 // Stages: 4 x (A hi 8 KB, A lo 8 KB, B hi 16 KB, B lo 16 KB) = 192 KB.
@@ -163,18 +163,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
 }
-__device__ __forceinline__ float tf32_rna(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
-}
-// Split x = hi + lo: hi = rna_tf32(x) and lo = x - hi (exact in f32).  The MMA
-// reads lo with tf32 precision, so per product the error is at most
-// 2^-21 (hi x lo_b) + 2^-21 (lo_a x hi) + 2^-22 (dropped lo x lo), about
-// 1.2e-6 |a b|.  A nonzero result marks an exponent of all ones: an inf/NaN
-// input, or a finite input whose rounding overflowed.
-__device__ __forceinline__ uint32_t nonfinite_bits(float h) {
-    return (__float_as_uint(h) & 0x7F800000u) == 0x7F800000u ? 1u : 0u;
+// Split x = hi + lo with hi = x truncated to tf32 (its low 13 mantissa bits
+// cleared) and lo = x - hi, exact in f32.  The tensor core itself reads f32
+// operands of a kind::tf32 MMA truncated to tf32, so the raw tile serves as hi
+// unchanged and only lo is written.  lo has at most 13 significant bits and the
+// MMA keeps 11 of them; with the dropped lo*lo term the error per product stays
+// below ~1.7e-6 |a b| even for adversarial mantissas.
+__device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+// Exponent of all ones: an inf or NaN input.
+__device__ __forceinline__ uint32_t nonfinite_bits(float x) {
+    return (__float_as_uint(x) & 0x7F800000u) == 0x7F800000u ? 1u : 0u;
 }
 
 // 16 consecutive f32 columns of this thread's TMEM lane.
@@ -355,21 +353,16 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 const bool in_a = c < A_TILE / 16;
                 float4 *hp = reinterpret_cast<float4 *>(base + (in_a ? c * 16 : 2 * A_TILE + (c - A_TILE / 16) * 16));
                 float4 *lp = reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(hp) + (in_a ? A_TILE : B_TILE));
-                const float4 v = *hp;
-                float4 h, l;
-                h.x = tf32_rna(v.x);
-                h.y = tf32_rna(v.y);
-                h.z = tf32_rna(v.z);
-                h.w = tf32_rna(v.w);
-                l.x = v.x - h.x;
-                l.y = v.y - h.y;
-                l.z = v.z - h.z;
-                l.w = v.w - h.w;
-                bad |= nonfinite_bits(h.x) | nonfinite_bits(h.y) | nonfinite_bits(h.z) | nonfinite_bits(h.w);
-                *hp = h;
+                const float4 v = *hp;   // stays in place: the MMA reads it as hi
+                float4 l;
+                l.x = v.x - tf32_trunc(v.x);
+                l.y = v.y - tf32_trunc(v.y);
+                l.z = v.z - tf32_trunc(v.z);
+                l.w = v.w - tf32_trunc(v.w);
+                bad |= nonfinite_bits(v.x) | nonfinite_bits(v.y) | nonfinite_bits(v.z) | nonfinite_bits(v.w);
                 *lp = l;
             }
-            if (bad) s_nonfinite = 1;   // inf/NaN input or a rounding overflow: FMA fallback
+            if (bad) s_nonfinite = 1;   // inf/NaN input: FMA fallback for this tile
             fence_proxy_async();        // generic-proxy writes -> visible to the tensor core
             __syncwarp();
             if (lane == 0) mbar_arrive(&conv[s]);

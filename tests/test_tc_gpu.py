@@ -2,7 +2,7 @@
 
 The f32 bound is the reference's scaled form |x - y| <= 2e-6 * sum|a b|
 (small_matmul_tests.rs:153-186); the kernel's representation error per product
-is at most 3 * 2^-22 |a b|.
+stays below ~1.7e-6 |a b| (hi = truncated tf32, lo = x - hi read as tf32).
 """
 import numpy as np
 import pytest
