@@ -14,6 +14,7 @@
 #include <cfloat>
 #include <cmath>
 #include <cstring>
+#include <limits>
 #include <type_traits>
 
 #include "kx_internal.hpp"
@@ -33,9 +34,16 @@ struct RowGeom {
     int64_t odims[kMaxOuter];   // outer dims (axis removed), C order
     int64_t sstr[kMaxOuter];    // source strides of the outer dims
     int64_t ostr[kMaxOuter];    // output strides of the outer dims
+    int collapsed;              // row r starts at r * rs_s (source) and r * rs_o (output)
+    int64_t rs_s, rs_o;
 };
 
 __device__ __forceinline__ void row_bases(const RowGeom &g, int64_t row, int64_t &sb, int64_t &ob) {
+    if (g.collapsed) {
+        sb = row * g.rs_s;
+        ob = row * g.rs_o;
+        return;
+    }
     sb = ob = 0;
     for (int d = g.nouter - 1; d >= 0; --d) {
         int64_t c = row % g.odims[d];
@@ -53,6 +61,39 @@ template <typename T>
 __device__ __forceinline__ T scaled_difference(T v, T m, T t) {
     T d = v - m;
     return isfinite(d) ? d / t : v / t - m / t;
+}
+
+// a / b from y = 1/b (the correctly rounded reciprocal) and one residual
+// correction, Markstein's scheme ("IA-64 and Elementary Functions", 2000):
+// q0 = a*y, r = a - b*q0 (exact through the fused multiply-add), q = q0 + r*y.
+// The result is within one ulp of the IEEE quotient (equal to it for almost
+// all operands) and costs three FMA-pipe instructions instead of a division.
+// Used only when y is a normal number (checked on the host).
+template <typename T>
+__device__ __forceinline__ T div_by(T a, T b, T y) {
+    const T q = a * y;
+    const T r = fma(-b, q, a);
+    return fma(r, y, q);
+}
+
+template <typename T> struct Vec16;
+template <> struct Vec16<float> {
+    using type = float4;
+    static constexpr int n = 4;
+};
+template <> struct Vec16<double> {
+    using type = double2;
+    static constexpr int n = 2;
+};
+template <typename V, typename T> __device__ __forceinline__ T &lane_of(V &v, int c) {
+    return reinterpret_cast<T *>(&v)[c];
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_min(T v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmin(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
 }
 
 template <typename T>
@@ -188,6 +229,124 @@ __global__ void __launch_bounds__(256) softmax_rows_warp_vec(const float *__rest
     }
 }
 
+// Contiguous rows that fit in registers (unit stride along the axis, 16-byte
+// aligned rows): one 256-thread block per row, NV 16-byte vectors per thread,
+// grid-stride over rows.  A block per row keeps ~30 registers per thread, so
+// 16 blocks share an SM and their loads overlap each other's exp/normalise
+// phases (a warp per row at 2048 elements ran at half the HBM rate).
+// Nonfinite inputs are detected from the row's max, min and sum (a NaN or +inf
+// makes the sum NaN, a -inf shows as the minimum); such rows are rescanned
+// from memory for the first bad index and nothing is written for them.
+template <typename T, int NV>
+__global__ void __launch_bounds__(256) softmax_rows_block_vec(const T *__restrict__ src, T *__restrict__ out,
+                                                              const __grid_constant__ RowGeom g, T temperature,
+                                                              T recip, int use_recip,
+                                                              unsigned long long *first_bad) {
+    using V = typename Vec16<T>::type;
+    constexpr int VN = Vec16<T>::n;
+    constexpr int NW = 8;
+    __shared__ T red[2][2][NW];
+    __shared__ int64_t redi[NW];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t lenv = g.len / VN;
+    int par = 0;
+    for (int64_t row = blockIdx.x; row < g.rows; row += gridDim.x, par ^= 1) {
+        int64_t sb, ob;
+        row_bases(g, row, sb, ob);
+        const V *sv = reinterpret_cast<const V *>(src + sb);
+        V v[NV];
+        T mx = -INFINITY, mn = INFINITY;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int64_t q = threadIdx.x + 256 * i;
+            if (q < lenv) {
+                v[i] = __ldg(sv + q);
+#pragma unroll
+                for (int c = 0; c < VN; ++c) {
+                    mx = fmax(mx, lane_of<V, T>(v[i], c));
+                    mn = fmin(mn, lane_of<V, T>(v[i], c));
+                }
+            }
+        }
+        mx = warp_max(mx);
+        mn = warp_min(mn);
+        if (lane == 0) {
+            red[par][0][w] = mx;
+            red[par][1][w] = mn;
+        }
+        __syncthreads();
+        mx = red[par][0][0];
+        mn = red[par][1][0];
+#pragma unroll
+        for (int j = 1; j < NW; ++j) {
+            mx = fmax(mx, red[par][0][j]);
+            mn = fmin(mn, red[par][1][j]);
+        }
+        T s = T(0);
+        if (use_recip && isfinite(mx - mn)) {
+            // every difference x - max is finite: (x - max) / T directly
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                if (threadIdx.x + 256 * i < lenv) {
+#pragma unroll
+                    for (int c = 0; c < VN; ++c) {
+                        T &e = lane_of<V, T>(v[i], c);
+                        e = kexp(div_by(e - mx, temperature, recip));
+                        s += e;
+                    }
+                }
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                if (threadIdx.x + 256 * i < lenv) {
+#pragma unroll
+                    for (int c = 0; c < VN; ++c) {
+                        T &e = lane_of<V, T>(v[i], c);
+                        e = kexp(scaled_difference(e, mx, temperature));
+                        s += e;
+                    }
+                }
+            }
+        }
+        s = warp_sum(s);
+        __syncthreads();   // all maxima read before the sums reuse the slot
+        if (lane == 0) red[par][0][w] = s;
+        __syncthreads();
+        s = T(0);
+#pragma unroll
+        for (int j = 0; j < NW; ++j) s += red[par][0][j];
+        if (!isfinite(s) || mn == -INFINITY) {
+            // some element is inf or NaN: find the first one in axis order
+            int64_t bad = INT64_MAX;
+            for (int64_t j = threadIdx.x; j < g.len; j += blockDim.x)
+                if (!isfinite(src[sb + j]) && j < bad) bad = j;
+            bad = warp_min_i64(bad);
+            if (lane == 0) redi[w] = bad;
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                int64_t b = redi[0];
+                for (int j = 1; j < NW; ++j) b = redi[j] < b ? redi[j] : b;
+                atomicMin(first_bad, (unsigned long long)(row * g.len + b));
+            }
+            __syncthreads();
+            continue;
+        }
+        const T rs = T(1) / s;   // s >= 1: the maximum contributes exp(0)
+        V *ov = reinterpret_cast<V *>(out + ob);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int64_t q = threadIdx.x + 256 * i;
+            if (q < lenv) {
+                V r = v[i];
+#pragma unroll
+                for (int c = 0; c < VN; ++c) lane_of<V, T>(r, c) = div_by(lane_of<V, T>(r, c), s, rs);
+                ov[q] = r;
+            }
+        }
+    }
+}
+
 // Long rows: one block per row, three passes over global memory.
 template <typename T>
 __global__ void __launch_bounds__(256) softmax_rows_block(const T *__restrict__ src, T *__restrict__ out,
@@ -250,6 +409,25 @@ __global__ void __launch_bounds__(256) softmax_rows_block(const T *__restrict__ 
     }
 }
 
+// True when row r (C order over the outer dims) starts at r * (*rs): the outer
+// dims nest like one C-ordered axis.  Size-one dims are ignored.
+bool collapse_rows(const int64_t *dims, const int64_t *str, int n, int64_t *rs) {
+    int64_t prod = 1, base = 0;
+    bool have = false;
+    for (int d = n - 1; d >= 0; --d) {
+        if (dims[d] == 1) continue;
+        if (!have) {
+            base = str[d];
+            have = true;
+        } else if (str[d] != base * prod) {
+            return false;
+        }
+        prod *= dims[d];
+    }
+    *rs = base;
+    return true;
+}
+
 template <typename T>
 int softmax_impl(kx_handle *hh, const kx_tensor *src, int64_t axis, T temperature, const kx_tensor *out,
                  kx_error *err) {
@@ -307,6 +485,7 @@ int softmax_impl(kx_handle *hh, const kx_tensor *src, int64_t axis, T temperatur
         ++nd;
     }
     g.nouter = nd;
+    g.collapsed = collapse_rows(g.odims, g.sstr, nd, &g.rs_s) && collapse_rows(g.odims, g.ostr, nd, &g.rs_o);
     if (g.rows > (INT64_MAX / (g.len > 0 ? g.len : 1)))
         return set_err(err, KX_E_UNSUPPORTED, kOp, "too many elements");
 
@@ -321,17 +500,31 @@ int softmax_impl(kx_handle *hh, const kx_tensor *src, int64_t axis, T temperatur
         const int64_t blocks_cap = 16LL * h->sm_count;
         const int64_t wblocks = (g.rows + 7) / 8;
         const unsigned grid_w = (unsigned)(wblocks < blocks_cap ? wblocks : blocks_cap);
-        const bool contig = std::is_same<T, float>::value && g.s_axis == 1 && g.o_axis == 1 && g.len % 4 == 0 &&
-                            (reinterpret_cast<uintptr_t>(sp) % 16 == 0) && (reinterpret_cast<uintptr_t>(op) % 16 == 0);
+        const unsigned grid_r = (unsigned)(g.rows < blocks_cap ? g.rows : blocks_cap);
+        constexpr int VN = Vec16<T>::n;
+        const bool aligned16 = g.s_axis == 1 && g.o_axis == 1 && g.len % VN == 0 &&
+                               (reinterpret_cast<uintptr_t>(sp) % 16 == 0) &&
+                               (reinterpret_cast<uintptr_t>(op) % 16 == 0);
         bool rows_aligned = true;
-        for (int d = 0; d < nd; ++d) rows_aligned &= (g.sstr[d] % 4 == 0) && (g.ostr[d] % 4 == 0);
-        if (contig && rows_aligned && g.len <= 32 * 4 * 16) {
-            if constexpr (std::is_same<T, float>::value) {
-                if (g.len <= 32 * 4 * 4)
-                    softmax_rows_warp_vec<4><<<grid_w, 256, 0, h->stream>>>(sp, op, g, temperature, flag);
-                else
-                    softmax_rows_warp_vec<16><<<grid_w, 256, 0, h->stream>>>(sp, op, g, temperature, flag);
-            }
+        for (int d = 0; d < nd; ++d) rows_aligned &= (g.sstr[d] % VN == 0) && (g.ostr[d] % VN == 0);
+        const int64_t lenv = g.len / VN;
+        // (x - max) / T through the reciprocal when 1/T is a normal number
+        const T recip = T(1) / temperature;
+        const int use_recip = std::isnormal((double)recip) && std::isnormal((double)temperature) &&
+                              std::fabs((double)recip) < (double)std::numeric_limits<T>::max() / 4;
+        if (aligned16 && rows_aligned && lenv <= 256 * 8 && g.len > 32 * VN * 4) {
+            if (lenv <= 256)
+                softmax_rows_block_vec<T, 1><<<grid_r, 256, 0, h->stream>>>(sp, op, g, temperature, recip, use_recip, flag);
+            else if (lenv <= 512)
+                softmax_rows_block_vec<T, 2><<<grid_r, 256, 0, h->stream>>>(sp, op, g, temperature, recip, use_recip, flag);
+            else if (lenv <= 1024)
+                softmax_rows_block_vec<T, 4><<<grid_r, 256, 0, h->stream>>>(sp, op, g, temperature, recip, use_recip, flag);
+            else
+                softmax_rows_block_vec<T, 8><<<grid_r, 256, 0, h->stream>>>(sp, op, g, temperature, recip, use_recip, flag);
+            h->last_kernel = "softmax_rows_block_vec";
+        } else if (std::is_same<T, float>::value && aligned16 && rows_aligned && g.len <= 32 * 4 * 4) {
+            if constexpr (std::is_same<T, float>::value)
+                softmax_rows_warp_vec<4><<<grid_w, 256, 0, h->stream>>>(sp, op, g, temperature, flag);
             h->last_kernel = "softmax_rows_warp_vec";
         } else if (g.len <= 32 * 4) {
             softmax_rows_warp<T, 4><<<grid_w, 256, 0, h->stream>>>(sp, op, g, temperature, flag);
@@ -340,8 +533,7 @@ int softmax_impl(kx_handle *hh, const kx_tensor *src, int64_t axis, T temperatur
             softmax_rows_warp<T, 32><<<grid_w, 256, 0, h->stream>>>(sp, op, g, temperature, flag);
             h->last_kernel = "softmax_rows_warp";
         } else {
-            const unsigned grid_b = (unsigned)(g.rows < blocks_cap ? g.rows : blocks_cap);
-            softmax_rows_block<T><<<grid_b, 256, 0, h->stream>>>(sp, op, g, temperature, flag);
+            softmax_rows_block<T><<<grid_r, 256, 0, h->stream>>>(sp, op, g, temperature, flag);
             h->last_kernel = "softmax_rows_block";
         }
         ce = cudaGetLastError();

@@ -135,6 +135,15 @@ def softmax_tol(dtype, length):
     return (8 + 2 * math.log2(max(length, 2))) * eps
 
 
+def softmax_tol_cond(x, axis, t):
+    """softmax_tol plus the conditioning of exp: rounding the argument
+    d = (x - max) / T to the working precision perturbs exp(d) by |d| ulps,
+    for the reference as much as for any implementation."""
+    xl = x.astype(np.longdouble)
+    d = np.abs((xl - xl.max(axis=axis, keepdims=True)) / np.longdouble(t))
+    return softmax_tol(x.dtype, x.shape[axis]) + 2 * d.astype(np.float64) * np.finfo(x.dtype).eps
+
+
 @pytest.mark.parametrize("shape,axis", [((7, 11), -1), ((3, 5, 300), 2), ((4, 2048), -1), ((2, 3, 4, 5), 1),
                                         ((3, 5000), 1), ((6, 33), 0), ((1, 1), 0)])
 @pytest.mark.parametrize("dtype", [np.float32, np.float64])
@@ -149,6 +158,45 @@ def test_softmax_matches_oracle(kx, torch_cuda, shape, axis, dtype):
     # the oracle (sequential sum) obeys the sequential bound len * eps
     seq = (8 + shape[axis]) * np.finfo(dtype).eps
     assert (np.abs(exp - truth) <= seq * np.abs(truth) + np.finfo(dtype).tiny).all()
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_softmax_block_rows_paths(kx, torch_cuda, dtype):
+    """Long contiguous rows (one block per row): reciprocal path, the
+    divide-first fallback for overflowing differences, a huge temperature
+    (subnormal reciprocal), outer dims that do not nest, and +inf rows."""
+    from kernix_b200 import rng
+    torch = torch_cuda
+    x = rng.normal(31, 6 * 4 * 2048, 2.0, dtype).reshape(6, 4, 2048)
+    for t in (0.37, 11.3, 1e38 if dtype == np.float32 else 1e307):
+        got = kx.softmax_temperature(to_dev(x, torch), -1, t).cpu().numpy()
+        assert kx.handle(0).last_kernel == "softmax_rows_block_vec"
+        truth = softmax_truth(x, -1, t)
+        assert (np.abs(got - truth) <= softmax_tol_cond(x, -1, t) * np.abs(truth) + np.finfo(dtype).tiny).all()
+    # (x - max) overflows: the reference divides first, x/T - max/T
+    big = np.finfo(dtype).max * 0.75
+    y = np.zeros((3, 2048), dtype=dtype)
+    y[:, ::2] = big
+    y[:, 1::2] = -big
+    y[1, 7] = big * 0.5
+    got = kx.softmax_temperature(to_dev(y, torch), -1, big).cpu().numpy()
+    truth = softmax_truth(y, -1, big)   # no overflow in extended precision: same value as divide-first
+    assert (np.abs(got - truth) <= softmax_tol(dtype, 2048) * np.abs(truth) + np.finfo(dtype).tiny).all()
+    exp = oracle.softmax_temperature(y, -1, big)   # sequential sum: the looser len * eps bound
+    assert (np.abs(exp - truth) <= (8 + 2048) * np.finfo(dtype).eps * np.abs(truth)).all()
+    # outer dims that do not collapse into one row stride: (4, 6, 2048) view of a (6, 4, 2048) buffer
+    src = to_dev(x, torch).permute(1, 0, 2)
+    got = kx.softmax_temperature(src, 2, 0.8).cpu().numpy()
+    xt = np.transpose(x, (1, 0, 2))
+    truth = softmax_truth(xt, 2, 0.8)
+    assert (np.abs(got - truth) <= softmax_tol_cond(xt, 2, 0.8) * np.abs(truth) + np.finfo(dtype).tiny).all()
+    # +inf alone in a long row, then NaN before it in a later row: first index wins
+    z = np.zeros((5, 1536), dtype=dtype)
+    z[3, 1000] = np.inf
+    z[4, 2] = np.nan
+    with pytest.raises(kx.NonFiniteInput) as ge:
+        kx.softmax_temperature(to_dev(z, torch), -1, 1.0)
+    assert ge.value.indices == [3, 1000]
 
 
 def test_softmax_strided_input(kx, torch_cuda):
