@@ -152,12 +152,12 @@ def run_ours(args, rank, world, local):
     import torch.distributed as dist
     import kernix_b200 as kx
     from kernix_b200 import rng
-    from kernix_b200.sharded import plan_rows, sharded_matmul
+    from kernix_b200.sharded import PeerOutput, plan_rows, sharded_matmul, sharded_matmul_push
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     h = kx.handle(local)
-    plan = plan_rows(M, world, target_piece=args.piece if world > 1 else M)
+    plan = plan_rows(M, world, target_piece=(args.piece or 512) if world > 1 else M)
     my_rows = plan.local_rows(rank)
     # Host inputs (pinned): this rank's rows of the A buffer, and B.
     a_host = torch.empty(len(my_rows) * ROW_STRIDE, dtype=torch.float32, pin_memory=True)
@@ -166,18 +166,29 @@ def run_ours(args, rank, world, local):
     rng.uniform(SEEDS["c5"][1], K * N, -1.0, 1.0, np.float32, out=b_host.numpy())
     a_buf = a_host.to(dev)
     b = b_host.to(dev).view(K, N)
-    c = torch.empty(M, N, dtype=torch.float32, device=dev)
+    group = dist.group.WORLD if world > 1 else None
+    push = world > 1 and args.gather == "p2p"
+    peer_out = PeerOutput(M, N, torch.float32, group, local) if push else None
+    c = peer_out.tensor if push else torch.empty(M, N, dtype=torch.float32, device=dev)
     # piece i of this rank: rows [i*piece, (i+1)*piece) of the local buffer,
     # viewed with the 8704 row stride (first 8192 columns)
     pieces = [kx.TensorView(a_buf, (plan.piece, K), (ROW_STRIDE, 1), i * plan.piece * ROW_STRIDE)
               for i in range(plan.pieces)]
     scratch = [torch.empty(plan.piece, N, dtype=torch.float32, device=dev) for _ in range(plan.pieces)] \
-        if world > 1 else None
-    streams = (torch.cuda.current_stream(dev), torch.cuda.Stream(dev)) if world > 1 else None
-    group = dist.group.WORLD if world > 1 else None
+        if world > 1 and not push else None
+    streams = (torch.cuda.current_stream(dev), torch.cuda.Stream(dev)) if world > 1 and not push else None
+    push_streams = None
+    if push:
+        push_streams = {r: torch.cuda.Stream(dev) for r in range(world) if r != rank}
+        push_streams["comm"] = torch.cuda.Stream(dev)
 
     def step():
-        sharded_matmul(pieces, b, c, plan, rank, group, streams=streams, scratch=scratch)
+        if push:
+            sharded_matmul_push(pieces, b, peer_out, plan, rank, group, streams=push_streams)
+        else:
+            sharded_matmul(pieces, b, c, plan, rank, group, streams=streams, scratch=scratch)
+
+    step.a_dev, step.b_dev = a_buf, b
 
     def barrier():
         if world > 1:
@@ -211,9 +222,17 @@ def run_ours(args, rank, world, local):
     value = flops * args.steps / elapsed / 1e12
 
     # end-to-end through the public API with host buffers
-    e2e = None if args.no_e2e else e2e_run(args, rank, world, local, a_host, b_host, plan, kx, dist, group)
-    # correctness spot check of the timed output: a checksum of rows
+    e2e = None if args.no_e2e else e2e_run(args, rank, world, local, a_host, b_host, plan, kx, dist, group,
+                                           step_fn=step, c=c)
+    # correctness of the timed output: rows against the compensated oracle on
+    # rank 0, and (N > 1) every gathered row equal to what its owner computed
     check = spot_check(c, a_host, b_host, plan, rank) if rank == 0 else None
+    gathered = gather_check(c, plan, rank, world, group) if world > 1 else None
+    if rank == 0 and gathered is not None:
+        check["gathered_rows_equal_owner"] = gathered
+        check["pass"] = check["pass"] and gathered
+    if peer_out is not None:
+        peer_out.close()
 
     result = None
     if rank == 0:
@@ -233,7 +252,9 @@ def run_ours(args, rank, world, local):
             "warmup": args.warmup, "ms_per_step": round(elapsed * 1e3 / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (SplitMix64 seeds 5, 6)",
             "config": {"workload": "c5: " + CONFIG_TEXT["c5"], "M": M, "N": N, "K": K, "a_row_stride": ROW_STRIDE,
-                       "parallelism": f"rows{world} block-cyclic piece={plan.piece} + all-gather",
+                       "parallelism": f"rows{world} block-cyclic piece={plan.piece}" + (
+                           "" if world == 1 else (" + copy-engine push to peers (CUDA IPC)" if push
+                                                  else " + NCCL all-gather")),
                        "l2": "inputs larger than L2 (A span 285 MB, B 268 MB)", "kernel": kname},
             "e2e": e2e,
             "gpu_launches": launches,
@@ -268,15 +289,15 @@ def time_dominant_kernel(h, pieces, b, c, plan, dev, reps=5):
     return s.elapsed_time(e) / reps
 
 
-def e2e_run(args, rank, world, local, a_host, b_host, plan, kx, dist, group):
+def e2e_run(args, rank, world, local, a_host, b_host, plan, kx, dist, group, step_fn=None, c=None):
     """Same metric measured through the public API from pinned host buffers.
 
     N=1: ``try_strided_matmul`` -- the reference-facing MatmulElement hook --
     on the host A view (row stride 8704) and B, result read back to host.
     N>1: host->device copy of this rank's A rows and B, the sharded matmul with
-    its all-gather, and rank 0 reads C back."""
+    its gather (``step_fn`` on the device buffers it was built on), and rank 0
+    reads C back."""
     import torch
-    from kernix_b200.sharded import sharded_matmul
     dev = torch.device("cuda", local)
     steps = max(1, min(args.steps, 5))
     if world == 1:
@@ -293,17 +314,13 @@ def e2e_run(args, rank, world, local, a_host, b_host, plan, kx, dist, group):
         h2d = ((M - 1) * ROW_STRIDE + K) * 4 + K * N * 4
         d2h = M * N * 4
     else:
-        a_dev = torch.empty_like(a_host, device=dev)
-        b_dev = torch.empty(K, N, dtype=torch.float32, device=dev)
-        c = torch.empty(M, N, dtype=torch.float32, device=dev)
+        a_dev, b_dev = step_fn.a_dev, step_fn.b_dev
         c_host = torch.empty(M, N, dtype=torch.float32, pin_memory=True) if rank == 0 else None
-        pieces = [kx.TensorView(a_dev, (plan.piece, K), (ROW_STRIDE, 1), i * plan.piece * ROW_STRIDE)
-                  for i in range(plan.pieces)]
 
         def one():
             a_dev.copy_(a_host, non_blocking=True)
             b_dev.view(-1).copy_(b_host, non_blocking=True)
-            sharded_matmul(pieces, b_dev, c, plan, rank, group)
+            step_fn()
             if rank == 0:
                 c_host.copy_(c, non_blocking=True)
             torch.cuda.synchronize(dev)
@@ -321,7 +338,25 @@ def e2e_run(args, rank, world, local, a_host, b_host, plan, kx, dist, group):
         d2h = M * N * 4
     return {"value": round(2.0 * M * N * K / dt / 1e12, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h), "ms_per_step": round(dt * 1e3, 3), "steps": steps,
-            "api": "try_strided_matmul (C-ABI hook)" if world == 1 else "sharded_matmul + torch H2D/D2H"}
+            "api": "try_strided_matmul (C-ABI hook)" if world == 1 else "sharded matmul + gather, torch H2D/D2H"}
+
+
+def gather_check(c, plan, rank, world, group):
+    """Every rank's rows, as rank 0 holds them after the gather, must equal
+    (bit for bit: the gather copies bytes) what the owning rank computed:
+    compared through per-row float64 sums, all-gathered from the owners."""
+    import torch
+    import torch.distributed as dist
+    mine = torch.cat([c[s:e] for s, e in (plan.rows_of(rank, i) for i in range(plan.pieces))]).double().sum(dim=1)
+    every = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(every, mine, group=group)
+    if rank != 0:
+        return None
+    ok = True
+    for r in range(world):
+        held = torch.cat([c[s:e] for s, e in (plan.rows_of(r, i) for i in range(plan.pieces))]).double().sum(dim=1)
+        ok = ok and bool(torch.equal(held, every[r]))
+    return ok
 
 
 def spot_check(c, a_host, b_host, plan, rank):
@@ -434,7 +469,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--piece", type=int, default=1024, help="rows per sharded piece")
+    ap.add_argument("--piece", type=int, default=0, help="rows per sharded piece (0: 512 when sharded)")
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
+                    help="gathered output: copy-engine pushes into peers' C, or NCCL all-gather")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")

@@ -225,6 +225,26 @@ int kx_matrix_validate(const kx_matrix *m, uint32_t elem_bytes, kx_error *err);
 int kx_matmul_splitk_f32_static(const kx_tensor *a, const kx_tensor *b, const kx_tensor *out, void *stream,
                                 kx_error *err);
 
+/* ---- gathered output across the GPUs of one node ------------------------ */
+/* No counterpart in the reference: CpuExecutor::matmul_into
+ * (execution.rs:188-233) splits output rows over threads that share one
+ * buffer.  Across GPUs each process owns its device, so a row-sharded GEMM
+ * gathers its output by pushing each rank's rows into every peer's copy of C:
+ * the buffer is exported once (kx_ipc_export), mapped by the other processes
+ * (kx_ipc_import), and rows are pushed with kx_copy_async, which runs on the
+ * copy engines over NVLink and takes no SMs from the GEMMs that overlap it.
+ * `device_ptr` for export must be a pointer returned by kx_alloc (the start of
+ * a cudaMalloc allocation).  Imported pointers are valid in this process only
+ * and are released with kx_ipc_close. */
+#define KX_IPC_HANDLE_BYTES 64
+int kx_ipc_export(kx_handle *h, void *device_ptr, unsigned char *handle_out, kx_error *err);
+int kx_ipc_import(kx_handle *h, const unsigned char *handle, void **device_ptr, kx_error *err);
+int kx_ipc_close(kx_handle *h, void *device_ptr);
+/* Enqueue a device-to-device copy of `bytes` on `stream` (a cudaStream_t of the
+ * handle's device; null = the handle's stream).  Either side may be an
+ * imported peer pointer.  Returns once the copy is enqueued. */
+int kx_copy_async(kx_handle *h, void *dst, const void *src, uint64_t bytes, void *stream, kx_error *err);
+
 /* ---- introspection ------------------------------------------------------ */
 /* Number of kernel launches this handle has issued since creation. */
 uint64_t kx_launch_count(const kx_handle *h);

@@ -11,20 +11,6 @@ using namespace kx;
 
 namespace {
 
-// Make the handle's device current for the duration of a call and restore the
-// caller's device afterwards.
-struct DeviceGuard {
-    int prev = -1;
-    bool ok = true;
-    explicit DeviceGuard(int dev) {
-        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
-    }
-    ~DeviceGuard() {
-        int cur = -1;
-        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
-    }
-};
 
 template <typename T> constexpr uint32_t ES = (uint32_t)sizeof(T);
 

@@ -6,14 +6,14 @@
 // ~1.7e-6 |a b| (see tf32_trunc below), inside the f32 bound the reference's
 // tests use, |x - y| <= 2e-6 sum|a b| (small_matmul_tests.rs:153-186).
 //
-// Pipeline per CTA (one 128 x 256 output tile, 384 threads):
+// Pipeline per CTA (one 128 x BN output tile, BN = 256 or 224, 384 threads):
 //   warp 0       TMA producer: raw f32 tiles of A and B into stage s (k depth 16)
 //   warp 1       TMEM owner and MMA issuer: 3 x 2 tcgen05.mma (kind::tf32) per stage
 //   warps 4..11  workers: write lo beside each raw tile (the raw tile is hi);
 //                every 64 k-tiles fold the hi*hi accumulator into f32
 //                registers (128 columns of one row per thread); at the end add
 //                the cross-term accumulator and store C
-// Stages: 4 x (A hi 8 KB, A lo 8 KB, B hi 16 KB, B lo 16 KB) = 192 KB.
+// Stages: 4 x (A hi 8 KB, A lo 8 KB, B hi 16 KB, B lo 16 KB) = 192 KB at BN = 256.
 // The tensor core's f32 accumulation truncates, so the large hi*hi sum is
 // restarted every 1024 k and summed with round-to-nearest adds on the CUDA
 // cores; the small cross terms keep one TMEM accumulator over all of K.
@@ -37,19 +37,27 @@
 namespace kx {
 namespace tc {
 
-constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4;
+constexpr int BM = 128, BK = 16, STAGES = 4;
 constexpr int A_TILE = BM * BK * 4;                   // 8 KB
-constexpr int B_TILE = BN * BK * 4;                   // 16 KB
-constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 48 KB
 constexpr int BAR_BYTES = 256;   // 3 x STAGES + 2 mbarriers and the TMEM address
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
 constexpr int NTHREADS = 384;                        // 12 warps
 constexpr int WORK_WARP0 = 4, WORK_WARPS = 8, WORK_THREADS = WORK_WARPS * 32;
-constexpr int HALF_COLS = BN / 2;                     // accumulator columns per worker thread
 constexpr int KC = 64;                                // k-tiles (1024 k) per hi*hi chunk
-constexpr int CONV_CHUNKS = (A_TILE + B_TILE) / 16;   // 1536 chunks = 6 per worker thread
-static_assert(CONV_CHUNKS % WORK_THREADS == 0, "converter work must divide evenly");
 constexpr uint32_t TMEM_COLS = 512;   // main (hi*hi) + cross (hi*lo + lo*hi) accumulators
+constexpr uint32_t XCOL = 256;        // first TMEM column of the cross-term accumulator
+
+// Tile width N: 256, or 224 when it packs the tiles into fewer full waves of
+// SMs (e.g. 512 x 8192 outputs: 148 tiles of 128 x 224 = one wave, against
+// 128 tiles of 128 x 256 leaving 20 SMs idle).
+template <int BN> struct TileN {
+    static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "tile width");
+    static constexpr int B_TILE = BN * BK * 4;                   // 16 KB at 256
+    static constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 48 KB at 256
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    static constexpr int HALF_COLS = BN / 2;                     // accumulator columns per worker thread
+    static constexpr int CONV_CHUNKS = (A_TILE + B_TILE) / 16;   // 16-byte chunks per stage
+    static constexpr int CONV_ITERS = (CONV_CHUNKS + WORK_THREADS - 1) / WORK_THREADS;
+};
 constexpr uint64_t WAIT_NS = 2000000000ull;           // 2 s per wait
 constexpr uint32_t KX_TIMEOUT_FLAG = 1u;
 
@@ -132,7 +140,8 @@ __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo_b
     return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16) |
            ((uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46) | ((uint64_t)1 << 61);
 }
-// Instruction descriptor: f32 accumulate, tf32 A and B, M = 128, N = 256.
+// Instruction descriptor: f32 accumulate, tf32 A and B, M = 128, N = BN.
+template <int BN>
 __host__ __device__ constexpr uint32_t idesc_tf32(bool b_mn_major) {
     return (1u << 4) | (2u << 7) | (2u << 10) | (0u << 15) | ((b_mn_major ? 1u : 0u) << 16) |
            ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
@@ -186,12 +195,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Add this thread's half row (128 columns starting at col0) of the TMEM
-// accumulator at `tcol` into the register running sum.
-__device__ __forceinline__ void tmem_accumulate(uint32_t tmem, int quarter, int col0, float (&sum)[HALF_COLS]) {
+// Add this thread's half row (HALF columns starting at col0) of the hi*hi
+// TMEM accumulator into the register running sum.
+template <int HALF>
+__device__ __forceinline__ void tmem_accumulate(uint32_t tmem, int quarter, int col0, float (&sum)[HALF]) {
+    static_assert(HALF % 16 == 0, "16-column groups");
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col0;
 #pragma unroll
-    for (int c = 0; c < HALF_COLS / 32; ++c) {
+    for (int c = 0; c < HALF / 32; ++c) {
         uint32_t r0[16], r1[16];   // two loads in flight per wait
         tmem_ld16(lane_base + (uint32_t)(c * 32), r0);
         tmem_ld16(lane_base + (uint32_t)(c * 32 + 16), r1);
@@ -202,12 +213,22 @@ __device__ __forceinline__ void tmem_accumulate(uint32_t tmem, int quarter, int 
             sum[c * 32 + 16 + j] += __uint_as_float(r1[j]);
         }
     }
+    if constexpr (HALF % 32 != 0) {
+        constexpr int c0 = HALF / 32 * 32;
+        uint32_t r0[16];
+        tmem_ld16(lane_base + (uint32_t)c0, r0);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sum[c0 + j] += __uint_as_float(r0[j]);
+    }
 }
 
-template <bool B_MN>
+template <bool B_MN, int BN>
 __global__ void __launch_bounds__(NTHREADS, 1)
 gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ TcParams p) {
+    using TN = TileN<BN>;
+    constexpr int B_TILE = TN::B_TILE, STAGE_BYTES = TN::STAGE_BYTES, HALF_COLS = TN::HALF_COLS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
@@ -288,11 +309,11 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         }
     } else if (warp == 1) {
         // ---- MMA issuer ------------------------------------------------
-        // hi*hi accumulates per chunk of KC k-tiles in columns [0, 256) (the
+        // hi*hi accumulates per chunk of KC k-tiles in columns [0, BN) (the
         // workers fold each chunk into f32 registers); the two cross terms,
-        // 2^-11 smaller, accumulate over all of K in [256, 512).
+        // 2^-11 smaller, accumulate over all of K in [256, 256 + BN).
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_tf32(B_MN);
+            constexpr uint32_t idesc = idesc_tf32<BN>(B_MN);
             for (int kt = 0; kt < ktiles; ++kt) {
                 const int s = kt % STAGES;
                 const int chunk = kt / KC, kin = kt % KC;
@@ -319,8 +340,8 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                         dbl = desc_k_sw64(b_lo + ks * 32);
                     }
                     mma_tf32(tmem, dah, dbh, idesc, (kin > 0 || ks > 0) ? 1u : 0u);
-                    mma_tf32(tmem + BN, dah, dbl, idesc, (kt > 0 || ks > 0) ? 1u : 0u);
-                    mma_tf32(tmem + BN, dal, dbh, idesc, 1u);
+                    mma_tf32(tmem + XCOL, dah, dbl, idesc, (kt > 0 || ks > 0) ? 1u : 0u);
+                    mma_tf32(tmem + XCOL, dal, dbh, idesc, 1u);
                 }
                 mma_commit(&empty[s]);
                 if (kin == KC - 1 || kt == ktiles - 1) mma_commit(chunk_full);   // chunk done (and all before it)
@@ -342,14 +363,15 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 s_fail = 1;
                 break;
             }
-            // The A and B tiles of the stage are 1536 16-byte chunks (A hi: 512
-            // at offset 0, B hi: 1024 at 16 KB); each of the 256 worker threads
-            // splits 6 of them, lo going to the buffer beside its hi.
+            // The A and B tiles of the stage are CONV_CHUNKS 16-byte chunks
+            // (A hi: 512 at offset 0, B hi: BN * 4 at 16 KB); the 256 worker
+            // threads split them, lo going to the buffer beside its hi.
             uint32_t bad = 0;
             uint8_t *base = stage_a(s);
 #pragma unroll
-            for (int j = 0; j < CONV_CHUNKS / WORK_THREADS; ++j) {
+            for (int j = 0; j < TN::CONV_ITERS; ++j) {
                 const int c = wt + j * WORK_THREADS;
+                if (TN::CONV_CHUNKS % WORK_THREADS != 0 && c >= TN::CONV_CHUNKS) break;
                 const bool in_a = c < A_TILE / 16;
                 float4 *hp = reinterpret_cast<float4 *>(base + (in_a ? c * 16 : 2 * A_TILE + (c - A_TILE / 16) * 16));
                 float4 *lp = reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(hp) + (in_a ? A_TILE : B_TILE));
@@ -410,7 +432,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 #pragma unroll
                 for (int c = 0; c < HALF_COLS / 16; ++c) {
                     uint32_t r[16];
-                    tmem_ld16(tmem + BN + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(col0 + c * 16), r);
+                    tmem_ld16(tmem + XCOL + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(col0 + c * 16), r);
                     tmem_wait_ld();
                     if (!in_rows) continue;
                     float v[16];
@@ -493,6 +515,35 @@ bool tc_eligible(const GemmParams<float> &p) {
     return true;
 }
 
+namespace {
+
+// Tile width with the least modelled time: waves of `sm_count` CTAs times a
+// per-tile cost of (BN + 32) (the MMA work, plus per-tile fixed costs: the
+// pipeline fill and the epilogue).
+int pick_bn(int64_t m, int64_t n, int64_t nbatch, int sm_count) {
+    const int64_t tm = (m + tc::BM - 1) / tc::BM;
+    auto cost = [&](int bn) {
+        const int64_t tiles = tm * ((n + bn - 1) / bn) * nbatch;
+        return ((tiles + sm_count - 1) / sm_count) * (int64_t)(bn + 32);
+    };
+    return cost(224) < cost(256) ? 224 : 256;
+}
+
+template <bool B_MN, int BN>
+cudaError_t launch_tc(Handle *h, const CUtensorMap &ma, const CUtensorMap &mb, const tc::TcParams &tp, int nb) {
+    using namespace tc;
+    constexpr int smem = TileN<BN>::SMEM_BYTES;
+    const int64_t tiles = (int64_t)((tp.M + BM - 1) / BM) * ((tp.N + BN - 1) / BN);
+    dim3 grid((unsigned)tiles, (unsigned)nb, 1);
+    auto k = gemm_3xtf32_kernel<B_MN, BN>;
+    cudaError_t ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (ce != cudaSuccess) return ce;
+    k<<<grid, NTHREADS, smem, h->stream>>>(ma, mb, tp);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
 int run_gemm_tc(Handle *h, const GemmParams<float> &p, const char **kernel_name) {
     using namespace tc;
     const bool b_mn = p.b_cs == 1 && (p.b_rs * 4) % 16 == 0 && p.b_rs > 0;
@@ -503,6 +554,7 @@ int run_gemm_tc(Handle *h, const GemmParams<float> &p, const char **kernel_name)
     const int a_batched = (nb > 1 && a_bs > 0) ? 1 : 0;
     const int b_batched = (nb > 1 && b_bs > 0) ? 1 : 0;
     const int64_t a_rs = p.M == 1 ? 16 : p.a_rs;   // a single row: any aligned stride
+    const int bn = pick_bn(p.M, p.N, nb, h->sm_count);
     CUtensorMap ma, mb;
     const uint64_t a_s2 = a_batched ? (uint64_t)a_bs * 4 : (uint64_t)((a_rs * 4 * (int64_t)p.M + 15) / 16 * 16);
     if (!make_map(&ma, p.A, (uint64_t)p.K, (uint64_t)p.M, a_batched ? (uint64_t)nb : 1, (uint64_t)a_rs * 4, a_s2, BK,
@@ -516,7 +568,7 @@ int run_gemm_tc(Handle *h, const GemmParams<float> &p, const char **kernel_name)
     } else {
         const uint64_t s2 = b_batched ? (uint64_t)b_bs * 4 : (uint64_t)((p.b_cs * 4 * (int64_t)p.N + 15) / 16 * 16);
         okb = make_map(&mb, p.B, (uint64_t)p.K, (uint64_t)p.N, b_batched ? (uint64_t)nb : 1, (uint64_t)p.b_cs * 4, s2,
-                       BK, BN, CU_TENSOR_MAP_SWIZZLE_64B);
+                       BK, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_64B);
     }
     if (!okb) return KX_DECLINED;
     TcParams tp;
@@ -537,25 +589,13 @@ int run_gemm_tc(Handle *h, const GemmParams<float> &p, const char **kernel_name)
     tp.a_batched = a_batched;
     tp.b_batched = b_batched;
     tp.status = h->flags + kStatusWord;
-    const int64_t tiles = (int64_t)((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
-    dim3 grid((unsigned)tiles, (unsigned)nb, 1);
     cudaError_t ce;
     if (b_mn) {
-        auto k = gemm_3xtf32_kernel<true>;
-        ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-        if (ce == cudaSuccess) {
-            k<<<grid, NTHREADS, SMEM_BYTES, h->stream>>>(ma, mb, tp);
-            ce = cudaGetLastError();
-        }
-        *kernel_name = "tc_3xtf32_128x256_bmn";
+        ce = bn == 224 ? launch_tc<true, 224>(h, ma, mb, tp, nb) : launch_tc<true, 256>(h, ma, mb, tp, nb);
+        *kernel_name = bn == 224 ? "tc_3xtf32_128x224_bmn" : "tc_3xtf32_128x256_bmn";
     } else {
-        auto k = gemm_3xtf32_kernel<false>;
-        ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-        if (ce == cudaSuccess) {
-            k<<<grid, NTHREADS, SMEM_BYTES, h->stream>>>(ma, mb, tp);
-            ce = cudaGetLastError();
-        }
-        *kernel_name = "tc_3xtf32_128x256_bk";
+        ce = bn == 224 ? launch_tc<false, 224>(h, ma, mb, tp, nb) : launch_tc<false, 256>(h, ma, mb, tp, nb);
+        *kernel_name = bn == 224 ? "tc_3xtf32_128x224_bk" : "tc_3xtf32_128x256_bk";
     }
     ++h->launches;
     return ce == cudaSuccess ? KX_OK : h->cuda_fail(ce);

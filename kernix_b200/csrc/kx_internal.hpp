@@ -60,6 +60,21 @@ struct Handle {
     }
 };
 
+// Make the handle's device current for the duration of a call and restore the
+// caller's device afterwards.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
 // Error record for a failed CUDA call.
 inline int cuda_err(kx_error *e, Handle *h, const char *op) {
     set_err(e, KX_E_CUDA, op, cudaGetErrorString((cudaError_t)h->last_cuda_error));

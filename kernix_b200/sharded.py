@@ -9,6 +9,18 @@ of every rank is all-gathered straight into rows
 layout is already C's row order.  The all-gather of piece ``i`` runs on a
 communication stream while piece ``i + 1`` is being multiplied.
 
+Two ways to gather on GPUs:
+
+* ``PeerOutput`` + ``sharded_matmul_push`` (the default for CUDA): C lives in
+  library-allocated memory that every rank maps into every other rank (CUDA
+  IPC over NVLink).  After each piece's GEMM a rank pushes that piece's rows
+  straight into the same rows of every peer's C with the copy engines, one
+  stream per peer, so the exchange overlaps the next piece's GEMM without
+  taking any of its SMs; one 4-byte NCCL all-reduce at the end of the step
+  tells every rank that all pushes into its C have landed.
+* ``sharded_matmul`` with ``all_gather_into_tensor`` per piece (NCCL; also the
+  gloo path the CPU tests use).
+
 This is the multi-worker counterpart of ``CpuExecutor::matmul_into``'s row
 chunking (crates/kernix-ops/src/execution.rs:188-233), lifted from threads in
 one process to GPUs in one node.
@@ -106,3 +118,128 @@ def sharded_matmul(a_pieces, b, c, plan: RowPlan, rank: int, group=None,
             matmul_into(a_pieces[i], b, scratch[i])
             g0, g1 = plan.gathered_rows(i)
             dist.all_gather_into_tensor(c[g0:g1], scratch[i], group=group)
+
+
+class _CudaArray:
+    """``__cuda_array_interface__`` view of library-owned device memory."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...], typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerOutput:
+    """An M x N output allocated by the library on every rank of ``group``
+    and mapped into every other rank, so that each rank can write its rows
+    into all copies (``kx_ipc_export`` / ``kx_ipc_import``)."""
+
+    def __init__(self, m: int, n: int, dtype, group, device: int):
+        import ctypes as C
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _abi, handle
+        self.h = handle(device)
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.dtype = dtype
+        esize = torch.empty((), dtype=dtype).element_size()
+        self.row_bytes = n * esize
+        self.nbytes = m * n * esize
+        lib = _abi.lib
+        ptr = C.c_void_p()
+        err = _abi.KxError()
+        _abi.raise_for(lib.kx_alloc(self.h.ptr, self.nbytes, C.byref(ptr), C.byref(err)), err)
+        self.ptr = int(ptr.value)
+        typestr = {torch.float32: "<f4", torch.float64: "<f8"}[dtype]
+        self._owner = _CudaArray(self.ptr, (m, n), typestr)
+        self.tensor = torch.as_tensor(self._owner, device=f"cuda:{device}")
+        hbuf = C.create_string_buffer(_abi.KX_IPC_HANDLE_BYTES)
+        _abi.raise_for(lib.kx_ipc_export(self.h.ptr, C.c_void_p(self.ptr), hbuf, C.byref(err)), err)
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, bytes(hbuf.raw), group=group)
+        self.peers: list[int] = []
+        for r, hd in enumerate(handles):
+            if r == self.rank:
+                self.peers.append(self.ptr)
+                continue
+            pp = C.c_void_p()
+            _abi.raise_for(lib.kx_ipc_import(self.h.ptr, hd, C.byref(pp), C.byref(err)), err)
+            self.peers.append(int(pp.value))
+        self.done = torch.zeros(1, dtype=torch.int32, device=f"cuda:{device}")
+
+    def push_rows(self, r0: int, r1: int, streams: dict) -> None:
+        """Enqueue copies of rows [r0, r1) of this rank's C into the same rows
+        of every peer's C, one copy per peer on ``streams[peer]``."""
+        import ctypes as C
+
+        from . import _abi
+        off, nbytes = r0 * self.row_bytes, (r1 - r0) * self.row_bytes
+        err = _abi.KxError()
+        for r, dst in enumerate(self.peers):
+            if r == self.rank:
+                continue
+            rc = _abi.lib.kx_copy_async(self.h.ptr, C.c_void_p(dst + off), C.c_void_p(self.ptr + off), nbytes,
+                                        C.c_void_p(streams[r].cuda_stream), C.byref(err))
+            _abi.raise_for(rc, err)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (collective: every
+        rank calls it, after its last push has completed)."""
+        import ctypes as C
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _abi
+        if not self.peers:
+            return
+        torch.cuda.synchronize(self.h.device)
+        dist.barrier(group=self.group)
+        for r, p in enumerate(self.peers):
+            if r != self.rank:
+                _abi.lib.kx_ipc_close(self.h.ptr, C.c_void_p(p))
+        dist.barrier(group=self.group)
+        self.tensor = None
+        _abi.lib.kx_free(self.h.ptr, C.c_void_p(self.ptr))
+        self.peers = []
+
+
+def sharded_matmul_push(a_pieces, b, out: PeerOutput, plan: RowPlan, rank: int, group=None,
+                        matmul_into: Callable | None = None, streams: dict | None = None) -> None:
+    """Compute this rank's pieces into ``out.tensor`` and push each piece into
+    every peer's copy as soon as its GEMM has finished.
+
+    ``streams`` maps each peer rank to a CUDA stream for its pushes and key
+    ``"comm"`` to the stream of the closing all-reduce.  On return the work is
+    enqueued on the current stream: once it completes, every rank's C holds
+    the full product.
+    """
+    import torch
+    import torch.distributed as dist
+
+    if matmul_into is None:
+        from . import matmul_into as _mi
+        matmul_into = _mi
+    c = out.tensor
+    compute = torch.cuda.current_stream(c.device)
+    if streams is None:
+        streams = {r: torch.cuda.Stream(c.device) for r in range(plan.world) if r != rank}
+        streams["comm"] = torch.cuda.Stream(c.device)
+    peers = [r for r in range(plan.world) if r != rank]
+    for i in range(plan.pieces):
+        s, e = plan.rows_of(rank, i)
+        matmul_into(a_pieces[i], b, c[s:e])
+        ev = torch.cuda.Event()
+        ev.record(compute)
+        for r in peers:
+            streams[r].wait_event(ev)
+        out.push_rows(s, e, streams)
+    comm = streams["comm"]
+    for r in peers:
+        comm.wait_stream(streams[r])
+    with torch.cuda.stream(comm):
+        dist.all_reduce(out.done, group=group)
+    compute.wait_stream(comm)

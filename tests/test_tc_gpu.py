@@ -54,6 +54,27 @@ def test_tc_2d_layouts(kx, torch_cuda, tc_handle, m, k, n, b_layout):
     _check(got, va, vb)
 
 
+@pytest.mark.parametrize("m,k,n", [(512, 96, 8192), (520, 1040, 1000)])
+@pytest.mark.parametrize("b_layout", ["row", "col"])
+def test_tc_224_wide_tiles(kx, torch_cuda, tc_handle, m, k, n, b_layout):
+    """Shapes whose tile count packs into whole waves with 128 x 224 tiles
+    (ragged last column tile included) against the compensated oracle."""
+    rng = np.random.default_rng(m + n + k)
+    abuf = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    if b_layout == "row":
+        bbuf = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+        vb = oracle.View(bbuf, (k, n), (n, 1))
+    else:
+        bbuf = rng.uniform(-1, 1, (n, k)).astype(np.float32)
+        vb = oracle.View(bbuf, (k, n), (1, k))
+    got = kx.matmul(_view(kx, torch_cuda, abuf, (m, k), (k, 1)),
+                    _view(kx, torch_cuda, bbuf, vb.dims, vb.strides)).cpu().numpy()
+    assert "128x224" in tc_handle.last_kernel, tc_handle.last_kernel
+    tc_handle.synchronize()
+    rows = np.r_[0:3, m // 2, m - 2:m]
+    _check(got[rows], oracle.View(abuf[rows].copy(), (len(rows), k), (k, 1)), vb)
+
+
 def test_tc_batched_and_broadcast(kx, torch_cuda, tc_handle):
     torch = torch_cuda
     rng = np.random.default_rng(5)
@@ -69,20 +90,22 @@ def test_tc_batched_and_broadcast(kx, torch_cuda, tc_handle):
     q = rng.uniform(-1, 1, (2, 4, 256, 128)).astype(np.float32)
     kk = rng.uniform(-1, 1, (2, 4, 256, 128)).astype(np.float32)
     s = kx.matmul(torch.from_numpy(q).cuda(), torch.from_numpy(kk).cuda().transpose(2, 3)).cpu().numpy()
-    assert tc_handle.last_kernel == "tc_3xtf32_128x256_bk"
+    assert tc_handle.last_kernel.startswith("tc_3xtf32_128x") and tc_handle.last_kernel.endswith("_bk")
     for i, j in [(0, 0), (1, 3)]:
         _check(s[i, j], oracle.View.of(q[i, j]), oracle.View(kk[i, j], (128, 256), (1, 128)))
     tc_handle.synchronize()
 
 
-def test_tc_nonfinite_keeps_ieee_propagation(kx, torch_cuda, tc_handle):
+@pytest.mark.parametrize("m,n,width", [(128, 256, "128x224"), (4096, 8192, "128x256")])
+def test_tc_nonfinite_keeps_ieee_propagation(kx, torch_cuda, tc_handle, m, n, width):
     """An inf in A must give inf (not NaN from inf * 0 in a cross term)."""
     torch = torch_cuda
-    a = np.full((128, 64), 0.5, dtype=np.float32)
-    b = np.ones((64, 256), dtype=np.float32)
+    a = np.full((m, 64), 0.5, dtype=np.float32)
+    b = np.ones((64, n), dtype=np.float32)
     a[3, 7] = np.inf
     a[5, 2] = np.nan
     got = kx.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()).cpu().numpy()
+    assert width in tc_handle.last_kernel, tc_handle.last_kernel
     tc_handle.set_f32_variant(1)
     ref = kx.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()).cpu().numpy()
     assert np.array_equal(np.isnan(got), np.isnan(ref))
