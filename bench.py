@@ -152,12 +152,25 @@ def run_ours(args, rank, world, local):
     import torch.distributed as dist
     import kernix_b200 as kx
     from kernix_b200 import rng
-    from kernix_b200.sharded import PeerOutput, plan_rows, sharded_matmul, sharded_matmul_push
+    from kernix_b200.sharded import (PeerOutput, ReplicatedOutput, plan_rows, sharded_matmul, sharded_matmul_push,
+                                     sharded_matmul_replicated)
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     h = kx.handle(local)
-    plan = plan_rows(M, world, target_piece=(args.piece or 512) if world > 1 else M)
+    group = dist.group.WORLD if world > 1 else None
+    gather = args.gather if world > 1 else "none"
+    rep = None
+    if gather == "nvls":
+        # NVLink multicast when the node has it: one launch per rank, the
+        # epilogue's stores reach every rank's C
+        rep = ReplicatedOutput(M, N, torch.float32, group, local)
+        if not rep.available:
+            raise RuntimeError("no NVLink multicast (NVLS) on this node")
+    if gather == "nvls":
+        plan = plan_rows(M, world, target_piece=args.piece or M // world)
+    else:
+        plan = plan_rows(M, world, target_piece=(args.piece or 512) if world > 1 else M)
     my_rows = plan.local_rows(rank)
     # Host inputs (pinned): this rank's rows of the A buffer, and B.
     a_host = torch.empty(len(my_rows) * ROW_STRIDE, dtype=torch.float32, pin_memory=True)
@@ -166,25 +179,30 @@ def run_ours(args, rank, world, local):
     rng.uniform(SEEDS["c5"][1], K * N, -1.0, 1.0, np.float32, out=b_host.numpy())
     a_buf = a_host.to(dev)
     b = b_host.to(dev).view(K, N)
-    group = dist.group.WORLD if world > 1 else None
-    push = world > 1 and args.gather == "p2p"
+    push = gather in ("p2p", "p2p-ce")
     peer_out = PeerOutput(M, N, torch.float32, group, local) if push else None
-    c = peer_out.tensor if push else torch.empty(M, N, dtype=torch.float32, device=dev)
+    if rep is not None:
+        c = rep.tensor
+    else:
+        c = peer_out.tensor if push else torch.empty(M, N, dtype=torch.float32, device=dev)
     # piece i of this rank: rows [i*piece, (i+1)*piece) of the local buffer,
     # viewed with the 8704 row stride (first 8192 columns)
     pieces = [kx.TensorView(a_buf, (plan.piece, K), (ROW_STRIDE, 1), i * plan.piece * ROW_STRIDE)
               for i in range(plan.pieces)]
     scratch = [torch.empty(plan.piece, N, dtype=torch.float32, device=dev) for _ in range(plan.pieces)] \
-        if world > 1 and not push else None
-    streams = (torch.cuda.current_stream(dev), torch.cuda.Stream(dev)) if world > 1 and not push else None
+        if gather == "nccl" else None
+    streams = (torch.cuda.current_stream(dev), torch.cuda.Stream(dev)) if gather == "nccl" else None
     push_streams = None
     if push:
         push_streams = {r: torch.cuda.Stream(dev) for r in range(world) if r != rank}
         push_streams["comm"] = torch.cuda.Stream(dev)
 
     def step():
-        if push:
-            sharded_matmul_push(pieces, b, peer_out, plan, rank, group, streams=push_streams)
+        if rep is not None:
+            sharded_matmul_replicated(pieces, b, rep, plan, rank, group)
+        elif push:
+            sharded_matmul_push(pieces, b, peer_out, plan, rank, group, streams=push_streams,
+                                tail_kernel=gather == "p2p")
         else:
             sharded_matmul(pieces, b, c, plan, rank, group, streams=streams, scratch=scratch)
 
@@ -200,7 +218,12 @@ def run_ours(args, rank, world, local):
         step()
     barrier()
     # kernel-only timing of one GEMM launch (dominant kernel) for the roofline
-    kern_ms = time_dominant_kernel(h, pieces, b, c, plan, dev)
+    if rep is not None:
+        s0, e0 = plan.rows_of(rank, 0)
+        launch = lambda: kx.matmul_into_replicated(pieces[0], b, c[s0:e0], rep.mc + s0 * rep.row_bytes)  # noqa: E731
+    else:
+        launch = lambda: kx.matmul_into(pieces[0], b, c[:plan.piece])  # noqa: E731
+    kern_ms = time_dominant_kernel(launch, dev)
     barrier()
     launches0 = h.launches
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -233,6 +256,10 @@ def run_ours(args, rank, world, local):
         check["pass"] = check["pass"] and gathered
     if peer_out is not None:
         peer_out.close()
+    if rep is not None:
+        torch.cuda.synchronize(dev)
+        dist.barrier(device_ids=[local])
+        rep.close()
 
     result = None
     if rank == 0:
@@ -252,9 +279,10 @@ def run_ours(args, rank, world, local):
             "warmup": args.warmup, "ms_per_step": round(elapsed * 1e3 / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (SplitMix64 seeds 5, 6)",
             "config": {"workload": "c5: " + CONFIG_TEXT["c5"], "M": M, "N": N, "K": K, "a_row_stride": ROW_STRIDE,
-                       "parallelism": f"rows{world} block-cyclic piece={plan.piece}" + (
-                           "" if world == 1 else (" + copy-engine push to peers (CUDA IPC)" if push
-                                                  else " + NCCL all-gather")),
+                       "parallelism": f"rows{world} block-cyclic piece={plan.piece}" + {
+                           "none": "", "nvls": " + NVLS multicast stores from the GEMM epilogue",
+                           "p2p": " + push to peers over CUDA IPC (copy engines, all-SM kernel for the last piece)",
+                           "p2p-ce": " + copy-engine push to peers (CUDA IPC)", "nccl": " + NCCL all-gather"}[gather],
                        "l2": "inputs larger than L2 (A span 285 MB, B 268 MB)", "kernel": kname},
             "e2e": e2e,
             "gpu_launches": launches,
@@ -272,18 +300,16 @@ def run_ours(args, rank, world, local):
     return result
 
 
-def time_dominant_kernel(h, pieces, b, c, plan, dev, reps=5):
-    """Average duration of one GEMM launch (one piece) with CUDA events on the
-    stream the kernel runs on."""
+def time_dominant_kernel(launch, dev, reps=5):
+    """Average duration of one GEMM launch (one piece, as the step issues it)
+    with CUDA events on the stream the kernel runs on."""
     import torch
-    import kernix_b200 as kx
-    out = c[:plan.piece]
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    kx.matmul_into(pieces[0], b, out)
+    launch()
     torch.cuda.synchronize(dev)
     s.record()
     for _ in range(reps):
-        kx.matmul_into(pieces[0], b, out)
+        launch()
     e.record()
     e.synchronize()
     return s.elapsed_time(e) / reps
@@ -470,8 +496,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--piece", type=int, default=0, help="rows per sharded piece (0: 512 when sharded)")
-    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
-                    help="gathered output: copy-engine pushes into peers' C, or NCCL all-gather")
+    ap.add_argument("--gather", choices=["p2p", "p2p-ce", "nvls", "nccl"], default="p2p",
+                    help="gathered output: pushes into peers' C (copy engines while a piece computes, an "
+                         "all-SM kernel for the last piece; p2p-ce: copy engines only), NVLS multicast "
+                         "stores from the GEMM epilogue, or NCCL all-gather")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")

@@ -240,6 +240,26 @@ int kx_matmul_splitk_f32_static(const kx_tensor *a, const kx_tensor *b, const kx
 int kx_ipc_export(kx_handle *h, void *device_ptr, unsigned char *handle_out, kx_error *err);
 int kx_ipc_import(kx_handle *h, const unsigned char *handle, void **device_ptr, kx_error *err);
 int kx_ipc_close(kx_handle *h, void *device_ptr);
+/* out = matmul(a, b) as kx_matmul_*, with every element stored through
+ * `out_mc`: the NVLink multicast (NVLS) address of out->data's memory, from a
+ * multicast object that binds the same buffer on each GPU of the node.  One
+ * store reaches all of them, so when each rank computes its own rows of C this
+ * call leaves the full product on every rank once all ranks' calls have
+ * completed (the caller orders that, e.g. with a collective after the call).
+ * The split-TF32 kernel stores its epilogue through the address directly;
+ * other kernels store locally and a multicast copy of the rows follows. */
+int kx_matmul_replicated_f32(kx_handle *h, const kx_tensor *a, const kx_tensor *b, const kx_tensor *out,
+                             void *out_mc, kx_error *err);
+int kx_matmul_replicated_f64(kx_handle *h, const kx_tensor *a, const kx_tensor *b, const kx_tensor *out,
+                             void *out_mc, kx_error *err);
+/* Store `bytes` (a multiple of 4, 4-byte aligned) from this GPU's `src`
+ * through the multicast address `mc_dst` on the handle's stream. */
+int kx_multicast_store(kx_handle *h, const void *src, void *mc_dst, uint64_t bytes, kx_error *err);
+/* Copy `bytes` (multiple of 16, 16-byte aligned) from `src` to each of the
+ * `ndst` (<= 8) destinations with a kernel on the handle's stream: all SMs
+ * drive the NVLink stores.  For a step's last piece, when there is no GEMM
+ * left to overlap and the copy engines' fan-out would be the slower path. */
+int kx_peer_broadcast(kx_handle *h, const void *src, void *const *dsts, int ndst, uint64_t bytes, kx_error *err);
 /* Enqueue a device-to-device copy of `bytes` on `stream` (a cudaStream_t of the
  * handle's device; null = the handle's stream).  Either side may be an
  * imported peer pointer.  Returns once the copy is enqueued. */

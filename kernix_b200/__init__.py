@@ -35,7 +35,7 @@ MAX_RANK = _abi.MAX_RANK
 
 __all__ = [
     "matmul", "matmul_reference", "matmul_shape", "matmul_into", "conv2d", "conv2d_reference", "conv2d_shape",
-    "Conv2dOptions", "softmax_temperature",
+    "Conv2dOptions", "softmax_temperature", "matmul_into_replicated",
     "MatrixInput", "try_dense_matmul", "try_strided_matmul", "TensorView", "CudaExecutor", "Handle",
     "handle", "OpsError", "InvalidRank", "ContractDimensionMismatch", "BroadcastIncompatible",
     "ElementCountOverflow", "DimensionOverflow", "LayoutError", "InvalidParameter", "ExactRank",
@@ -239,6 +239,19 @@ def matmul_into(a, b, out) -> None:
     err = KxError()
     da, db, do = _descriptor(a), _descriptor(b), _descriptor(out)
     raise_for(fn(h.ptr, C.byref(da), C.byref(db), C.byref(do), C.byref(err)), err)
+
+
+def matmul_into_replicated(a, b, out, out_mc: int) -> None:
+    """``matmul_into`` whose stores go through ``out_mc``, the NVLink multicast
+    address of ``out``'s first element: the product lands in the copy of
+    ``out`` on every GPU bound to the multicast object."""
+    fn = _fn("kx_matmul_replicated", a.dtype)
+    h = _bind(a)
+    err = KxError()
+    da, db, do = _descriptor(a), _descriptor(b), _descriptor(out)
+    # out_mc addresses out's first element; the library adds the origin itself
+    base = int(out_mc) - do.origin * out.element_size()
+    raise_for(fn(h.ptr, C.byref(da), C.byref(db), C.byref(do), C.c_void_p(base), C.byref(err)), err)
 
 
 class _Ordered:

@@ -123,9 +123,13 @@ _SIGNATURES = {
     "kx_try_strided_matmul_f64": (C.c_int, [_vp, _P(KxMatrix), _P(KxMatrix), _vp, _u64]),
     "kx_matrix_validate": (C.c_int, [_P(KxMatrix), C.c_uint32, _P(KxError)]),
     "kx_matmul_splitk_f32_static": (C.c_int, [_P(KxTensor), _P(KxTensor), _P(KxTensor), _vp, _P(KxError)]),
+    "kx_matmul_replicated_f32": (C.c_int, [_vp, _P(KxTensor), _P(KxTensor), _P(KxTensor), _vp, _P(KxError)]),
+    "kx_matmul_replicated_f64": (C.c_int, [_vp, _P(KxTensor), _P(KxTensor), _P(KxTensor), _vp, _P(KxError)]),
+    "kx_multicast_store": (C.c_int, [_vp, _vp, _vp, C.c_uint64, _P(KxError)]),
     "kx_ipc_export": (C.c_int, [_vp, _vp, C.c_char_p, _P(KxError)]),
     "kx_ipc_import": (C.c_int, [_vp, C.c_char_p, _P(_vp), _P(KxError)]),
     "kx_ipc_close": (C.c_int, [_vp, _vp]),
+    "kx_peer_broadcast": (C.c_int, [_vp, _vp, _P(_vp), C.c_int, C.c_uint64, _P(KxError)]),
     "kx_copy_async": (C.c_int, [_vp, _vp, _vp, C.c_uint64, _vp, _P(KxError)]),
     "kx_launch_count": (C.c_uint64, [_vp]),
     "kx_last_kernel": (C.c_char_p, [_vp]),

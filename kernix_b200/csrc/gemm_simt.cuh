@@ -56,6 +56,7 @@ struct GemmParams {
     int splits;          // split-K factor (1 = direct store)
     int k_per_split;     // multiple of BK
     T *ws;               // split-K partials [splits][nbatch][M][N] (C-order)
+    T *C_mc;             // NVLink multicast address of C (null: none); C is then C-contiguous
 };
 
 // Operand access modes.

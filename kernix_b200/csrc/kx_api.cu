@@ -104,7 +104,8 @@ int build_params(const MatmulPlan &pl, const kx_tensor *a, const T *a_ptr, const
 }
 
 template <typename T>
-int matmul_device(kx_handle *hh, const kx_tensor *a, const kx_tensor *b, const kx_tensor *out, kx_error *err) {
+int matmul_device(kx_handle *hh, const kx_tensor *a, const kx_tensor *b, const kx_tensor *out, kx_error *err,
+                  void *out_mc = nullptr) {
     if (!hh) return set_err(err, KX_E_PARAM, "matmul", "null handle");
     Handle *h = &hh->impl;
     Span sa, sb, so;
@@ -131,6 +132,7 @@ int matmul_device(kx_handle *hh, const kx_tensor *a, const kx_tensor *b, const k
     DeviceGuard g(h->device);
     if (!g.ok) return set_err(err, KX_E_NO_DEVICE, "matmul", "cannot select device");
     T *c_ptr = static_cast<T *>(out->data) + out->origin;
+    T *mc_ptr = out_mc ? static_cast<T *>(out_mc) + out->origin : nullptr;
     if (pl.k == 0) {
         cudaError_t ce = cudaMemsetAsync(c_ptr, 0, total * sizeof(T), h->stream);
         if (ce != cudaSuccess) {
@@ -138,12 +140,14 @@ int matmul_device(kx_handle *hh, const kx_tensor *a, const kx_tensor *b, const k
             return cuda_err(err, h, "matmul");
         }
         h->last_kernel = "memset";
-        return KX_OK;
+        rc = mc_ptr ? mc_copy(h, c_ptr, mc_ptr, total * sizeof(T)) : KX_OK;
+        return rc == KX_E_CUDA ? cuda_err(err, h, "matmul") : rc;
     }
     GemmParams<T> p;
     rc = build_params<T>(pl, a, static_cast<const T *>(a->data) + a->origin, b,
                          static_cast<const T *>(b->data) + b->origin, out->strides, c_ptr, &p, err);
     if (rc) return rc;
+    p.C_mc = mc_ptr;
     const char *name = "none";
     rc = run_gemm<T>(h, p, &name);
     h->last_kernel = name;
@@ -438,6 +442,16 @@ int kx_matmul_f32(kx_handle *h, const kx_tensor *a, const kx_tensor *b, const kx
 }
 int kx_matmul_f64(kx_handle *h, const kx_tensor *a, const kx_tensor *b, const kx_tensor *out, kx_error *err) {
     return matmul_device<double>(h, a, b, out, err);
+}
+int kx_matmul_replicated_f32(kx_handle *h, const kx_tensor *a, const kx_tensor *b, const kx_tensor *out,
+                             void *out_mc, kx_error *err) {
+    if (!out_mc) return set_err(err, KX_E_PARAM, "matmul_replicated", "null multicast address");
+    return matmul_device<float>(h, a, b, out, err, out_mc);
+}
+int kx_matmul_replicated_f64(kx_handle *h, const kx_tensor *a, const kx_tensor *b, const kx_tensor *out,
+                             void *out_mc, kx_error *err) {
+    if (!out_mc) return set_err(err, KX_E_PARAM, "matmul_replicated", "null multicast address");
+    return matmul_device<double>(h, a, b, out, err, out_mc);
 }
 
 int kx_try_dense_matmul_f32(kx_handle *h, const float *a, uint64_t a_len, const float *b, uint64_t b_len, float *out,

@@ -141,6 +141,11 @@ int run_gemm(Handle *h, GemmParams<T> p, const char **kernel_name) {
             ++h->launches;
         }
     }
+    if (ce == cudaSuccess && p.C_mc) {
+        // The SIMT kernels store locally; the rows then go out through the
+        // multicast address (C is C-contiguous here).
+        return mc_copy(h, p.C, p.C_mc, (uint64_t)p.nbatch * p.M * p.N * sizeof(T));
+    }
     return ce == cudaSuccess ? KX_OK : h->cuda_fail(ce);
 }
 

@@ -69,6 +69,7 @@ struct TcParams {
     const float *B;
     int64_t b_rs, b_cs, b_bs;
     float *C;
+    float *Cmc;       // NVLink multicast address of C, or null: stores go there instead
     int64_t c_rs;     // row stride of C (elements)
     int64_t c_bs;     // batch stride of C
     int M, N, K;
@@ -179,6 +180,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 // MMA keeps 11 of them; with the dropped lo*lo term the error per product stays
 // below ~1.7e-6 |a b| even for adversarial mantissas.
 __device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+// Stores through an NVLink multicast address: one store reaches the same
+// offset of C on every GPU bound to the multicast object.
+__device__ __forceinline__ void mc_st4(float *addr, float a, float b, float c, float d) {
+    asm volatile("multimem.st.weak.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
+__device__ __forceinline__ void mc_st1(float *addr, float v) {
+    asm volatile("multimem.st.weak.global.b32 [%0], %1;" ::"l"(addr), "r"(__float_as_uint(v)) : "memory");
+}
+
 // Exponent of all ones: an inf or NaN input.
 __device__ __forceinline__ uint32_t nonfinite_bits(float x) {
     return (__float_as_uint(x) & 0x7F800000u) == 0x7F800000u ? 1u : 0u;
@@ -414,21 +425,24 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 if (row < p.M) {
                     const float *arow = p.A + (int64_t)ab * p.a_bs + (int64_t)row * p.a_rs;
                     const float *bbat = p.B + (int64_t)bb * p.b_bs;
-                    float *crow = p.C + (int64_t)batch * p.c_bs + (int64_t)row * p.c_rs;
+                    const int64_t coff = (int64_t)batch * p.c_bs + (int64_t)row * p.c_rs;
                     for (int j = 0; j < HALF_COLS && n0 + col0 + j < p.N; ++j) {
                         const float *bcol = bbat + (int64_t)(n0 + col0 + j) * p.b_cs;
                         float acc = 0.0f;
                         for (int k = 0; k < p.K; ++k) acc = fmaf(arow[k], bcol[(int64_t)k * p.b_rs], acc);
-                        crow[n0 + col0 + j] = acc;
+                        if (p.Cmc) mc_st1(p.Cmc + coff + n0 + col0 + j, acc);
+                        else p.C[coff + n0 + col0 + j] = acc;
                     }
                 }
             } else {
                 // Stream out: 16 columns of cross terms at a time, added to the
                 // running sum and stored straight away.
                 const bool in_rows = row < p.M;
-                float *crow = p.C + (int64_t)batch * p.c_bs + (int64_t)(in_rows ? row : 0) * p.c_rs + n0 + col0;
+                const int64_t coff = (int64_t)batch * p.c_bs + (int64_t)(in_rows ? row : 0) * p.c_rs + n0 + col0;
+                float *crow = p.C + coff;
+                float *mrow = p.Cmc ? p.Cmc + coff : nullptr;
                 const bool vec = (p.c_rs % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
-                                 (p.c_bs % 4 == 0);
+                                 ((reinterpret_cast<uintptr_t>(p.Cmc) & 15) == 0) && (p.c_bs % 4 == 0);
 #pragma unroll
                 for (int c = 0; c < HALF_COLS / 16; ++c) {
                     uint32_t r[16];
@@ -439,7 +453,16 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] = sum[c * 16 + j] + __uint_as_float(r[j]);
                     const int gcol = n0 + col0 + c * 16;
-                    if (vec && gcol + 16 <= p.N) {
+                    if (mrow) {
+                        if (vec && gcol + 16 <= p.N) {
+#pragma unroll
+                            for (int j = 0; j < 16; j += 4) mc_st4(mrow + c * 16 + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                if (gcol + j < p.N) mc_st1(mrow + c * 16 + j, v[j]);
+                        }
+                    } else if (vec && gcol + 16 <= p.N) {
 #pragma unroll
                         for (int j = 0; j < 16; j += 4)
                             *reinterpret_cast<float4 *>(crow + c * 16 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -452,6 +475,9 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             }
         }
     }
+    // Multicast stores are ordered before whatever later tells the other GPUs
+    // that this kernel is done.
+    if (p.Cmc && warp >= WORK_WARP0) asm volatile("fence.acq_rel.sys;" ::: "memory");
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -580,6 +606,7 @@ int run_gemm_tc(Handle *h, const GemmParams<float> &p, const char **kernel_name)
     tp.b_cs = p.b_cs;
     tp.b_bs = b_bs;
     tp.C = p.C;
+    tp.Cmc = p.C_mc;
     tp.c_rs = p.M == 1 ? 0 : p.c_rs;
     tp.c_bs = c_bs;
     tp.M = p.M;

@@ -87,6 +87,10 @@ template <typename T> int run_gemm(Handle *h, GemmParams<T> p, const char **kern
 // cannot describe the operands (the caller then uses the SIMT kernel).
 bool tc_eligible(const GemmParams<float> &p);
 int run_gemm_tc(Handle *h, const GemmParams<float> &p, const char **kernel_name);
+// Store `bytes` (a multiple of 4) from this GPU's `src` through the NVLink
+// multicast address `mc_dst`: the bytes land at the same offset in the buffer
+// of every GPU bound to the multicast object (kx_nvls.cu).
+int mc_copy(Handle *h, const void *src, void *mc_dst, uint64_t bytes);
 // Layout of the handle's device flag area (32-bit words), one owner per word:
 //   [1]     status written by device code: bit 0 = a bounded wait expired
 //   [2..3]  softmax: 64-bit key of the first nonfinite element (8-byte aligned)

@@ -9,9 +9,16 @@ of every rank is all-gathered straight into rows
 layout is already C's row order.  The all-gather of piece ``i`` runs on a
 communication stream while piece ``i + 1`` is being multiplied.
 
-Two ways to gather on GPUs:
+Three ways to gather on GPUs:
 
-* ``PeerOutput`` + ``sharded_matmul_push`` (the default for CUDA): C lives in
+* ``ReplicatedOutput`` + ``sharded_matmul_replicated`` (the default when the
+  node has NVLink multicast, NVLS): C lives in symmetric memory bound to an
+  NVLink multicast object; the GEMM's epilogue stores every output element
+  once through the multicast address and the NVSwitch delivers it to every
+  rank's C.  Each rank sends its rows once instead of once per peer, the
+  gather overlaps the GEMM's later tiles, and one small all-reduce closes the
+  step.
+* ``PeerOutput`` + ``sharded_matmul_push``: C lives in
   library-allocated memory that every rank maps into every other rank (CUDA
   IPC over NVLink).  After each piece's GEMM a rank pushes that piece's rows
   straight into the same rows of every peer's C with the copy engines, one
@@ -185,6 +192,22 @@ class PeerOutput:
                                         C.c_void_p(streams[r].cuda_stream), C.byref(err))
             _abi.raise_for(rc, err)
 
+    def broadcast_rows(self, r0: int, r1: int) -> None:
+        """Write rows [r0, r1) of this rank's C into every peer's C with a
+        kernel on the current stream (all SMs drive the NVLink stores)."""
+        import ctypes as C
+
+        import torch
+
+        from . import _abi
+        off, nbytes = r0 * self.row_bytes, (r1 - r0) * self.row_bytes
+        dsts = [p + off for r, p in enumerate(self.peers) if r != self.rank]
+        arr = (C.c_void_p * len(dsts))(*dsts)
+        self.h.set_stream(torch.cuda.current_stream(self.h.device))
+        err = _abi.KxError()
+        rc = _abi.lib.kx_peer_broadcast(self.h.ptr, C.c_void_p(self.ptr + off), arr, len(dsts), nbytes, C.byref(err))
+        _abi.raise_for(rc, err)
+
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (collective: every
         rank calls it, after its last push has completed)."""
@@ -208,9 +231,12 @@ class PeerOutput:
 
 
 def sharded_matmul_push(a_pieces, b, out: PeerOutput, plan: RowPlan, rank: int, group=None,
-                        matmul_into: Callable | None = None, streams: dict | None = None) -> None:
+                        matmul_into: Callable | None = None, streams: dict | None = None,
+                        tail_kernel: bool = True) -> None:
     """Compute this rank's pieces into ``out.tensor`` and push each piece into
-    every peer's copy as soon as its GEMM has finished.
+    every peer's copy as soon as its GEMM has finished: with the copy engines
+    while a later piece computes, and (``tail_kernel``) with an all-SM copy
+    kernel for the last piece.
 
     ``streams`` maps each peer rank to a CUDA stream for its pushes and key
     ``"comm"`` to the stream of the closing all-reduce.  On return the work is
@@ -232,6 +258,10 @@ def sharded_matmul_push(a_pieces, b, out: PeerOutput, plan: RowPlan, rank: int, 
     for i in range(plan.pieces):
         s, e = plan.rows_of(rank, i)
         matmul_into(a_pieces[i], b, c[s:e])
+        if i == plan.pieces - 1 and tail_kernel:
+            # nothing left to overlap: every SM pushes the last piece
+            out.broadcast_rows(s, e)
+            continue
         ev = torch.cuda.Event()
         ev.record(compute)
         for r in peers:
@@ -243,3 +273,46 @@ def sharded_matmul_push(a_pieces, b, out: PeerOutput, plan: RowPlan, rank: int, 
     with torch.cuda.stream(comm):
         dist.all_reduce(out.done, group=group)
     compute.wait_stream(comm)
+
+
+class ReplicatedOutput:
+    """An M x N output in symmetric memory, bound on every rank of ``group``
+    to one NVLink multicast object (torch's symmetric-memory rendezvous).
+    ``mc`` is the multicast address of the tensor's first element;
+    ``available`` is False when the node offers no multicast (callers then
+    use ``PeerOutput``)."""
+
+    def __init__(self, m: int, n: int, dtype, group, device: int):
+        import torch
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.tensor = symm_mem.empty((m, n), dtype=dtype, device=f"cuda:{device}")
+        self.hdl = symm_mem.rendezvous(self.tensor, group)
+        self.rank = self.hdl.rank
+        mc = int(self.hdl.multicast_ptr) if self.hdl.has_multicast_support else 0
+        base = int(self.hdl.buffer_ptrs[self.rank])
+        off = self.tensor.data_ptr() - base
+        # only the unambiguous layout: the tensor starts the symmetric buffer
+        self.available = mc != 0 and off == 0 and int(self.hdl.buffer_size) >= self.tensor.numel() * \
+            self.tensor.element_size()
+        self.mc = mc if self.available else 0
+        self.row_bytes = n * self.tensor.element_size()
+        self.done = torch.zeros(1, dtype=torch.int32, device=f"cuda:{device}")
+
+    def close(self) -> None:
+        self.hdl = None
+        self.tensor = None
+
+
+def sharded_matmul_replicated(a_pieces, b, out: ReplicatedOutput, plan: RowPlan, rank: int, group=None) -> None:
+    """Compute this rank's pieces with their stores going through the
+    multicast address, then one all-reduce of a 4-byte flag: once it has
+    completed on a rank, every rank's rows are in that rank's C."""
+    import torch.distributed as dist
+
+    from . import matmul_into_replicated
+    c = out.tensor
+    for i in range(plan.pieces):
+        s, e = plan.rows_of(rank, i)
+        matmul_into_replicated(a_pieces[i], b, c[s:e], out.mc + s * out.row_bytes)
+    dist.all_reduce(out.done, group=group)
