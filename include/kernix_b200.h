@@ -118,12 +118,19 @@ typedef struct kx_conv2d_options {
     uint64_t groups;
 } kx_conv2d_options;
 
-/* Kernel family selection for f32 (f64 always runs on the FP64 pipe). */
+/* Kernel family selection for f32. */
 typedef enum kx_f32_variant {
     KX_F32_AUTO = 0,    /* library chooses per shape and layout */
     KX_F32_FFMA = 1,    /* SIMT FP32 FMA, fp32 accumulation */
     KX_F32_3XTF32 = 2   /* split-TF32 tensor-core contraction (tcgen05 + TMEM) */
 } kx_f32_variant;
+
+/* Kernel family selection for f64. */
+typedef enum kx_f64_variant {
+    KX_F64_AUTO = 0,    /* library chooses per shape and layout */
+    KX_F64_DFMA = 1,    /* SIMT DFMA outer products */
+    KX_F64_DMMA = 2     /* FP64 tensor pipe (mma.sync m16n8k4 .f64), f64 accumulation */
+} kx_f64_variant;
 
 typedef struct kx_handle kx_handle;
 
@@ -138,6 +145,7 @@ int kx_destroy(kx_handle *h);
 /* Subsequent work on this handle is ordered on `stream` (a cudaStream_t). */
 int kx_set_stream(kx_handle *h, void *stream);
 int kx_set_f32_variant(kx_handle *h, int variant);
+int kx_set_f64_variant(kx_handle *h, int variant);
 /* Ordered mode (CpuExecutor::with_ordered_matmul, execution.rs:76-84): every
  * output is accumulated in increasing k with separately rounded multiply and
  * add, so device matmul results equal matmul_reference (linalg.rs:57-64,

@@ -80,6 +80,10 @@ class Handle:
     def set_f32_variant(self, variant: int) -> None:
         raise_for(lib.kx_set_f32_variant(self._h, int(variant)), None)
 
+    def set_f64_variant(self, variant: int) -> None:
+        """0 = automatic, 1 = SIMT DFMA, 2 = FP64 tensor pipe (DMMA)."""
+        raise_for(lib.kx_set_f64_variant(self._h, int(variant)), None)
+
     def set_ordered_matmul(self, ordered: bool) -> None:
         """Increasing-k, separately rounded accumulation (bitwise equal to
         matmul_reference); see CpuExecutor::with_ordered_matmul."""

@@ -128,6 +128,7 @@ _SIGNATURES = {
     "kx_multicast_store": (C.c_int, [_vp, _vp, _vp, C.c_uint64, _P(KxError)]),
     "kx_ipc_export": (C.c_int, [_vp, _vp, C.c_char_p, _P(KxError)]),
     "kx_ipc_import": (C.c_int, [_vp, C.c_char_p, _P(_vp), _P(KxError)]),
+    "kx_set_f64_variant": (C.c_int, [_vp, C.c_int]),
     "kx_ipc_close": (C.c_int, [_vp, _vp]),
     "kx_peer_broadcast": (C.c_int, [_vp, _vp, _P(_vp), C.c_int, C.c_uint64, _P(KxError)]),
     "kx_copy_async": (C.c_int, [_vp, _vp, _vp, C.c_uint64, _vp, _P(KxError)]),

@@ -332,6 +332,12 @@ int kx_set_f32_variant(kx_handle *hh, int variant) {
     return KX_OK;
 }
 
+int kx_set_f64_variant(kx_handle *hh, int variant) {
+    if (!hh || variant < KX_F64_AUTO || variant > KX_F64_DMMA) return KX_E_PARAM;
+    hh->impl.f64_variant = variant;
+    return KX_OK;
+}
+
 int kx_set_ordered_matmul(kx_handle *hh, int ordered) {
     if (!hh) return KX_E_PARAM;
     hh->impl.ordered = ordered != 0;

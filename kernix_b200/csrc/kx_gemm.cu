@@ -94,6 +94,18 @@ int run_gemm(Handle *h, GemmParams<T> p, const char **kernel_name) {
             }
         }
     }
+    if constexpr (std::is_same<T, double>::value) {
+        // FP64 tensor pipe for layouts with a unit stride along k or m/n and
+        // enough 128x128 tiles to spread over the SMs.
+        if (!h->ordered && h->f64_variant != KX_F64_DFMA) {
+            const int64_t tiles = (int64_t)((p.M + 127) / 128) * ((p.N + 127) / 128) * p.nbatch;
+            if (h->f64_variant == KX_F64_DMMA || tiles >= h->sm_count / 2) {
+                int rc = run_gemm_dmma(h, p, kernel_name);
+                if (rc == KX_OK && p.C_mc) return mc_copy(h, p.C, p.C_mc, (uint64_t)p.nbatch * p.M * p.N * sizeof(T));
+                if (rc != KX_DECLINED) return rc;
+            }
+        }
+    }
     if (h->ordered) {
         // Ordered mode: one pass over k per output, separately rounded
         // multiply and add -- bitwise equal to the reference's ordered path.

@@ -17,6 +17,7 @@ struct Handle {
     int sm_count = 148;
     cudaStream_t stream = nullptr;
     int f32_variant = KX_F32_AUTO;
+    int f64_variant = KX_F64_AUTO;
     bool ordered = false;        // CpuExecutor::with_ordered_matmul equivalent
     uint64_t launches = 0;
     const char *last_kernel = "none";
@@ -87,6 +88,9 @@ template <typename T> int run_gemm(Handle *h, GemmParams<T> p, const char **kern
 // cannot describe the operands (the caller then uses the SIMT kernel).
 bool tc_eligible(const GemmParams<float> &p);
 int run_gemm_tc(Handle *h, const GemmParams<float> &p, const char **kernel_name);
+// f64 on the FP64 tensor pipe (kx_gemm_f64.cu).  KX_DECLINED for layouts
+// without a unit stride along k or m/n (the SIMT DFMA kernel takes those).
+int run_gemm_dmma(Handle *h, const GemmParams<double> &p, const char **kernel_name);
 // Store `bytes` (a multiple of 4) from this GPU's `src` through the NVLink
 // multicast address `mc_dst`: the bytes land at the same offset in the buffer
 // of every GPU bound to the multicast object (kx_nvls.cu).
