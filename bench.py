@@ -10,8 +10,10 @@ NVLink, so ``scaling`` is strong (fixed total work).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 N > 1 runs under ``python -m torch.distributed.run --nproc-per-node N``.  Rank 0
-prints one JSON line.  ``--config c1..c5`` selects the other configurations
-(parity-test cases, reported in the design notes, not bench lines).
+prints one JSON line.  ``--workload c1|c2|c3|c4`` measures one of the other
+configurations on one GPU (device-resident seeded inputs, a parity check of the
+timed output against the oracle) and prints its own JSON line; those are
+reported in the design notes, not as the bench line.
 """
 from __future__ import annotations
 
@@ -489,6 +491,159 @@ def run_reference(args, rank, world):
             "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# ---------------------------------------------------------------------------
+# the other workloads (one GPU): c1..c4
+# ---------------------------------------------------------------------------
+def _timed(fn, steps, warmup, dev):
+    """Average ms per call over ``steps`` after ``warmup`` calls, CUDA events
+    on the current stream, with the clock record of the timed region."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index or 0) as clk:
+        s.record()
+        for _ in range(steps):
+            fn()
+        e.record()
+        e.synchronize()
+    return s.elapsed_time(e) / steps, clk.summary()
+
+
+def _pipe_of(kernel: str) -> str:
+    if "tf32" in kernel:
+        return "3xtf32"
+    if "dmma" in kernel or kernel.endswith("f64"):
+        return "fp64"
+    return "fp32-simt"
+
+
+def run_workload(args):
+    """Measure c1..c4 on cuda:0 and check the timed output against the oracle."""
+    import torch
+    import kernix_b200 as kx
+    import oracle
+    from kernix_b200 import rng
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    h = kx.handle(0)
+    peaks, _ = measured_peaks()
+    w = args.workload
+    res = {"metric": METRIC, "workload": f"{w}: {CONFIG_TEXT[w]}", "n_gpus": 1, "steps": args.steps,
+           "warmup": args.warmup, "data": f"synthetic (SplitMix64 seed(s) {SEEDS[w]})"}
+    if w == "c1":
+        v = rng.uniform(SEEDS["c1"][0], 2 * 512 * 512, -1.0, 1.0, np.float32)
+        a_np, b_np = v[:512 * 512].reshape(512, 512), v[512 * 512:].reshape(512, 512)
+        a, b = torch.from_numpy(a_np).to(dev), torch.from_numpy(b_np).to(dev)
+        c = torch.empty(512, 512, device=dev)
+        ms, clocks = _timed(lambda: kx.matmul_into(a, b, c), args.steps, args.warmup, dev)
+        flops = 2.0 * 512 ** 3
+        exp, ab = oracle.gemm_dot2(oracle.View.of(a_np), oracle.View.of(b_np))
+        err = float(np.max(np.abs(c.cpu().numpy().astype(np.float64) - exp) / ab))
+        check = {"rows_checked": 512, "max_err_over_sum_abs": err, "bound": 2e-6, "pass": err <= 2e-6}
+        res.update(dtype="f32", config={"workload": "c1", "M": 512, "N": 512, "K": 512,
+                                        "l2": "inputs (3 MB) stay L2-resident: latency-bound"})
+    elif w == "c2":
+        n = args.size or 4096
+        v = rng.normal(SEEDS["c2"][0], 2 * n * n, 1.0, np.float64)
+        a_np, bt_np = v[:n * n].reshape(n, n), v[n * n:].reshape(n, n)
+        a, bt = torch.from_numpy(a_np).to(dev), torch.from_numpy(bt_np).to(dev)
+        c = torch.empty(n, n, dtype=torch.float64, device=dev)
+        ms, clocks = _timed(lambda: kx.matmul_into(a, bt.t(), c), args.steps, args.warmup, dev)
+        flops = 2.0 * n ** 3
+        worst = 0.0
+        for r in (0, n // 3, n - 1):
+            exp, ab = oracle.gemm_dot2(oracle.View(a_np, (1, n), (n, 1), r * n), oracle.View(bt_np, (n, n), (1, n)))
+            worst = max(worst, float(np.max(np.abs(c[r].cpu().numpy() - exp[0]) / ab[0])))
+        check = {"rows_checked": 3, "max_err_over_sum_abs": worst, "bound": 1e-13, "pass": worst <= 1e-13}
+        res.update(dtype="f64", config={"workload": "c2", "M": n, "N": n, "K": n, "b_layout": "transposed view",
+                                        "l2": "inputs larger than L2 (268 MB each)"})
+    elif w == "c3":
+        nb = args.batch or 16
+        shape = (nb, 32, 2048, 128)
+        cnt = int(np.prod(shape))
+        host = torch.empty(3 * cnt, dtype=torch.float32, pin_memory=True)
+        rng.normal(SEEDS["c3"][0], 3 * cnt, 1.0, np.float32, out=host.numpy())
+        q = host[:cnt].view(shape).to(dev)
+        k_ = host[cnt:2 * cnt].view(shape).to(dev)
+        v_ = host[2 * cnt:].view(shape).to(dev)
+        t = math.sqrt(128.0)
+        sc = torch.empty(nb, 32, 2048, 2048, device=dev)
+        pr = torch.empty_like(sc)
+        o = torch.empty(shape, device=dev)
+
+        def step():
+            kx.matmul_into(q, k_.transpose(2, 3), sc)
+            kx.softmax_temperature_into(sc, -1, t, pr)
+            kx.matmul_into(pr, v_, o)
+        ms, clocks = _timed(step, args.steps, args.warmup, dev)
+        qk_ms, _ = _timed(lambda: kx.matmul_into(q, k_.transpose(2, 3), sc), 2, 1, dev)
+        qk_kernel = h.last_kernel
+        sm_ms, _ = _timed(lambda: kx.softmax_temperature_into(sc, -1, t, pr), 2, 1, dev)
+        pv_ms, _ = _timed(lambda: kx.matmul_into(pr, v_, o), 2, 1, dev)
+        flops = 2.0 * 2 * nb * 32 * 2048 * 2048 * 128
+        # parity: two heads, three rows each
+        worst_s = worst_o = worst_p = 0.0
+        for bi, hi in ((0, 0), (nb - 1, 31)):
+            qh, kh, vh = (x[bi, hi].cpu().numpy() for x in (q, k_, v_))
+            for r in (0, 1000, 2047):
+                exp, ab = oracle.gemm_dot2(oracle.View(qh, (1, 128), (128, 1), r * 128), oracle.View(kh, (128, 2048), (1, 128)))
+                srow = sc[bi, hi, r].cpu().numpy()
+                worst_s = max(worst_s, float(np.max(np.abs(srow - exp[0]) / ab[0])))
+                xl = srow.astype(np.longdouble)
+                d = (xl - xl.max()) / np.longdouble(t)
+                truth = np.exp(d) / np.exp(d).sum()
+                prow = pr[bi, hi, r].cpu().numpy()
+                tol = (8 + 2 * 11 + 2 * np.abs(d).astype(np.float64)) * np.finfo(np.float32).eps
+                worst_p = max(worst_p, float(np.max(np.abs(prow - truth).astype(np.float64) / (tol * np.abs(truth).astype(np.float64) + 1e-38))))
+                exp, ab = oracle.gemm_dot2(oracle.View(prow, (1, 2048), (2048, 1)), oracle.View.of(vh))
+                worst_o = max(worst_o, float(np.max(np.abs(o[bi, hi, r].cpu().numpy() - exp[0]) / ab[0])))
+        check = {"heads_checked": 2, "rows_per_head": 3, "S_max_err_over_sum_abs": worst_s,
+                 "P_max_err_over_tolerance": worst_p, "O_max_err_over_sum_abs": worst_o,
+                 "pass": worst_s <= 2e-6 and worst_o <= 2e-6 and worst_p <= 1.0}
+        sm_bytes = 2.0 * sc.numel() * 4
+        res["parts"] = {"qk_ms": round(qk_ms, 3), "qk_tflops": round(flops / 2 / qk_ms / 1e9, 2), "qk_kernel": qk_kernel,
+                        "softmax_ms": round(sm_ms, 3), "softmax_gbs": round(sm_bytes / sm_ms / 1e6, 1),
+                        "softmax_frac_of_hbm": round(sm_bytes / sm_ms / 1e6 / peaks["hbm_gbs"], 3),
+                        "pv_ms": round(pv_ms, 3), "pv_tflops": round(flops / 2 / pv_ms / 1e9, 2),
+                        "pv_kernel": h.last_kernel}
+        res.update(dtype="f32", config={"workload": "c3", "batch": nb, "heads": 32, "seq": 2048, "d": 128,
+                                        "l2": "inputs larger than L2 (S and P 8.6 GB at batch 16)"})
+    elif w == "c4":
+        nb = args.batch or 64
+        xn = nb * 128 * 56 * 56
+        x_np = rng.uniform(SEEDS["c4"][0], 64 * 128 * 56 * 56, -1.0, 1.0, np.float32)[:xn].reshape(nb, 128, 56, 56)
+        w_np = rng.normal(SEEDS["c4"][1], 256 * 128 * 9, math.sqrt(2.0 / 1152.0), np.float32).reshape(256, 128, 3, 3)
+        x, wt = torch.from_numpy(x_np).to(dev), torch.from_numpy(w_np).to(dev)
+        opts = kx.Conv2dOptions(padding=(1, 1))
+        y = kx.conv2d(x, wt, opts)
+        ms, clocks = _timed(lambda: kx.conv2d_into(x, wt, y, opts), args.steps, args.warmup, dev)
+        flops = 2.0 * 256 * 1152 * nb * 56 * 56
+        sub = np.ascontiguousarray(w_np[[0, 255]])
+        d2, ab = oracle.conv2d_dot2(oracle.View.of(x_np[:1]), oracle.View.of(sub), padding=(1, 1))
+        got = y[:1, [0, 255]].cpu().numpy().astype(np.float64)
+        err = float(np.max(np.abs(got - d2) / np.maximum(ab, 1e-300)))
+        check = {"outputs_checked": int(got.size), "max_err_over_sum_abs": err, "bound": 2e-6, "pass": err <= 2e-6}
+        res.update(dtype="f32", config={"workload": "c4", "batch": nb, "c_in": 128, "hw": 56, "c_out": 256,
+                                        "kernel_hw": 3, "stride": 1, "pad": 1,
+                                        "l2": "x 103 MB + y 206 MB at batch 64: larger than L2"})
+    else:
+        raise ValueError(w)
+    kernel = h.last_kernel
+    h.synchronize()
+    tflops = flops / ms / 1e9
+    pipe = _pipe_of(kernel if w != "c3" else res["parts"]["qk_kernel"])
+    sm_max = clocks.get("sm_max_mhz") or peaks.get("sm_max_mhz", 1965.0)
+    peak, basis = pipe_peak(pipe, peaks, float(sm_max))
+    res.update(value=round(tflops, 3), unit="TFLOP/s", ms_per_step=round(ms, 4), higher_is_better=True,
+               kernel=kernel, clocks=clocks, check=check,
+               roofline={"bound": "tensor" if pipe != "fp32-simt" else "fp32 pipe", "pipe": pipe,
+                         "achieved": round(tflops, 3), "peak": round(peak, 3), "unit": "TFLOP/s",
+                         "frac": round(tflops / peak, 4), "peak_basis": basis})
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -503,6 +658,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
+    ap.add_argument("--workload", choices=["c5", "c1", "c2", "c3", "c4"], default="c5",
+                    help="c5 is the headline (this bench line); c1..c4 print their own measurement on one GPU")
+    ap.add_argument("--batch", type=int, default=0, help="c3/c4: batch size (default: the workload's)")
     ap.add_argument("--size", type=int, default=8192,
                     help="profiling aid: M=N=K=size with row stride size+512 (8192 is the workload)")
     args = ap.parse_args()
@@ -511,6 +669,11 @@ def main():
         M = N = K = args.size
         ROW_STRIDE = args.size + 512
     rank, world, local = env_rank()
+    if args.workload != "c5":
+        if args.size == 8192:
+            args.size = 0
+        print(json.dumps(run_workload(args)), flush=True)
+        return
     if world != args.gpus:
         print(f"warning: WORLD_SIZE={world} but --gpus {args.gpus}", file=sys.stderr)
     if args.impl == "reference":

@@ -35,7 +35,7 @@ MAX_RANK = _abi.MAX_RANK
 
 __all__ = [
     "matmul", "matmul_reference", "matmul_shape", "matmul_into", "conv2d", "conv2d_reference", "conv2d_shape",
-    "Conv2dOptions", "softmax_temperature", "matmul_into_replicated",
+    "Conv2dOptions", "softmax_temperature", "matmul_into_replicated", "conv2d_into", "softmax_temperature_into",
     "MatrixInput", "try_dense_matmul", "try_strided_matmul", "TensorView", "CudaExecutor", "Handle",
     "handle", "OpsError", "InvalidRank", "ContractDimensionMismatch", "BroadcastIncompatible",
     "ElementCountOverflow", "DimensionOverflow", "LayoutError", "InvalidParameter", "ExactRank",
@@ -317,16 +317,20 @@ def conv2d_shape(input_dims: Sequence[int], weight_dims: Sequence[int],
 
 def conv2d(x, w, options: Conv2dOptions = Conv2dOptions()):
     """NCHW cross-correlation with weights [out, in/groups, kh, kw]."""
-    import torch
     out_dims = conv2d_shape(x.shape, w.shape, options)
     out = _empty(out_dims, x.dtype, x.device)
+    conv2d_into(x, w, out, options)
+    return out
+
+
+def conv2d_into(x, w, out, options: Conv2dOptions = Conv2dOptions()) -> None:
+    """``conv2d`` written into an existing C-contiguous device tensor."""
     fn = _fn("kx_conv2d", x.dtype)
     h = _bind(x)
     err = KxError()
     o = options.to_c()
     dx, dw, do = _descriptor(x), _descriptor(w), _descriptor(out)
     raise_for(fn(h.ptr, C.byref(dx), C.byref(dw), C.byref(o), C.byref(do), C.byref(err)), err)
-    return out
 
 
 def conv2d_reference(x, w, options: Conv2dOptions = Conv2dOptions()):
@@ -342,14 +346,18 @@ def conv2d_reference(x, w, options: Conv2dOptions = Conv2dOptions()):
 def softmax_temperature(src, axis: int, temperature: float):
     """Softmax of ``(x - max) / temperature`` along ``axis`` (negative axes
     count from the end).  Nonfinite input raises NonFiniteInput."""
-    import torch
     out = _empty(tuple(src.shape), src.dtype, src.device)
+    softmax_temperature_into(src, axis, temperature, out)
+    return out
+
+
+def softmax_temperature_into(src, axis: int, temperature: float, out) -> None:
+    """``softmax_temperature`` written into an existing C-contiguous tensor."""
     fn = _fn("kx_softmax_temperature", src.dtype)
     h = _bind(src)
     err = KxError()
     ds, do = _descriptor(src), _descriptor(out)
     raise_for(fn(h.ptr, C.byref(ds), int(axis), float(temperature), C.byref(do), C.byref(err)), err)
-    return out
 
 
 # ---------------------------------------------------------------------------

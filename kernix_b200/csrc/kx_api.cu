@@ -1,6 +1,7 @@
 // C-ABI entry points: handles, device buffers, shape planning, matmul and the
 // MatmulElement-style host-buffer hooks.  All validation happens on the host
 // before any device work, so a rejected call writes nothing.
+#include <algorithm>
 #include <cstring>
 #include <new>
 
@@ -156,6 +157,91 @@ int matmul_device(kx_handle *hh, const kx_tensor *a, const kx_tensor *b, const k
     return KX_OK;
 }
 
+// Pipelined host-buffer GEMM for A with disjoint rows (positive row stride
+// larger than the row's reach): B goes up first, then A in row pieces on a
+// copy stream; piece i multiplies while piece i+1 uploads and piece i-1's rows
+// of C download on a third stream, so both PCIe directions and the GEMM
+// overlap.  Same staging layout as the one-shot path.
+template <typename T>
+int hook_gemm_pipelined(Handle *h, const T *a_host, uint64_t a_start, uint64_t a_count, uint64_t a_origin,
+                        int64_t a_rs, int64_t a_cs, const T *b_host, uint64_t b_start, uint64_t b_count,
+                        uint64_t b_origin, int64_t b_rs, int64_t b_cs, T *out, uint64_t m, uint64_t k, uint64_t n,
+                        T *da, T *db, T *dc, int pieces) {
+    cudaError_t ce = cudaSuccess;
+    if (!h->h2d) ce = cudaStreamCreateWithFlags(&h->h2d, cudaStreamNonBlocking);
+    if (ce == cudaSuccess && !h->d2h) ce = cudaStreamCreateWithFlags(&h->d2h, cudaStreamNonBlocking);
+    for (int i = 0; ce == cudaSuccess && i < 3 * pieces + 2; ++i)
+        if (!h->ev[i]) ce = cudaEventCreateWithFlags(&h->ev[i], cudaEventDisableTiming);
+    if (ce != cudaSuccess) return h->cuda_fail(ce);
+    cudaEvent_t start = h->ev[0], b_up = h->ev[1];
+    cudaEvent_t *a_up = h->ev + 2, *c_done = h->ev + 2 + pieces, *c_down = h->ev + 2 + 2 * pieces;
+    const uint64_t rows = (m + pieces - 1) / pieces;
+    // staging is free once earlier work on the handle's stream is done
+    ce = cudaEventRecord(start, h->stream);
+    if (ce == cudaSuccess) ce = cudaStreamWaitEvent(h->h2d, start, 0);
+    if (ce == cudaSuccess) ce = cudaStreamWaitEvent(h->d2h, start, 0);
+    if (ce == cudaSuccess)
+        ce = cudaMemcpyAsync(db, b_host + b_start, b_count * sizeof(T), cudaMemcpyHostToDevice, h->h2d);
+    if (ce == cudaSuccess) ce = cudaEventRecord(b_up, h->h2d);
+    for (int i = 0; ce == cudaSuccess && i < pieces; ++i) {
+        const uint64_t r0 = i * rows, r1 = std::min<uint64_t>(m, r0 + rows);
+        if (r0 >= r1) break;
+        const uint64_t s0 = a_origin + r0 * (uint64_t)a_rs;
+        const uint64_t s1 = a_origin + (r1 - 1) * (uint64_t)a_rs + (k - 1) * (uint64_t)a_cs + 1;
+        ce = cudaMemcpyAsync(da + (s0 - a_start), a_host + s0, (s1 - s0) * sizeof(T), cudaMemcpyHostToDevice,
+                             h->h2d);
+        if (ce == cudaSuccess) ce = cudaEventRecord(a_up[i], h->h2d);
+    }
+    if (ce == cudaSuccess) ce = cudaStreamWaitEvent(h->stream, b_up, 0);
+    if (ce != cudaSuccess) return h->cuda_fail(ce);
+    int rc = KX_OK;
+    const char *name = "none";
+    int last = -1;
+    for (int i = 0; i < pieces; ++i) {
+        const uint64_t r0 = i * rows, r1 = std::min<uint64_t>(m, r0 + rows);
+        if (r0 >= r1) break;
+        ce = cudaStreamWaitEvent(h->stream, a_up[i], 0);
+        if (ce != cudaSuccess) return h->cuda_fail(ce);
+        GemmParams<T> p;
+        std::memset(&p, 0, sizeof(p));
+        p.A = da + (a_origin - a_start) + r0 * (uint64_t)a_rs;
+        p.B = db + (b_origin - b_start);
+        p.C = dc + r0 * n;
+        p.a_rs = (r1 - r0) == 1 ? 0 : a_rs;
+        p.a_cs = k == 1 ? 0 : a_cs;
+        p.b_rs = k == 1 ? 0 : b_rs;
+        p.b_cs = n == 1 ? 0 : b_cs;
+        p.c_rs = (int64_t)n;
+        p.c_cs = 1;
+        p.M = (int)(r1 - r0);
+        p.N = (int)n;
+        p.K = (int)k;
+        p.nbatch = 1;
+        p.splits = 1;
+        p.k_per_split = (int)k;
+        rc = run_gemm<T>(h, p, &name);
+        if (rc) break;
+        ce = cudaEventRecord(c_done[i], h->stream);
+        if (ce == cudaSuccess) ce = cudaStreamWaitEvent(h->d2h, c_done[i], 0);
+        if (ce == cudaSuccess)
+            ce = cudaMemcpyAsync(out + r0 * n, dc + r0 * n, (r1 - r0) * n * sizeof(T), cudaMemcpyDeviceToHost,
+                                 h->d2h);
+        if (ce == cudaSuccess) ce = cudaEventRecord(c_down[i], h->d2h);
+        if (ce != cudaSuccess) return h->cuda_fail(ce);
+        last = i;
+    }
+    h->last_kernel = name;
+    // the call returns once the last rows are on the host; later work on the
+    // handle's stream is ordered after the downloads
+    if (last >= 0) {
+        ce = cudaStreamWaitEvent(h->stream, c_down[last], 0);
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(h->d2h);
+    }
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(h->stream);
+    if (ce != cudaSuccess) return h->cuda_fail(ce);
+    return rc;
+}
+
 // Host-buffer GEMM used by both hooks: copy the reachable spans to device
 // staging, run, copy the C-order product back.  a_start/b_start are the first
 // reachable elements; the GEMM reads A at a_dev + (origin - start).
@@ -174,6 +260,14 @@ int hook_gemm(Handle *h, const T *a_host, uint64_t a_start, uint64_t a_count, ui
     T *da = static_cast<T *>(h->stage[0]);
     T *db = static_cast<T *>(h->stage[1]);
     T *dc = static_cast<T *>(h->stage[2]);
+    // Large products with disjoint A rows: overlap the transfers with the GEMM.
+    const uint64_t flops = 2 * m * n * k;
+    const bool disjoint_rows = a_rs > 0 && a_cs >= 0 && (uint64_t)a_cs * (k - 1) < (uint64_t)a_rs;
+    if (disjoint_rows && m >= 1024 && flops >= (1ull << 34)) {
+        const int pieces = (int)std::min<uint64_t>(8, m / 512);
+        return hook_gemm_pipelined<T>(h, a_host, a_start, a_count, a_origin, a_rs, a_cs, b_host, b_start, b_count,
+                                      b_origin, b_rs, b_cs, out, m, k, n, da, db, dc, pieces);
+    }
     cudaError_t ce = cudaMemcpyAsync(da, a_host + a_start, a_count * sizeof(T), cudaMemcpyHostToDevice, h->stream);
     if (ce == cudaSuccess)
         ce = cudaMemcpyAsync(db, b_host + b_start, b_count * sizeof(T), cudaMemcpyHostToDevice, h->stream);
@@ -312,9 +406,15 @@ int kx_destroy(kx_handle *hh) {
         DeviceGuard g(h.device);
         if (h.stream) cudaStreamSynchronize(h.stream);
         else cudaDeviceSynchronize();
+        if (h.h2d) cudaStreamSynchronize(h.h2d);
+        if (h.d2h) cudaStreamSynchronize(h.d2h);
         cudaFree(h.ws);
         for (auto &s : h.stage) cudaFree(s);
         cudaFree(h.flags);
+        for (auto &e : h.ev)
+            if (e) cudaEventDestroy(e);
+        if (h.h2d) cudaStreamDestroy(h.h2d);
+        if (h.d2h) cudaStreamDestroy(h.d2h);
     }
     delete hh;
     return KX_OK;

@@ -6,7 +6,7 @@
 // ~1.7e-6 |a b| (see tf32_trunc below), inside the f32 bound the reference's
 // tests use, |x - y| <= 2e-6 sum|a b| (small_matmul_tests.rs:153-186).
 //
-// Pipeline per CTA (one 128 x BN output tile, BN = 256 or 224, 384 threads):
+// Pipeline per CTA (one 128 x BN output tile, BN = 256, 224 or 128, 384 threads):
 //   warp 0       TMA producer: raw f32 tiles of A and B into stage s (k depth 16)
 //   warp 1       TMEM owner and MMA issuer: 3 x 2 tcgen05.mma (kind::tf32) per stage
 //   warps 4..11  workers: write lo beside each raw tile (the raw tile is hi);
@@ -46,9 +46,10 @@ constexpr int KC = 64;                                // k-tiles (1024 k) per hi
 constexpr uint32_t TMEM_COLS = 512;   // main (hi*hi) + cross (hi*lo + lo*hi) accumulators
 constexpr uint32_t XCOL = 256;        // first TMEM column of the cross-term accumulator
 
-// Tile width N: 256, or 224 when it packs the tiles into fewer full waves of
-// SMs (e.g. 512 x 8192 outputs: 148 tiles of 128 x 224 = one wave, against
-// 128 tiles of 128 x 256 leaving 20 SMs idle).
+// Tile width N: 256; 224 when it packs the tiles into fewer full waves of SMs
+// (e.g. 512 x 8192 outputs: 148 tiles of 128 x 224 = one wave, against 128
+// tiles of 128 x 256 leaving 20 SMs idle); 128 for narrow products (N = 128:
+// the attention value product) that would leave most of a wider tile empty.
 template <int BN> struct TileN {
     static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "tile width");
     static constexpr int B_TILE = BN * BK * 4;                   // 16 KB at 256
@@ -552,7 +553,10 @@ int pick_bn(int64_t m, int64_t n, int64_t nbatch, int sm_count) {
         const int64_t tiles = tm * ((n + bn - 1) / bn) * nbatch;
         return ((tiles + sm_count - 1) / sm_count) * (int64_t)(bn + 32);
     };
-    return cost(224) < cost(256) ? 224 : 256;
+    int best = 256;
+    for (int bn : {224, 128})
+        if (cost(bn) < cost(best)) best = bn;
+    return best;
 }
 
 template <bool B_MN, int BN>
@@ -618,11 +622,15 @@ int run_gemm_tc(Handle *h, const GemmParams<float> &p, const char **kernel_name)
     tp.status = h->flags + kStatusWord;
     cudaError_t ce;
     if (b_mn) {
-        ce = bn == 224 ? launch_tc<true, 224>(h, ma, mb, tp, nb) : launch_tc<true, 256>(h, ma, mb, tp, nb);
-        *kernel_name = bn == 224 ? "tc_3xtf32_128x224_bmn" : "tc_3xtf32_128x256_bmn";
+        ce = bn == 224   ? launch_tc<true, 224>(h, ma, mb, tp, nb)
+             : bn == 128 ? launch_tc<true, 128>(h, ma, mb, tp, nb)
+                         : launch_tc<true, 256>(h, ma, mb, tp, nb);
+        *kernel_name = bn == 224 ? "tc_3xtf32_128x224_bmn" : bn == 128 ? "tc_3xtf32_128x128_bmn" : "tc_3xtf32_128x256_bmn";
     } else {
-        ce = bn == 224 ? launch_tc<false, 224>(h, ma, mb, tp, nb) : launch_tc<false, 256>(h, ma, mb, tp, nb);
-        *kernel_name = bn == 224 ? "tc_3xtf32_128x224_bk" : "tc_3xtf32_128x256_bk";
+        ce = bn == 224   ? launch_tc<false, 224>(h, ma, mb, tp, nb)
+             : bn == 128 ? launch_tc<false, 128>(h, ma, mb, tp, nb)
+                         : launch_tc<false, 256>(h, ma, mb, tp, nb);
+        *kernel_name = bn == 224 ? "tc_3xtf32_128x224_bk" : bn == 128 ? "tc_3xtf32_128x128_bk" : "tc_3xtf32_128x256_bk";
     }
     ++h->launches;
     return ce == cudaSuccess ? KX_OK : h->cuda_fail(ce);

@@ -29,6 +29,10 @@ struct Handle {
     uint64_t stage_bytes[3] = {0, 0, 0};
     uint32_t *flags = nullptr;   // device status words (nonfinite index, timeouts)
     static constexpr int kFlagWords = 64;
+    // Host-hook pipeline: copy streams and per-piece events, created on first use.
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    static constexpr int kMaxPieces = 16;
+    cudaEvent_t ev[3 * kMaxPieces + 2] = {};
 
     int cuda_fail(cudaError_t ce) {
         last_cuda_error = (int)ce;

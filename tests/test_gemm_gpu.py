@@ -276,3 +276,33 @@ def test_layout_modes_and_kernel_families(kx, torch_cuda):
             g = got.cpu().numpy().astype(np.float64)
             assert (np.abs(g - exp) <= 2e-6 * ab + 1e-30).all(), (name, m, k, n)
     assert {"simt_128x128", "simt_64x64_splitk"} <= seen or {"simt_128x128", "simt_64x64"} <= seen, seen
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_strided_hook_pipelined_large(kx, dtype):
+    """try_strided_matmul on a product large enough for the pipelined host
+    path (row pieces uploaded, multiplied and downloaded on three streams):
+    A a row-strided slice of a wider buffer (disjoint rows), as in the 8192^3
+    workload, checked row by row against the compensated oracle and against
+    the one-shot device result."""
+    import torch
+    m, k, n, pitch = 4096, 1536, 1536, 1600
+    rng = np.random.default_rng(3)
+    abuf = rng.uniform(-1, 1, (m, pitch)).astype(dtype)
+    bbuf = rng.uniform(-1, 1, (k, n)).astype(dtype)
+    out = np.full(m * n, np.nan, dtype=dtype)
+    ma = kx.MatrixInput(abuf.reshape(-1), [m, k], [pitch, 1], 0)
+    mb = kx.MatrixInput(bbuf.reshape(-1), [k, n], [n, 1], 0)
+    assert kx.try_strided_matmul(ma, mb, out)
+    got = out.reshape(m, n)
+    assert np.isfinite(got).all()
+    bound = 2e-6 if dtype == np.float32 else 1e-13
+    for r in (0, 1, 511, 512, 1023, 2048, 4095):
+        exp, ab = oracle.gemm_dot2(oracle.View(abuf, (1, k), (pitch, 1), r * pitch), oracle.View.of(bbuf))
+        assert (np.abs(got[r].astype(np.float64) - exp[0]) <= bound * ab[0]).all(), r
+    dev = kx.matmul(kx.TensorView(torch.from_numpy(abuf.reshape(-1)).cuda(), (m, k), (pitch, 1), 0),
+                    torch.from_numpy(bbuf).cuda()).cpu().numpy()
+    # the pieces may take another kernel family than the one-shot call
+    # (fewer tiles per launch), so the two agree within twice the bound
+    ref = np.abs(bbuf).sum(axis=0)[None, :] * np.abs(abuf[:, :k]).max(axis=1)[:, None]
+    assert (np.abs(got.astype(np.float64) - dev) <= 2 * bound * ref).all()

@@ -54,11 +54,13 @@ def test_tc_2d_layouts(kx, torch_cuda, tc_handle, m, k, n, b_layout):
     _check(got, va, vb)
 
 
-@pytest.mark.parametrize("m,k,n", [(512, 96, 8192), (520, 1040, 1000)])
+@pytest.mark.parametrize("m,k,n,width", [(512, 96, 8192, "128x224"), (520, 1040, 1000, "128x128"),
+                                         (4096, 64, 8192, "128x256"), (1024, 200, 128, "128x128")])
 @pytest.mark.parametrize("b_layout", ["row", "col"])
-def test_tc_224_wide_tiles(kx, torch_cuda, tc_handle, m, k, n, b_layout):
-    """Shapes whose tile count packs into whole waves with 128 x 224 tiles
-    (ragged last column tile included) against the compensated oracle."""
+def test_tc_tile_widths(kx, torch_cuda, tc_handle, m, k, n, width, b_layout):
+    """Each tile width the wave model picks (224: packs into whole waves, 128:
+    narrow products, 256: the rest), ragged last column tiles included,
+    against the compensated oracle."""
     rng = np.random.default_rng(m + n + k)
     abuf = rng.uniform(-1, 1, (m, k)).astype(np.float32)
     if b_layout == "row":
@@ -69,7 +71,7 @@ def test_tc_224_wide_tiles(kx, torch_cuda, tc_handle, m, k, n, b_layout):
         vb = oracle.View(bbuf, (k, n), (1, k))
     got = kx.matmul(_view(kx, torch_cuda, abuf, (m, k), (k, 1)),
                     _view(kx, torch_cuda, bbuf, vb.dims, vb.strides)).cpu().numpy()
-    assert "128x224" in tc_handle.last_kernel, tc_handle.last_kernel
+    assert width in tc_handle.last_kernel, tc_handle.last_kernel
     tc_handle.synchronize()
     rows = np.r_[0:3, m // 2, m - 2:m]
     _check(got[rows], oracle.View(abuf[rows].copy(), (len(rows), k), (k, 1)), vb)
@@ -96,7 +98,7 @@ def test_tc_batched_and_broadcast(kx, torch_cuda, tc_handle):
     tc_handle.synchronize()
 
 
-@pytest.mark.parametrize("m,n,width", [(128, 256, "128x224"), (4096, 8192, "128x256")])
+@pytest.mark.parametrize("m,n,width", [(128, 256, "128x128"), (512, 8192, "128x224"), (4096, 8192, "128x256")])
 def test_tc_nonfinite_keeps_ieee_propagation(kx, torch_cuda, tc_handle, m, n, width):
     """An inf in A must give inf (not NaN from inf * 0 in a cross term)."""
     torch = torch_cuda
