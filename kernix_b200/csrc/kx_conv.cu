@@ -14,6 +14,7 @@
 // and, only when it is set, a direct kernel recomputes the output in the
 // scalar path's order, so 0*inf never reaches the result.
 #include <cstring>
+#include <type_traits>
 
 #include "gemm_simt.cuh"
 #include "kx_internal.hpp"
@@ -359,7 +360,27 @@ int conv_impl(kx_handle *hh, const kx_tensor *in, const kx_tensor *wt, const kx_
             ++h->launches;
         }
     }
-    if (ce == cudaSuccess) {
+    bool done = false;
+    if constexpr (std::is_same<T, float>::value) {
+        // Tensor cores for the split-TF32 implicit GEMM when the tiles cover
+        // the SMs (or the handle asks for it); the SIMT kernel otherwise.
+        const int64_t tc_tiles = ((g.cog + 127) / 128) * ((g.ncols + 127) / 128) * g.groups;
+        if (ce == cudaSuccess && h->f32_variant != KX_F32_FFMA &&
+            (h->f32_variant == KX_F32_3XTF32 || tc_tiles >= h->sm_count / 2)) {
+            int64_t ws[4] = {g.ws[0], g.ws[1], g.ws[2], g.ws[3]};
+            if (g.co == 1) ws[0] = (g.kk + 3) / 4 * 4;   // a single row: any aligned pitch
+            const char *name = "none";
+            const int rc = run_conv_tc(h, xp, g.xs, wp, ws, yp, g.n, g.c, g.h, g.w, g.co, g.cg, g.kh, g.kw, g.oh,
+                                       g.ow, g.groups, g.sy, g.sx, g.py, g.px, g.dy, g.dx, &name);
+            if (rc == KX_OK) {
+                h->last_kernel = name;
+                done = true;
+            } else if (rc != KX_DECLINED) {
+                ce = (cudaError_t)h->last_cuda_error;
+            }
+        }
+    }
+    if (ce == cudaSuccess && !done) {
         const int64_t big = ((g.cog + 127) / 128) * ((g.ncols + 127) / 128) * g.groups;
         if (big >= 2LL * h->sm_count) {
             ce = launch_igemm<T, ConvCfg<T>>(h, xp, wp, yp, g);

@@ -1,0 +1,441 @@
+// conv2d on the 5th-generation tensor cores: split-TF32 implicit GEMM whose
+// B operand (the im2col columns) is gathered straight from the NCHW input by
+// the worker warps, so no column buffer ever exists.
+//
+// GEMM view (kernix-ops neural.rs:200-302, conv_impl's native branch): per
+// group, out[co][(img,oy,ox)] = sum_k weight[co][k] * col[k][(img,oy,ox)] with
+// k = (ci, ky, kx) in the reference's im2col order and col[k][pixel] the
+// input element under tap k, zero on padding.  M = output channels of the
+// group, N = batch * oh * ow pixels, K = cin/groups * kh * kw.
+//
+// Per CTA: 128 output channels x 128 pixels, 384 threads.
+//   warp 0       TMA producer: the weight tile (K-major, 64-byte swizzle)
+//   warp 1       TMEM owner and MMA issuer (3 x 2 tcgen05.mma kind::tf32 per stage)
+//   warps 4..11  workers: gather the B tile for stage s (one pixel and 8 taps
+//                per thread, loads for stage s+1 issued before stage s is
+//                written), write its hi (raw) and lo parts in the canonical
+//                K-major no-swizzle layout, split the weight tile's lo part,
+//                fold hi*hi chunks into registers, and store the NCHW output
+// A per-CTA table of (ci, ky, kx) offsets in shared memory turns each tap into
+// one add and two bounds checks.  Split-TF32 arithmetic, chunked folding and
+// the nonfinite fallback are those of the GEMM kernel (kx_gemm_tc.cu): with
+// inf/NaN in a tile's inputs the tile is recomputed with f32 FMA in k order,
+// as the SIMT implicit GEMM does.  Every mbarrier wait is bounded.
+#include <cstring>
+
+#include "gemm_simt.cuh"
+#include "tc_common.cuh"
+
+namespace kx {
+namespace tc {
+namespace conv {
+
+constexpr int BN = 128;                                   // pixels per tile
+constexpr int B_TILE = BN * BK * 4;                       // 8 KB
+constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;      // 32 KB
+constexpr int HALF_COLS = BN / 2;                         // 64 columns per worker thread
+constexpr int MAX_TAPS = 3072;                            // table capacity (K extent)
+constexpr int TABLE_BYTES = MAX_TAPS * 16;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + TABLE_BYTES + 1024;
+
+struct Params {
+    const float *x;       // input at its origin
+    const float *w;       // weights at their origin (used by the nonfinite fallback)
+    float *y;             // output at its origin, C-contiguous NCHW
+    int64_t xs[4];        // input strides (elements)
+    int64_t ws0;          // weight stride between output channels; taps are contiguous
+    int64_t ih, iw, oh, ow, hw;
+    int64_t co_total, cog, cg;
+    int kh, kw, sy, sx, py, px, dy, dx;
+    int kk;               // cg * kh * kw
+    int64_t ncols;        // batch * oh * ow
+    uint32_t *status;
+};
+
+struct Tap {
+    int64_t x_off;        // ci*xs1 + ky*dy*xs2 + kx*dx*xs3
+    int32_t ry, rx;       // ky*dy, kx*dx
+};
+
+// Offset of element (row r, k) of a 128 x 16 K-major tile in the canonical
+// no-swizzle layout: 8x4 core matrices of 128 contiguous bytes, the four along
+// k adjacent (LBO 128 B), row groups 512 B apart (SBO).
+__device__ __forceinline__ uint32_t kmaj_off(int r, int kc) {   // kc = k / 4
+    return (uint32_t)((r >> 3) * 512 + kc * 128 + (r & 7) * 16);
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1)
+conv_3xtf32_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+    uint64_t *conv = full + STAGES;
+    uint64_t *empty = conv + STAGES;
+    uint64_t *chunk_full = empty + STAGES;
+    uint64_t *chunk_empty = chunk_full + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(chunk_empty + 1);
+    Tap *taps = reinterpret_cast<Tap *>(smem + STAGES * STAGE_BYTES + BAR_BYTES);
+    __shared__ int s_fail_storage, s_nonfinite_storage;
+    volatile int &s_fail = s_fail_storage;
+    volatile int &s_nonfinite = s_nonfinite_storage;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_m = (int)((p.cog + BM - 1) / BM), tiles_n = (int)((p.ncols + BN - 1) / BN);
+    int tm, tn;
+    raster(blockIdx.x, tiles_m, tiles_n, 8, tm, tn);
+    const int m0 = tm * BM;
+    const int64_t n0 = (int64_t)tn * BN;
+    const int grp = blockIdx.y;
+    const int ktiles = (p.kk + BK - 1) / BK;
+    const int nchunks = (ktiles + KC - 1) / KC;
+
+    for (int k = threadIdx.x; k < p.kk; k += NTHREADS) {
+        const int khw = p.kh * p.kw;
+        const int ci = k / khw, r = k % khw;
+        const int ky = r / p.kw, kx = r % p.kw;
+        Tap t;
+        t.ry = ky * p.dy;
+        t.rx = kx * p.dx;
+        t.x_off = (int64_t)ci * p.xs[1] + (int64_t)t.ry * p.xs[2] + (int64_t)t.rx * p.xs[3];
+        taps[k] = t;
+    }
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&conv[s], WORK_WARPS);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(chunk_full, 1);
+        mbar_init(chunk_empty, WORK_WARPS);
+        s_fail = 0;
+        s_nonfinite = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    auto stage_a = [&](int s) { return smem + s * STAGE_BYTES; };
+    auto stage_b = [&](int s) { return smem + s * STAGE_BYTES + 2 * A_TILE; };
+
+    if (warp == 0) {
+        // ---- TMA producer: weight tiles ---------------------------------
+        if (lane == 0) {
+            int issued = 0;
+            for (int kt = 0; kt < ktiles && !s_fail; ++kt) {
+                const int s = kt % STAGES;
+                if (kt >= STAGES && !mbar_wait(&empty[s], ((kt / STAGES) - 1) & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                mbar_expect_tx(&full[s], A_TILE);
+                tma_load_3d(stage_a(s), &tmW, kt * BK, m0, grp, &full[s]);
+                issued = kt + 1;
+            }
+            for (int s = 0; s < STAGES && s < issued; ++s) {
+                const int last = s + STAGES * ((issued - 1 - s) / STAGES);
+                mbar_wait(&full[s], (last / STAGES) & 1);
+            }
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer ----------------------------------------------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_tf32<BN>(false);
+            for (int kt = 0; kt < ktiles; ++kt) {
+                const int s = kt % STAGES;
+                const int chunk = kt / KC, kin = kt % KC;
+                if (kin == 0 && chunk > 0 && (s_fail || !mbar_wait(chunk_empty, (chunk - 1) & 1))) {
+                    s_fail = 1;
+                    break;
+                }
+                if (s_fail || !mbar_wait(&conv[s], (kt / STAGES) & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_hi = smem_u32(stage_a(s)), a_lo = a_hi + A_TILE;
+                const uint32_t b_hi = smem_u32(stage_b(s)), b_lo = b_hi + B_TILE;
+#pragma unroll
+                for (int ks = 0; ks < BK / 8; ++ks) {
+                    const uint64_t dah = desc_k_sw64(a_hi + ks * 32), dal = desc_k_sw64(a_lo + ks * 32);
+                    const uint64_t dbh = desc_k_none(b_hi + ks * 256, 128, 512);
+                    const uint64_t dbl = desc_k_none(b_lo + ks * 256, 128, 512);
+                    mma_tf32(tmem, dah, dbh, idesc, (kin > 0 || ks > 0) ? 1u : 0u);
+                    mma_tf32(tmem + XCOL, dah, dbl, idesc, (kt > 0 || ks > 0) ? 1u : 0u);
+                    mma_tf32(tmem + XCOL, dal, dbh, idesc, 1u);
+                }
+                mma_commit(&empty[s]);
+                if (kin == KC - 1 || kt == ktiles - 1) mma_commit(chunk_full);
+            }
+            if (s_fail) mma_commit(chunk_full);
+        }
+    } else if (warp >= WORK_WARP0) {
+        // ---- workers: gather B, split, fold, epilogue --------------------
+        const int wt = threadIdx.x - WORK_WARP0 * 32;           // 0..255
+        const int quarter = warp & 3;
+        const int col0 = ((warp - WORK_WARP0) >> 2) * HALF_COLS;
+        // this thread's pixel (B row) and which 8 of the stage's 16 taps
+        const int prow = wt & (BN - 1);
+        const int khalf = wt >> 7;
+        const int64_t gcol = n0 + prow;
+        const bool col_ok = gcol < p.ncols;
+        int iy0 = 0, ix0 = 0;
+        int64_t xbase = 0;
+        if (col_ok) {
+            const int64_t img = gcol / p.hw, pix = gcol % p.hw;
+            const int64_t oy = pix / p.ow, ox = pix % p.ow;
+            iy0 = (int)(oy * p.sy - p.py);
+            ix0 = (int)(ox * p.sx - p.px);
+            xbase = img * p.xs[0] + (int64_t)grp * p.cg * p.xs[1] + (int64_t)iy0 * p.xs[2] + (int64_t)ix0 * p.xs[3];
+        }
+        const int ih = (int)p.ih, iw = (int)p.iw;
+        float nxt[8];
+        auto gather = [&](int kt) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int k = kt * BK + khalf * 8 + j;
+                float v = 0.0f;
+                if (col_ok && k < p.kk) {
+                    const Tap t = taps[k];
+                    const int iy = iy0 + t.ry, ix = ix0 + t.rx;
+                    if (iy >= 0 && iy < ih && ix >= 0 && ix < iw) v = __ldg(p.x + xbase + t.x_off);
+                }
+                nxt[j] = v;
+            }
+        };
+        float sum[HALF_COLS];
+#pragma unroll
+        for (int j = 0; j < HALF_COLS; ++j) sum[j] = 0.0f;
+        gather(0);
+        int chunk = 0;
+        for (int kt = 0; kt < ktiles; ++kt) {
+            const int s = kt % STAGES;
+            float cur[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+            if (kt + 1 < ktiles) gather(kt + 1);    // in flight while this stage is written
+            if (s_fail || !mbar_wait(&full[s], (kt / STAGES) & 1)) {
+                s_fail = 1;
+                break;
+            }
+            uint32_t bad = 0;
+            uint8_t *bh = stage_b(s), *bl = bh + B_TILE;
+#pragma unroll
+            for (int jc = 0; jc < 2; ++jc) {
+                float4 v = make_float4(cur[4 * jc], cur[4 * jc + 1], cur[4 * jc + 2], cur[4 * jc + 3]);
+                float4 l;
+                l.x = v.x - tf32_trunc(v.x);
+                l.y = v.y - tf32_trunc(v.y);
+                l.z = v.z - tf32_trunc(v.z);
+                l.w = v.w - tf32_trunc(v.w);
+                bad |= nonfinite_bits(v.x) | nonfinite_bits(v.y) | nonfinite_bits(v.z) | nonfinite_bits(v.w);
+                const uint32_t off = kmaj_off(prow, khalf * 2 + jc);
+                *reinterpret_cast<float4 *>(bh + off) = v;
+                *reinterpret_cast<float4 *>(bl + off) = l;
+            }
+            // weight tile: 512 16-byte chunks, two per thread, lo beside hi
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                float4 *hp = reinterpret_cast<float4 *>(stage_a(s) + (wt + j * WORK_THREADS) * 16);
+                float4 *lp = reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(hp) + A_TILE);
+                const float4 v = *hp;
+                float4 l;
+                l.x = v.x - tf32_trunc(v.x);
+                l.y = v.y - tf32_trunc(v.y);
+                l.z = v.z - tf32_trunc(v.z);
+                l.w = v.w - tf32_trunc(v.w);
+                bad |= nonfinite_bits(v.x) | nonfinite_bits(v.y) | nonfinite_bits(v.z) | nonfinite_bits(v.w);
+                *lp = l;
+            }
+            if (bad) s_nonfinite = 1;
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&conv[s]);
+            if (kt % KC == KC - 1 || kt == ktiles - 1) {
+                if (!mbar_wait(chunk_full, chunk & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                if (s_fail) break;
+                tmem_accumulate(tmem, quarter, col0, sum);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(chunk_empty);
+                ++chunk;
+            }
+        }
+        // ---- epilogue: row = output channel, columns = pixels -----------
+        const int co = m0 + quarter * 32 + lane;
+        const bool row_ok = co < p.cog;
+        const int64_t co_abs = (int64_t)grp * p.cog + co;
+        if (!s_fail && chunk == nchunks) {
+            if (s_nonfinite) {
+                // inf/NaN among this tile's inputs: f32 FMA in k order
+                if (row_ok) {
+                    const float *wrow = p.w + co_abs * p.ws0;
+                    for (int j = 0; j < HALF_COLS; ++j) {
+                        const int64_t c = n0 + col0 + j;
+                        if (c >= p.ncols) break;
+                        const int64_t img = c / p.hw, pix = c % p.hw;
+                        const int64_t oy = pix / p.ow, ox = pix % p.ow;
+                        const int y0 = (int)(oy * p.sy - p.py), x0 = (int)(ox * p.sx - p.px);
+                        const int64_t base = img * p.xs[0] + (int64_t)grp * p.cg * p.xs[1] + (int64_t)y0 * p.xs[2] +
+                                             (int64_t)x0 * p.xs[3];
+                        float acc = 0.0f;
+                        for (int k = 0; k < p.kk; ++k) {
+                            const Tap t = taps[k];
+                            const int iy = y0 + t.ry, ix = x0 + t.rx;
+                            const float xv = (iy >= 0 && iy < ih && ix >= 0 && ix < iw) ? p.x[base + t.x_off] : 0.0f;
+                            acc = fmaf(wrow[k], xv, acc);
+                        }
+                        p.y[(img * p.co_total + co_abs) * p.hw + pix] = acc;
+                    }
+                }
+            } else {
+                const bool vec_ok = (p.hw % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.y) & 15) == 0);
+#pragma unroll
+                for (int c = 0; c < HALF_COLS / 16; ++c) {
+                    uint32_t r[16];
+                    tmem_ld16(tmem + XCOL + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(col0 + c * 16), r);
+                    tmem_wait_ld();
+                    if (!row_ok) continue;
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = sum[c * 16 + j] + __uint_as_float(r[j]);
+                    const int64_t c0 = n0 + col0 + c * 16;
+                    const int64_t img = c0 / p.hw, pix = c0 % p.hw;
+                    if (vec_ok && c0 + 16 <= p.ncols && pix + 16 <= p.hw) {
+                        float *dst = p.y + (img * p.co_total + co_abs) * p.hw + pix;
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4)
+                            *reinterpret_cast<float4 *>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int64_t cc = c0 + j;
+                            if (cc < p.ncols) p.y[((cc / p.hw) * p.co_total + co_abs) * p.hw + cc % p.hw] = v[j];
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+    if (threadIdx.x == 0 && s_fail) atomicOr(p.status, KX_TIMEOUT_FLAG);
+}
+
+// Weights [co][cg][kh][kw] under any strides -> dense rows of `pitch` floats
+// in the reference's tap order (ci, ky, kx), zero beyond the taps: the layout
+// the weight tensor map reads (16-byte aligned rows).
+__global__ void pack_weights_kernel(const float *__restrict__ w, int64_t ws0, int64_t ws1, int64_t ws2, int64_t ws3,
+                                    int64_t co, int kh, int kw, int kk, int pitch, float *__restrict__ out) {
+    const int64_t total = co * pitch;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t o = e / pitch;
+        const int k = (int)(e % pitch);
+        float v = 0.0f;
+        if (k < kk) {
+            const int khw = kh * kw;
+            const int ci = k / khw, r = k % khw;
+            v = w[o * ws0 + ci * ws1 + (r / kw) * ws2 + (r % kw) * ws3];
+        }
+        out[e] = v;
+    }
+}
+
+}  // namespace conv
+}  // namespace tc
+
+// The tensor-core conv reads each group's weights as dense [cog, cg*kh*kw]
+// rows with 16-byte aligned pitch (repacked into the handle's workspace when
+// the caller's layout is not that), at least one k-tile and at most MAX_TAPS
+// taps, and geometry whose pixel and tap coordinates fit int32.
+int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, const int64_t *ws, float *y,
+                int64_t n, int64_t c, int64_t ih, int64_t iw, int64_t co, int64_t cg, int64_t kh, int64_t kw,
+                int64_t oh, int64_t ow, int64_t groups, int64_t sy, int64_t sx, int64_t py, int64_t px, int64_t dy,
+                int64_t dx, const char **kernel_name) {
+    using namespace tc;
+    using namespace tc::conv;
+    (void)c;
+    const int64_t kk = cg * kh * kw;
+    const int64_t cog = co / groups;
+    if (kk < 16 || kk > MAX_TAPS) return KX_DECLINED;
+    if (groups > 65535) return KX_DECLINED;
+    const bool taps_dense = (kw == 1 || ws[3] == 1) && (kh == 1 || ws[2] == kw) && (cg == 1 || ws[1] == kh * kw);
+    int64_t w_pitch = ws[0];
+    if (!taps_dense || ws[0] < kk || (ws[0] * 4) % 16 || (reinterpret_cast<uintptr_t>(w) & 15)) {
+        // repack into dense, 16-byte aligned tap rows in the handle's workspace
+        const int pitch = (int)((kk + 3) / 4 * 4);
+        void *buf = nullptr;
+        int rc = h->workspace((uint64_t)co * pitch * sizeof(float), &buf);
+        if (rc) return rc;
+        int64_t blocks = (co * pitch + 255) / 256;
+        if (blocks > 4LL * h->sm_count) blocks = 4LL * h->sm_count;
+        pack_weights_kernel<<<(unsigned)blocks, 256, 0, h->stream>>>(w, ws[0], ws[1], ws[2], ws[3], co, (int)kh,
+                                                                      (int)kw, (int)kk, pitch,
+                                                                      static_cast<float *>(buf));
+        ++h->launches;
+        cudaError_t ce = cudaGetLastError();
+        if (ce != cudaSuccess) return h->cuda_fail(ce);
+        w = static_cast<const float *>(buf);
+        w_pitch = pitch;
+    }
+    const int64_t ncols = n * oh * ow;
+    const int64_t tiles = ((cog + BM - 1) / BM) * ((ncols + BN - 1) / BN);
+    if (tiles > INT32_MAX) return KX_DECLINED;
+    CUtensorMap mw;
+    if (!make_map(&mw, w, (uint64_t)kk, (uint64_t)cog, (uint64_t)groups, (uint64_t)w_pitch * 4,
+                  (uint64_t)(w_pitch * cog) * 4, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B))
+        return KX_DECLINED;
+    Params p;
+    std::memset(&p, 0, sizeof(p));
+    p.x = x;
+    p.w = w;
+    p.y = y;
+    for (int i = 0; i < 4; ++i) p.xs[i] = xs[i];
+    p.ws0 = w_pitch;
+    p.ih = ih;
+    p.iw = iw;
+    p.oh = oh;
+    p.ow = ow;
+    p.hw = oh * ow;
+    p.co_total = co;
+    p.cog = cog;
+    p.cg = cg;
+    p.kh = (int)kh;
+    p.kw = (int)kw;
+    p.sy = (int)sy;
+    p.sx = (int)sx;
+    p.py = (int)py;
+    p.px = (int)px;
+    p.dy = (int)dy;
+    p.dx = (int)dx;
+    p.kk = (int)kk;
+    p.ncols = ncols;
+    p.status = h->flags + kStatusWord;
+    auto k = conv_3xtf32_kernel;
+    cudaError_t ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (ce == cudaSuccess) {
+        dim3 grid((unsigned)tiles, (unsigned)groups, 1);
+        k<<<grid, NTHREADS, SMEM_BYTES, h->stream>>>(mw, p);
+        ce = cudaGetLastError();
+    }
+    *kernel_name = "conv_tc_3xtf32_128x128";
+    ++h->launches;
+    return ce == cudaSuccess ? KX_OK : h->cuda_fail(ce);
+}
+
+}  // namespace kx

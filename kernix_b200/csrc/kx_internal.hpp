@@ -92,6 +92,13 @@ template <typename T> int run_gemm(Handle *h, GemmParams<T> p, const char **kern
 // cannot describe the operands (the caller then uses the SIMT kernel).
 bool tc_eligible(const GemmParams<float> &p);
 int run_gemm_tc(Handle *h, const GemmParams<float> &p, const char **kernel_name);
+// conv2d as a split-TF32 implicit GEMM on the tensor cores (kx_conv_tc.cu);
+// strides of x and w in elements (singleton dims zero).  KX_DECLINED when the
+// weights are not dense tap rows or the tap count is outside its table.
+int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, const int64_t *ws, float *y,
+                int64_t n, int64_t c, int64_t ih, int64_t iw, int64_t co, int64_t cg, int64_t kh, int64_t kw,
+                int64_t oh, int64_t ow, int64_t groups, int64_t sy, int64_t sx, int64_t py, int64_t px, int64_t dy,
+                int64_t dx, const char **kernel_name);
 // f64 on the FP64 tensor pipe (kx_gemm_f64.cu).  KX_DECLINED for layouts
 // without a unit stride along k or m/n (the SIMT DFMA kernel takes those).
 int run_gemm_dmma(Handle *h, const GemmParams<double> &p, const char **kernel_name);
