@@ -16,8 +16,9 @@
 //                written), write its hi (raw) and lo parts in the canonical
 //                K-major no-swizzle layout, split the weight tile's lo part,
 //                fold hi*hi chunks into registers, and store the NCHW output
-// A per-CTA table of (ci, ky, kx) offsets in shared memory turns each tap into
-// one add and two bounds checks.  Split-TF32 arithmetic, chunked folding and
+// A per-CTA table of (ci, ky, kx) offsets in shared memory and a per-pixel
+// mask of in-bounds taps turn each gathered element into one table read, one
+// bit test and one 4-byte cp.async (zero-filled on padding).  Split-TF32 arithmetic, chunked folding and
 // the nonfinite fallback are those of the GEMM kernel (kx_gemm_tc.cu): with
 // inf/NaN in a tile's inputs the tile is recomputed with f32 FMA in k order,
 // as the SIMT implicit GEMM does.  Every mbarrier wait is bounded.
@@ -30,13 +31,19 @@ namespace kx {
 namespace tc {
 namespace conv {
 
-constexpr int BN = 128;                                   // pixels per tile
-constexpr int B_TILE = BN * BK * 4;                       // 8 KB
-constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;      // 32 KB
-constexpr int HALF_COLS = BN / 2;                         // 64 columns per worker thread
-constexpr int MAX_TAPS = 3072;                            // table capacity (K extent)
-constexpr int TABLE_BYTES = MAX_TAPS * 16;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + TABLE_BYTES + 1024;
+// Pixels per tile: 256, or 128 when that packs the tiles into fewer waves.
+template <int BN> struct Tile {
+    static constexpr int B_TILE = BN * BK * 4;                   // 16 KB at 256
+    static constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 48 KB at 256
+    static constexpr int HALF_COLS = BN / 2;                     // columns per worker thread
+    // Stage ring: the gather for k-tile kt + LOOKAHEAD goes into the stage of
+    // k-tile kt + LOOKAHEAD - NST, so LOOKAHEAD stages cover the gather latency
+    // and NST - LOOKAHEAD MMA groups may be in flight when a worker reuses a stage.
+    static constexpr int NST = BN == 128 ? 6 : 4;
+    static constexpr int LOOKAHEAD = NST / 2;
+    static constexpr int FIXED_SMEM = NST * STAGE_BYTES + BAR_BYTES + 1024;
+};
+constexpr int SMEM_LIMIT = 227 * 1024;
 
 struct Params {
     const float *x;       // input at its origin
@@ -54,27 +61,39 @@ struct Params {
 
 struct Tap {
     int64_t x_off;        // ci*xs1 + ky*dy*xs2 + kx*dx*xs3
-    int32_t ry, rx;       // ky*dy, kx*dx
+    int32_t r;            // ky*kw + kx: bit of the pixel's in-bounds mask; 63 past the last tap
+    int32_t unused;
 };
+constexpr int PAD_TAP = 63;
 
-// Offset of element (row r, k) of a 128 x 16 K-major tile in the canonical
-// no-swizzle layout: 8x4 core matrices of 128 contiguous bytes, the four along
-// k adjacent (LBO 128 B), row groups 512 B apart (SBO).
-__device__ __forceinline__ uint32_t kmaj_off(int r, int kc) {   // kc = k / 4
-    return (uint32_t)((r >> 3) * 512 + kc * 128 + (r & 7) * 16);
+// B tiles (BN pixels x 16 taps) use the canonical K-major no-swizzle layout:
+// 8x4 core matrices of 128 contiguous bytes, the four along k adjacent (LBO
+// 128 B), row groups 512 B apart (SBO); element (r, k) of core matrix
+// 4*(r/8) + k/4 sits at byte 16*(r%8) + 4*(k%4) within it.
+// 4-byte asynchronous copy into shared memory; `valid` false zero-fills
+// (the source is not read).
+__device__ __forceinline__ void cp4(void *dst, const void *src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 4 : 0)
+                 : "memory");
 }
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+template <int BN>
 __global__ void __launch_bounds__(NTHREADS, 1)
 conv_3xtf32_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ Params p) {
+    using TL = Tile<BN>;
+    constexpr int B_TILE = TL::B_TILE, STAGE_BYTES = TL::STAGE_BYTES, HALF_COLS = TL::HALF_COLS;
+    constexpr int NST = TL::NST, LOOKAHEAD = TL::LOOKAHEAD;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
-    uint64_t *conv = full + STAGES;
-    uint64_t *empty = conv + STAGES;
-    uint64_t *chunk_full = empty + STAGES;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + NST * STAGE_BYTES);
+    uint64_t *conv = full + NST;
+    uint64_t *empty = conv + NST;
+    uint64_t *chunk_full = empty + NST;
     uint64_t *chunk_empty = chunk_full + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(chunk_empty + 1);
-    Tap *taps = reinterpret_cast<Tap *>(smem + STAGES * STAGE_BYTES + BAR_BYTES);
+    Tap *taps = reinterpret_cast<Tap *>(smem + NST * STAGE_BYTES + BAR_BYTES);
     __shared__ int s_fail_storage, s_nonfinite_storage;
     volatile int &s_fail = s_fail_storage;
     volatile int &s_nonfinite = s_nonfinite_storage;
@@ -89,18 +108,23 @@ conv_3xtf32_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
     const int ktiles = (p.kk + BK - 1) / BK;
     const int nchunks = (ktiles + KC - 1) / KC;
 
-    for (int k = threadIdx.x; k < p.kk; k += NTHREADS) {
-        const int khw = p.kh * p.kw;
-        const int ci = k / khw, r = k % khw;
-        const int ky = r / p.kw, kx = r % p.kw;
+    for (int k = threadIdx.x; k < ktiles * BK; k += NTHREADS) {
         Tap t;
-        t.ry = ky * p.dy;
-        t.rx = kx * p.dx;
-        t.x_off = (int64_t)ci * p.xs[1] + (int64_t)t.ry * p.xs[2] + (int64_t)t.rx * p.xs[3];
+        t.unused = 0;
+        if (k < p.kk) {
+            const int khw = p.kh * p.kw;
+            const int ci = k / khw, r = k % khw;
+            const int ky = r / p.kw, kx = r % p.kw;
+            t.r = r;
+            t.x_off = (int64_t)ci * p.xs[1] + (int64_t)(ky * p.dy) * p.xs[2] + (int64_t)(kx * p.dx) * p.xs[3];
+        } else {
+            t.r = PAD_TAP;
+            t.x_off = 0;
+        }
         taps[k] = t;
     }
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < NST; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&conv[s], WORK_WARPS);
             mbar_init(&empty[s], 1);
@@ -130,8 +154,8 @@ conv_3xtf32_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
         if (lane == 0) {
             int issued = 0;
             for (int kt = 0; kt < ktiles && !s_fail; ++kt) {
-                const int s = kt % STAGES;
-                if (kt >= STAGES && !mbar_wait(&empty[s], ((kt / STAGES) - 1) & 1)) {
+                const int s = kt % NST;
+                if (kt >= NST && !mbar_wait(&empty[s], ((kt / NST) - 1) & 1)) {
                     s_fail = 1;
                     break;
                 }
@@ -139,9 +163,9 @@ conv_3xtf32_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
                 tma_load_3d(stage_a(s), &tmW, kt * BK, m0, grp, &full[s]);
                 issued = kt + 1;
             }
-            for (int s = 0; s < STAGES && s < issued; ++s) {
-                const int last = s + STAGES * ((issued - 1 - s) / STAGES);
-                mbar_wait(&full[s], (last / STAGES) & 1);
+            for (int s = 0; s < NST && s < issued; ++s) {
+                const int last = s + NST * ((issued - 1 - s) / NST);
+                mbar_wait(&full[s], (last / NST) & 1);
             }
         }
     } else if (warp == 1) {
@@ -149,13 +173,13 @@ conv_3xtf32_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_tf32<BN>(false);
             for (int kt = 0; kt < ktiles; ++kt) {
-                const int s = kt % STAGES;
+                const int s = kt % NST;
                 const int chunk = kt / KC, kin = kt % KC;
                 if (kin == 0 && chunk > 0 && (s_fail || !mbar_wait(chunk_empty, (chunk - 1) & 1))) {
                     s_fail = 1;
                     break;
                 }
-                if (s_fail || !mbar_wait(&conv[s], (kt / STAGES) & 1)) {
+                if (s_fail || !mbar_wait(&conv[s], (kt / NST) & 1)) {
                     s_fail = 1;
                     break;
                 }
@@ -181,63 +205,79 @@ conv_3xtf32_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
         const int wt = threadIdx.x - WORK_WARP0 * 32;           // 0..255
         const int quarter = warp & 3;
         const int col0 = ((warp - WORK_WARP0) >> 2) * HALF_COLS;
-        // this thread's pixel (B row) and which 8 of the stage's 16 taps
-        const int prow = wt & (BN - 1);
-        const int khalf = wt >> 7;
-        const int64_t gcol = n0 + prow;
-        const bool col_ok = gcol < p.ncols;
-        int iy0 = 0, ix0 = 0;
-        int64_t xbase = 0;
-        if (col_ok) {
-            const int64_t img = gcol / p.hw, pix = gcol % p.hw;
-            const int64_t oy = pix / p.ow, ox = pix % p.ow;
-            iy0 = (int)(oy * p.sy - p.py);
-            ix0 = (int)(ox * p.sx - p.px);
-            xbase = img * p.xs[0] + (int64_t)grp * p.cg * p.xs[1] + (int64_t)iy0 * p.xs[2] + (int64_t)ix0 * p.xs[3];
-        }
+        // Gather ownership: worker warp ww owns the CM core matrices
+        // [ww*CM, (ww+1)*CM) of every B stage (core matrix cm = row group cm/4,
+        // k group cm%4, 8 pixels x 4 taps = 128 contiguous bytes); lane l of a
+        // warp instruction fetches pixel 8*(cm/4) + l/4, tap 4*(cm%4) + l%4, so
+        // one instruction fills one core matrix with 32 bank-distinct 4-byte
+        // copies.  A thread therefore gathers for NPIX pixels, 4 taps each.
+        constexpr int CM = BN / 16;                 // core matrices per warp per stage
+        constexpr int NPIX = CM / 4;
+        const int ww = warp - WORK_WARP0;
         const int ih = (int)p.ih, iw = (int)p.iw;
-        float nxt[8];
-        auto gather = [&](int kt) {
+        const float *xpix[NPIX];
+        uint64_t inb[NPIX];      // bit r: tap r = ky*kw + kx of the pixel lands inside the input
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int k = kt * BK + khalf * 8 + j;
-                float v = 0.0f;
-                if (col_ok && k < p.kk) {
-                    const Tap t = taps[k];
-                    const int iy = iy0 + t.ry, ix = ix0 + t.rx;
-                    if (iy >= 0 && iy < ih && ix >= 0 && ix < iw) v = __ldg(p.x + xbase + t.x_off);
+        for (int q = 0; q < NPIX; ++q) {
+            const int prow = 8 * (ww * CM / 4 + q) + (lane >> 2);
+            const int64_t gcol = n0 + prow;
+            xpix[q] = p.x;
+            inb[q] = 0;
+            if (gcol < p.ncols) {
+                const int64_t img = gcol / p.hw, pix = gcol % p.hw;
+                const int64_t oy = pix / p.ow, ox = pix % p.ow;
+                const int iy0 = (int)(oy * p.sy - p.py), ix0 = (int)(ox * p.sx - p.px);
+                xpix[q] = p.x + img * p.xs[0] + (int64_t)grp * p.cg * p.xs[1] + (int64_t)iy0 * p.xs[2] +
+                          (int64_t)ix0 * p.xs[3];
+                for (int r = 0; r < p.kh * p.kw; ++r) {
+                    const int iy = iy0 + (r / p.kw) * p.dy, ix = ix0 + (r % p.kw) * p.dx;
+                    if (iy >= 0 && iy < ih && ix >= 0 && ix < iw) inb[q] |= 1ull << r;
                 }
-                nxt[j] = v;
+            }
+        }
+        // Gather k-tile kt into its stage with 4-byte asynchronous copies
+        // (zero on padding and past the last tap).
+        auto gather = [&](int kt) {
+            uint8_t *bh = stage_b(kt % NST) + ww * CM * 128 + lane * 4;
+            const Tap *tk = taps + kt * BK + (lane & 3);
+#pragma unroll
+            for (int i = 0; i < CM; ++i) {
+                const Tap t = tk[4 * (i & 3)];
+                const bool ok = (inb[i >> 2] >> t.r) & 1;
+                cp4(bh + i * 128, ok ? xpix[i >> 2] + t.x_off : p.x, ok);
             }
         };
         float sum[HALF_COLS];
 #pragma unroll
         for (int j = 0; j < HALF_COLS; ++j) sum[j] = 0.0f;
-        gather(0);
+        // the first LOOKAHEAD stages start free
+#pragma unroll
+        for (int j = 0; j < LOOKAHEAD; ++j) {
+            if (j < ktiles) gather(j);
+            cp_commit();
+        }
         int chunk = 0;
         for (int kt = 0; kt < ktiles; ++kt) {
-            const int s = kt % STAGES;
-            float cur[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
-            if (kt + 1 < ktiles) gather(kt + 1);    // in flight while this stage is written
-            if (s_fail || !mbar_wait(&full[s], (kt / STAGES) & 1)) {
+            const int s = kt % NST;
+            cp_wait<LOOKAHEAD - 1>();                 // this thread's copies for k-tile kt have landed
+            __syncwarp();                             // ... and those of the rest of its warp
+            if (s_fail || !mbar_wait(&full[s], (kt / NST) & 1)) {
                 s_fail = 1;
                 break;
             }
             uint32_t bad = 0;
-            uint8_t *bh = stage_b(s), *bl = bh + B_TILE;
+            // lo of the warp's own core matrices: CM * 8 chunks of 16 bytes
+            uint8_t *bh = stage_b(s) + ww * CM * 128, *bl = bh + B_TILE;
 #pragma unroll
-            for (int jc = 0; jc < 2; ++jc) {
-                float4 v = make_float4(cur[4 * jc], cur[4 * jc + 1], cur[4 * jc + 2], cur[4 * jc + 3]);
+            for (int jc = 0; jc < CM / 4; ++jc) {
+                const uint32_t off = (uint32_t)(lane + 32 * jc) * 16;
+                const float4 v = *reinterpret_cast<const float4 *>(bh + off);   // hi: the gathered values
                 float4 l;
                 l.x = v.x - tf32_trunc(v.x);
                 l.y = v.y - tf32_trunc(v.y);
                 l.z = v.z - tf32_trunc(v.z);
                 l.w = v.w - tf32_trunc(v.w);
                 bad |= nonfinite_bits(v.x) | nonfinite_bits(v.y) | nonfinite_bits(v.z) | nonfinite_bits(v.w);
-                const uint32_t off = kmaj_off(prow, khalf * 2 + jc);
-                *reinterpret_cast<float4 *>(bh + off) = v;
                 *reinterpret_cast<float4 *>(bl + off) = l;
             }
             // weight tile: 512 16-byte chunks, two per thread, lo beside hi
@@ -258,6 +298,17 @@ conv_3xtf32_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
             fence_proxy_async();
             __syncwarp();
             if (lane == 0) mbar_arrive(&conv[s]);
+            // Gather k-tile kt + LOOKAHEAD into the stage of k-tile
+            // kt + LOOKAHEAD - NST, once the MMAs that read that stage have completed.
+            const int ahead = kt + LOOKAHEAD, prev = ahead - NST;
+            if (ahead < ktiles) {
+                if (prev >= 0 && !mbar_wait(&empty[prev % NST], (prev / NST) & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                gather(ahead);
+            }
+            cp_commit();
             if (kt % KC == KC - 1 || kt == ktiles - 1) {
                 if (!mbar_wait(chunk_full, chunk & 1)) {
                     s_fail = 1;
@@ -272,6 +323,7 @@ conv_3xtf32_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
                 ++chunk;
             }
         }
+        cp_wait<0>();    // no copy of this thread may land after the CTA's shared memory is released
         // ---- epilogue: row = output channel, columns = pixels -----------
         const int co = m0 + quarter * 32 + lane;
         const bool row_ok = co < p.cog;
@@ -292,7 +344,7 @@ conv_3xtf32_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
                         float acc = 0.0f;
                         for (int k = 0; k < p.kk; ++k) {
                             const Tap t = taps[k];
-                            const int iy = y0 + t.ry, ix = x0 + t.rx;
+                            const int iy = y0 + (t.r / p.kw) * p.dy, ix = x0 + (t.r % p.kw) * p.dx;
                             const float xv = (iy >= 0 && iy < ih && ix >= 0 && ix < iw) ? p.x[base + t.x_off] : 0.0f;
                             acc = fmaf(wrow[k], xv, acc);
                         }
@@ -361,8 +413,9 @@ __global__ void pack_weights_kernel(const float *__restrict__ w, int64_t ws0, in
 
 // The tensor-core conv reads each group's weights as dense [cog, cg*kh*kw]
 // rows with 16-byte aligned pitch (repacked into the handle's workspace when
-// the caller's layout is not that), at least one k-tile and at most MAX_TAPS
-// taps, and geometry whose pixel and tap coordinates fit int32.
+// the caller's layout is not that), at least one k-tile, a tap table that fits
+// in shared memory beside the stages, and geometry whose pixel and tap
+// coordinates fit int32.
 int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, const int64_t *ws, float *y,
                 int64_t n, int64_t c, int64_t ih, int64_t iw, int64_t co, int64_t cg, int64_t kh, int64_t kw,
                 int64_t oh, int64_t ow, int64_t groups, int64_t sy, int64_t sx, int64_t py, int64_t px, int64_t dy,
@@ -372,7 +425,8 @@ int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, co
     (void)c;
     const int64_t kk = cg * kh * kw;
     const int64_t cog = co / groups;
-    if (kk < 16 || kk > MAX_TAPS) return KX_DECLINED;
+    if (kk < 16 || kh * kw > PAD_TAP || (kk + BK) * (int64_t)sizeof(Tap) + Tile<128>::FIXED_SMEM > SMEM_LIMIT)
+        return KX_DECLINED;
     if (groups > 65535) return KX_DECLINED;
     const bool taps_dense = (kw == 1 || ws[3] == 1) && (kh == 1 || ws[2] == kw) && (cg == 1 || ws[1] == kh * kw);
     int64_t w_pitch = ws[0];
@@ -394,8 +448,7 @@ int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, co
         w_pitch = pitch;
     }
     const int64_t ncols = n * oh * ow;
-    const int64_t tiles = ((cog + BM - 1) / BM) * ((ncols + BN - 1) / BN);
-    if (tiles > INT32_MAX) return KX_DECLINED;
+    if (((cog + BM - 1) / BM) * ((ncols + 127) / 128) > INT32_MAX) return KX_DECLINED;
     CUtensorMap mw;
     if (!make_map(&mw, w, (uint64_t)kk, (uint64_t)cog, (uint64_t)groups, (uint64_t)w_pitch * 4,
                   (uint64_t)(w_pitch * cog) * 4, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B))
@@ -426,14 +479,25 @@ int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, co
     p.kk = (int)kk;
     p.ncols = ncols;
     p.status = h->flags + kStatusWord;
-    auto k = conv_3xtf32_kernel;
-    cudaError_t ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    // tile width from the wave model (as the GEMM's), within shared memory
+    const int64_t tm = (cog + BM - 1) / BM;
+    auto cost = [&](int bn) {
+        const int64_t t = tm * ((ncols + bn - 1) / bn) * groups;
+        return ((t + h->sm_count - 1) / h->sm_count) * (int64_t)(bn + 32);
+    };
+    const int table = (int)((kk + BK - 1) / BK * BK) * (int)sizeof(Tap);
+    int bn = (cost(256) <= cost(128) && Tile<256>::FIXED_SMEM + table <= SMEM_LIMIT) ? 256 : 128;
+    if (Tile<128>::FIXED_SMEM + table > SMEM_LIMIT) return KX_DECLINED;
+    const int smem = (bn == 256 ? Tile<256>::FIXED_SMEM : Tile<128>::FIXED_SMEM) + table;
+    auto k = bn == 256 ? conv_3xtf32_kernel<256> : conv_3xtf32_kernel<128>;
+    cudaError_t ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (ce == cudaSuccess) {
-        dim3 grid((unsigned)tiles, (unsigned)groups, 1);
-        k<<<grid, NTHREADS, SMEM_BYTES, h->stream>>>(mw, p);
+        const int64_t tiles_bn = tm * ((ncols + bn - 1) / bn);
+        dim3 grid((unsigned)tiles_bn, (unsigned)groups, 1);
+        k<<<grid, NTHREADS, smem, h->stream>>>(mw, p);
         ce = cudaGetLastError();
     }
-    *kernel_name = "conv_tc_3xtf32_128x128";
+    *kernel_name = bn == 256 ? "conv_tc_3xtf32_128x256" : "conv_tc_3xtf32_128x128";
     ++h->launches;
     return ce == cudaSuccess ? KX_OK : h->cuda_fail(ce);
 }

@@ -43,6 +43,7 @@ GEOMETRIES = [
     ((2, 32, 15, 15), (48, 3, 3), dict(stride=(1, 1), padding=(1, 1), dilation=(1, 1), groups=2)),
     ((2, 64, 9, 11), (130, 1, 1), dict(stride=(1, 1), padding=(0, 0), dilation=(1, 1), groups=1)),
     ((1, 8, 30, 30), (16, 5, 5), dict(stride=(3, 3), padding=(2, 2), dilation=(1, 1), groups=1)),
+    ((2, 3, 40, 40), (64, 7, 7), dict(stride=(2, 2), padding=(3, 3), dilation=(1, 1), groups=1)),
 ]
 
 
@@ -107,12 +108,12 @@ def test_conv_tc_nonfinite_weight_in_padding(kx, torch_cuda, tc):
 
 
 def test_conv_tc_declines_to_simt(kx, torch_cuda, tc):
-    """More taps than the kernel's table (cin 512 x 3 x 3) or too few (fewer
-    than one k-tile): the SIMT implicit GEMM takes over with the same bound."""
+    """More taps than the shared-memory tap table holds (cin 1024 x 3 x 3) or
+    fewer than one k-tile: the SIMT implicit GEMM takes over, same bound."""
     torch = torch_cuda
     rng = np.random.default_rng(12)
-    x = rng.uniform(-1, 1, (1, 512, 6, 6)).astype(np.float32)
-    w = rng.normal(0, 0.02, (8, 512, 3, 3)).astype(np.float32)
+    x = rng.uniform(-1, 1, (1, 1024, 6, 6)).astype(np.float32)
+    w = rng.normal(0, 0.02, (8, 1024, 3, 3)).astype(np.float32)
     _check(kx, torch, x, w, dict(stride=(1, 1), padding=(1, 1), dilation=(1, 1), groups=1))
     assert tc.last_kernel.startswith("conv_igemm"), tc.last_kernel
     x = rng.uniform(-1, 1, (1, 3, 6, 6)).astype(np.float32)
