@@ -155,7 +155,7 @@ def run_ours(args, rank, world, local):
     import kernix_b200 as kx
     from kernix_b200 import rng
     from kernix_b200.sharded import (PeerOutput, ReplicatedOutput, plan_rows, sharded_matmul, sharded_matmul_push,
-                                     sharded_matmul_replicated)
+                                     sharded_matmul_push_mc, sharded_matmul_replicated)
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -163,9 +163,8 @@ def run_ours(args, rank, world, local):
     group = dist.group.WORLD if world > 1 else None
     gather = args.gather if world > 1 else "none"
     rep = None
-    if gather == "nvls":
-        # NVLink multicast when the node has it: one launch per rank, the
-        # epilogue's stores reach every rank's C
+    if gather in ("nvls", "p2p-nvls"):
+        # symmetric memory bound to an NVLink multicast object
         rep = ReplicatedOutput(M, N, torch.float32, group, local)
         if not rep.available:
             raise RuntimeError("no NVLink multicast (NVLS) on this node")
@@ -182,6 +181,7 @@ def run_ours(args, rank, world, local):
     a_buf = a_host.to(dev)
     b = b_host.to(dev).view(K, N)
     push = gather in ("p2p", "p2p-ce")
+    push_mc = gather == "p2p-nvls"
     peer_out = PeerOutput(M, N, torch.float32, group, local) if push else None
     if rep is not None:
         c = rep.tensor
@@ -195,12 +195,14 @@ def run_ours(args, rank, world, local):
         if gather == "nccl" else None
     streams = (torch.cuda.current_stream(dev), torch.cuda.Stream(dev)) if gather == "nccl" else None
     push_streams = None
-    if push:
+    if push or push_mc:
         push_streams = {r: torch.cuda.Stream(dev) for r in range(world) if r != rank}
         push_streams["comm"] = torch.cuda.Stream(dev)
 
     def step():
-        if rep is not None:
+        if push_mc:
+            sharded_matmul_push_mc(pieces, b, rep, plan, rank, group, streams=push_streams)
+        elif rep is not None:
             sharded_matmul_replicated(pieces, b, rep, plan, rank, group)
         elif push:
             sharded_matmul_push(pieces, b, peer_out, plan, rank, group, streams=push_streams,
@@ -220,7 +222,7 @@ def run_ours(args, rank, world, local):
         step()
     barrier()
     # kernel-only timing of one GEMM launch (dominant kernel) for the roofline
-    if rep is not None:
+    if rep is not None and not push_mc:
         s0, e0 = plan.rows_of(rank, 0)
         launch = lambda: kx.matmul_into_replicated(pieces[0], b, c[s0:e0], rep.mc + s0 * rep.row_bytes)  # noqa: E731
     else:
@@ -283,6 +285,7 @@ def run_ours(args, rank, world, local):
             "config": {"workload": "c5: " + CONFIG_TEXT["c5"], "M": M, "N": N, "K": K, "a_row_stride": ROW_STRIDE,
                        "parallelism": f"rows{world} block-cyclic piece={plan.piece}" + {
                            "none": "", "nvls": " + NVLS multicast stores from the GEMM epilogue",
+                           "p2p-nvls": " + copy-engine push to peers, NVLS multicast store of the last piece",
                            "p2p": " + push to peers over CUDA IPC (copy engines, all-SM kernel for the last piece)",
                            "p2p-ce": " + copy-engine push to peers (CUDA IPC)", "nccl": " + NCCL all-gather"}[gather],
                        "l2": "inputs larger than L2 (A span 285 MB, B 268 MB)", "kernel": kname},
@@ -651,10 +654,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--piece", type=int, default=0, help="rows per sharded piece (0: 512 when sharded)")
-    ap.add_argument("--gather", choices=["p2p", "p2p-ce", "nvls", "nccl"], default="p2p",
+    ap.add_argument("--gather", choices=["p2p", "p2p-ce", "p2p-nvls", "nvls", "nccl"], default="p2p",
                     help="gathered output: pushes into peers' C (copy engines while a piece computes, an "
-                         "all-SM kernel for the last piece; p2p-ce: copy engines only), NVLS multicast "
-                         "stores from the GEMM epilogue, or NCCL all-gather")
+                         "all-SM kernel for the last piece; p2p-ce: copy engines only; p2p-nvls: NVLS "
+                         "multicast store for the last piece), NVLS multicast stores from the GEMM "
+                         "epilogue, or NCCL all-gather")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")

@@ -299,6 +299,39 @@ class ReplicatedOutput:
         self.row_bytes = n * self.tensor.element_size()
         self.done = torch.zeros(1, dtype=torch.int32, device=f"cuda:{device}")
 
+    def push_rows(self, r0: int, r1: int, streams: dict) -> None:
+        """Copy-engine copies of rows [r0, r1) into every peer's buffer (the
+        symmetric-memory peer mappings), one per peer on ``streams[peer]``."""
+        import ctypes as C
+
+        from . import _abi, handle
+        h = handle(self.tensor.device.index)
+        off, nbytes = r0 * self.row_bytes, (r1 - r0) * self.row_bytes
+        src = self.tensor.data_ptr() + off
+        err = _abi.KxError()
+        for r, base in enumerate(self.hdl.buffer_ptrs):
+            if r == self.rank:
+                continue
+            rc = _abi.lib.kx_copy_async(h.ptr, C.c_void_p(int(base) + off), C.c_void_p(src), nbytes,
+                                        C.c_void_p(streams[r].cuda_stream), C.byref(err))
+            _abi.raise_for(rc, err)
+
+    def multicast_rows(self, r0: int, r1: int) -> None:
+        """Store rows [r0, r1) once through the multicast address (all SMs, on
+        the current stream); the NVSwitch delivers them to every rank."""
+        import ctypes as C
+
+        import torch
+
+        from . import _abi, handle
+        h = handle(self.tensor.device.index)
+        h.set_stream(torch.cuda.current_stream(self.tensor.device))
+        off, nbytes = r0 * self.row_bytes, (r1 - r0) * self.row_bytes
+        err = _abi.KxError()
+        rc = _abi.lib.kx_multicast_store(h.ptr, C.c_void_p(self.tensor.data_ptr() + off), C.c_void_p(self.mc + off),
+                                         nbytes, C.byref(err))
+        _abi.raise_for(rc, err)
+
     def close(self) -> None:
         self.hdl = None
         self.tensor = None
@@ -316,3 +349,38 @@ def sharded_matmul_replicated(a_pieces, b, out: ReplicatedOutput, plan: RowPlan,
         s, e = plan.rows_of(rank, i)
         matmul_into_replicated(a_pieces[i], b, c[s:e], out.mc + s * out.row_bytes)
     dist.all_reduce(out.done, group=group)
+
+
+def sharded_matmul_push_mc(a_pieces, b, out: ReplicatedOutput, plan: RowPlan, rank: int, group=None,
+                           matmul_into: Callable | None = None, streams: dict | None = None) -> None:
+    """As ``sharded_matmul_push``, on symmetric memory: pieces before the last
+    go to the peers' buffers on the copy engines while the next piece
+    computes; the last piece is stored once through the NVLink multicast
+    address (each rank sends its rows once, the NVSwitch fans them out)."""
+    import torch
+    import torch.distributed as dist
+
+    if matmul_into is None:
+        from . import matmul_into as _mi
+        matmul_into = _mi
+    c = out.tensor
+    compute = torch.cuda.current_stream(c.device)
+    peers = [r for r in range(plan.world) if r != rank]
+    for i in range(plan.pieces):
+        s, e = plan.rows_of(rank, i)
+        matmul_into(a_pieces[i], b, c[s:e])
+        if i == plan.pieces - 1:
+            out.multicast_rows(s, e)
+            continue
+        ev = torch.cuda.Event()
+        ev.record(compute)
+        for r in peers:
+            streams[r].wait_event(ev)
+        out.push_rows(s, e, streams)
+    comm = streams["comm"]
+    for r in peers:
+        comm.wait_stream(streams[r])
+    comm.wait_stream(compute)
+    with torch.cuda.stream(comm):
+        dist.all_reduce(out.done, group=group)
+    compute.wait_stream(comm)
