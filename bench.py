@@ -163,11 +163,16 @@ def run_ours(args, rank, world, local):
     group = dist.group.WORLD if world > 1 else None
     gather = args.gather if world > 1 else "none"
     rep = None
-    if gather in ("nvls", "p2p-nvls"):
+    if gather in ("auto", "nvls", "p2p-nvls"):
         # symmetric memory bound to an NVLink multicast object
         rep = ReplicatedOutput(M, N, torch.float32, group, local)
         if not rep.available:
-            raise RuntimeError("no NVLink multicast (NVLS) on this node")
+            if gather != "auto":
+                raise RuntimeError("no NVLink multicast (NVLS) on this node")
+            rep.close()
+            rep = None
+        if gather == "auto":
+            gather = "p2p-nvls" if rep is not None else "p2p"
     if gather == "nvls":
         plan = plan_rows(M, world, target_piece=args.piece or M // world)
     else:
@@ -654,11 +659,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--piece", type=int, default=0, help="rows per sharded piece (0: 512 when sharded)")
-    ap.add_argument("--gather", choices=["p2p", "p2p-ce", "p2p-nvls", "nvls", "nccl"], default="p2p",
+    ap.add_argument("--gather", choices=["auto", "p2p", "p2p-ce", "p2p-nvls", "nvls", "nccl"], default="auto",
                     help="gathered output: pushes into peers' C (copy engines while a piece computes, an "
                          "all-SM kernel for the last piece; p2p-ce: copy engines only; p2p-nvls: NVLS "
                          "multicast store for the last piece), NVLS multicast stores from the GEMM "
-                         "epilogue, or NCCL all-gather")
+                         "epilogue, or NCCL all-gather; auto = p2p-nvls where the node has NVLink "
+                         "multicast, else p2p")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
