@@ -122,7 +122,8 @@ typedef struct kx_conv2d_options {
 typedef enum kx_f32_variant {
     KX_F32_AUTO = 0,    /* library chooses per shape and layout */
     KX_F32_FFMA = 1,    /* SIMT FP32 FMA, fp32 accumulation */
-    KX_F32_3XTF32 = 2   /* split-TF32 tensor-core contraction (tcgen05 + TMEM) */
+    KX_F32_3XTF32 = 2,  /* split-TF32 tensor-core contraction (tcgen05 + TMEM) */
+    KX_F32_3XTF32_1SM = 3   /* the same, one-SM tiles only (no CTA-pair kernel) */
 } kx_f32_variant;
 
 /* Kernel family selection for f64. */

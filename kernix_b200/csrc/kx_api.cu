@@ -427,7 +427,7 @@ int kx_set_stream(kx_handle *hh, void *stream) {
 }
 
 int kx_set_f32_variant(kx_handle *hh, int variant) {
-    if (!hh || variant < KX_F32_AUTO || variant > KX_F32_3XTF32) return KX_E_PARAM;
+    if (!hh || variant < KX_F32_AUTO || variant > KX_F32_3XTF32_1SM) return KX_E_PARAM;
     hh->impl.f32_variant = variant;
     return KX_OK;
 }

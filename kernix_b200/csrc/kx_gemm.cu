@@ -88,8 +88,15 @@ int run_gemm(Handle *h, GemmParams<T> p, const char **kernel_name) {
         if (!h->ordered && h->f32_variant != KX_F32_FFMA && tc_eligible(p)) {
             const int64_t tc_tiles = (int64_t)((p.M + 127) / 128) * ((p.N + 255) / 256) * p.nbatch;
             const bool big = tc_tiles >= h->sm_count / 2 && p.K >= 64;
-            if (h->f32_variant == KX_F32_3XTF32 || big) {
-                int rc = run_gemm_tc(h, p, kernel_name);
+            if (h->f32_variant == KX_F32_3XTF32 || h->f32_variant == KX_F32_3XTF32_1SM || big) {
+                // CTA pairs (256 x 256 tiles) when they still give every SM
+                // several tiles; one-SM tiles otherwise.
+                const int64_t pair_ctas = 2 * (int64_t)((p.M + 255) / 256) * ((p.N + 255) / 256) * p.nbatch;
+                int rc = KX_DECLINED;
+                if (h->f32_variant != KX_F32_3XTF32_1SM && !p.C_mc &&
+                    (h->f32_variant == KX_F32_3XTF32 || pair_ctas >= 4LL * h->sm_count))
+                    rc = run_gemm_tc_pair(h, p, kernel_name);
+                if (rc == KX_DECLINED) rc = run_gemm_tc(h, p, kernel_name);
                 if (rc != KX_DECLINED) return rc;
             }
         }

@@ -92,6 +92,9 @@ template <typename T> int run_gemm(Handle *h, GemmParams<T> p, const char **kern
 // cannot describe the operands (the caller then uses the SIMT kernel).
 bool tc_eligible(const GemmParams<float> &p);
 int run_gemm_tc(Handle *h, const GemmParams<float> &p, const char **kernel_name);
+// The same arithmetic on CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles;
+// kx_gemm_tc2.cu).  KX_DECLINED when a tensor map cannot describe the operands.
+int run_gemm_tc_pair(Handle *h, const GemmParams<float> &p, const char **kernel_name);
 // conv2d as a split-TF32 implicit GEMM on the tensor cores (kx_conv_tc.cu);
 // strides of x and w in elements (singleton dims zero).  KX_DECLINED when the
 // weights are not dense tap rows or the tap count is outside its table.

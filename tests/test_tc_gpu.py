@@ -15,7 +15,15 @@ pytestmark = pytest.mark.gpu
 @pytest.fixture
 def tc_handle(kx, torch_cuda):
     h = kx.handle(0)
-    h.set_f32_variant(2)    # KX_F32_3XTF32
+    h.set_f32_variant(3)    # KX_F32_3XTF32_1SM: the one-SM kernel at every size
+    yield h
+    h.set_f32_variant(0)
+
+
+@pytest.fixture
+def pair_handle(kx, torch_cuda):
+    h = kx.handle(0)
+    h.set_f32_variant(2)    # KX_F32_3XTF32: CTA pairs where the product is large enough
     yield h
     h.set_f32_variant(0)
 
@@ -132,3 +140,48 @@ def test_auto_selects_tensor_cores_for_large_products(kx, torch_cuda):
     assert h.last_kernel.startswith("simt"), h.last_kernel
     h.set_f32_variant(0)
     h.synchronize()
+
+
+@pytest.mark.parametrize("b_layout", ["row", "col"])
+@pytest.mark.parametrize("m,k,n", [(2304, 200, 4352), (4096, 1040, 2400)])
+def test_tc_pair_kernel(kx, torch_cuda, pair_handle, b_layout, m, k, n):
+    """CTA-pair kernel (tcgen05 cta_group::2, 256 x 256 tiles): ragged k, m and
+    n edges, both B layouts, row samples from both CTAs of a pair."""
+    rng = np.random.default_rng(m + k + n)
+    pad = 4
+    abuf = rng.uniform(-1, 1, (m, k + pad)).astype(np.float32)
+    if b_layout == "row":
+        bbuf = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+        vb = oracle.View(bbuf, (k, n), (n, 1))
+    else:
+        bbuf = rng.uniform(-1, 1, (n, k)).astype(np.float32)
+        vb = oracle.View(bbuf, (k, n), (1, k))
+    got = kx.matmul(_view(kx, torch_cuda, abuf, (m, k), (k + pad, 1)),
+                    _view(kx, torch_cuda, bbuf, vb.dims, vb.strides)).cpu().numpy()
+    assert pair_handle.last_kernel.startswith("tc_3xtf32_pair"), pair_handle.last_kernel
+    pair_handle.synchronize()
+    rows = np.array([0, 1, 127, 128, 129, 255, 256, 383, m // 2, m - 129, m - 1])
+    _check(got[rows], oracle.View(np.ascontiguousarray(abuf[rows, :k]), (len(rows), k), (k, 1)), vb)
+
+
+def test_tc_pair_batched_and_nonfinite(kx, torch_cuda, pair_handle):
+    torch = torch_cuda
+    rng = np.random.default_rng(8)
+    a = rng.uniform(-1, 1, (3, 1024, 96)).astype(np.float32)
+    b = rng.uniform(-1, 1, (3, 96, 1536)).astype(np.float32)
+    got = kx.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()).cpu().numpy()
+    assert pair_handle.last_kernel.startswith("tc_3xtf32_pair"), pair_handle.last_kernel
+    for i in range(3):
+        rows = np.array([0, 200, 511, 700, 1023])
+        _check(got[i][rows], oracle.View(np.ascontiguousarray(a[i][rows]), (5, 96), (96, 1)), oracle.View.of(b[i]))
+    # an inf in the peer CTA's rows and a NaN in the leader's: IEEE propagation as the FFMA path
+    a2 = np.full((2048, 64), 0.5, dtype=np.float32)
+    b2 = np.ones((64, 8192), dtype=np.float32)
+    a2[130, 7] = np.inf
+    a2[3, 2] = np.nan
+    got = kx.matmul(torch.from_numpy(a2).cuda(), torch.from_numpy(b2).cuda()).cpu().numpy()
+    assert pair_handle.last_kernel.startswith("tc_3xtf32_pair"), pair_handle.last_kernel
+    assert np.isinf(got[130]).all() and np.isnan(got[3]).all()
+    fin = np.isfinite(got)
+    assert np.array_equal(got[fin], np.full(fin.sum(), 32.0, dtype=np.float32))
+    pair_handle.synchronize()
