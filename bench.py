@@ -233,6 +233,7 @@ def run_ours(args, rank, world, local):
     else:
         launch = lambda: kx.matmul_into(pieces[0], b, c[:plan.piece])  # noqa: E731
     kern_ms = time_dominant_kernel(launch, dev)
+    step_kernel = h.last_kernel     # the family the timed GEMM launches use
     barrier()
     launches0 = h.launches
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -275,7 +276,7 @@ def run_ours(args, rank, world, local):
         peaks, peak_src = measured_peaks()
         clocks = clk.summary()
         pipe = "fp32-simt"
-        kname = h.last_kernel
+        kname = step_kernel
         if "tf32" in kname:
             pipe = "3xtf32"
         sm_max = clocks.get("sm_max_mhz") or peaks.get("sm_max_mhz", 1965.0)
