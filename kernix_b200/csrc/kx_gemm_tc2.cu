@@ -1,6 +1,6 @@
 // Split-TF32 f32 GEMM on CTA pairs: tcgen05.mma.cta_group::2 computes a
-// 256 x 256 tile on two SMs of a cluster, each SM staging only its half of A
-// (128 rows) and its half of B (128 columns).
+// 256 x 256 (or 256 x 224) tile on two SMs of a cluster, each SM staging only
+// its half of A (128 rows) and its half of B (128 or 112 columns).
 //
 // Same arithmetic as the one-SM kernel (kx_gemm_tc.cu): hi = the raw tile (the
 // tensor core reads f32 as tf32 by truncation), lo = x - hi written by the
@@ -34,16 +34,24 @@ namespace kx {
 namespace tc {
 namespace pair {
 
-constexpr int BMP = 256, BNP = 256;            // pair tile
-constexpr int HB = 128;                        // B columns staged per CTA
-constexpr int B_TILE = HB * BK * 4;            // 8 KB
+constexpr int BMP = 256;                       // pair tile rows
+constexpr int B_TILE = 128 * BK * 4;           // 8 KB of B staging per CTA and stage
 constexpr int NST = 6;                         // stages
 constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;   // 32 KB
 constexpr int SMEM_BYTES = NST * STAGE_BYTES + BAR_BYTES + 1024;
-constexpr int HALF_COLS = BNP / 2;             // accumulator columns per worker thread
-constexpr int CONV_CHUNKS = (A_TILE + B_TILE) / 16;     // 1024
-static_assert(CONV_CHUNKS % WORK_THREADS == 0, "converter work must divide evenly");
 static_assert(3 * NST + 2 <= (BAR_BYTES - 8) / 8, "barrier area");
+
+// Pair tile width 2 * HB: 256, or 224 when that packs the pairs into whole
+// waves (a 512 x 8192 piece: 74 pairs = 148 CTAs).  Each CTA's B half is HB
+// columns; MN-major B is loaded as four 32-column boxes (128 columns, the
+// last 16 unused at HB = 112), K-major B as an HB-row box.
+template <int HB> struct Pair {
+    static_assert(HB == 128 || HB == 112, "pair half width");
+    static constexpr int BNP = 2 * HB;
+    static constexpr int HALF_COLS = HB;       // accumulator columns per worker thread
+    static constexpr int B_BYTES_MN = B_TILE;          // four 32-column boxes
+    static constexpr int B_BYTES_K = HB * BK * 4;      // one HB-row box
+};
 
 struct Params {
     const float *A;
@@ -58,9 +66,9 @@ struct Params {
     uint32_t *status;
 };
 
-// f32 accumulate, tf32 A and B, M = 256 (the pair), N = 256.
-__host__ __device__ constexpr uint32_t idesc_pair(bool b_mn_major) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(BNP >> 3) << 17) |
+// f32 accumulate, tf32 A and B, M = 256 (the pair), N = the pair's width.
+__host__ __device__ constexpr uint32_t idesc_pair(bool b_mn_major, int bnp) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(bnp >> 3) << 17) |
            ((uint32_t)(BMP >> 4) << 24);
 }
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -129,10 +137,15 @@ __device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t cluster_addr) {
     return v;
 }
 
-template <bool B_MN>
+template <bool B_MN, int HB>
 __global__ void __launch_bounds__(NTHREADS, 1)
 gemm_3xtf32_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ Params p) {
+    using PT = Pair<HB>;
+    constexpr int BNP = PT::BNP, HALF_COLS = PT::HALF_COLS;
+    constexpr int B_BYTES = B_MN ? PT::B_BYTES_MN : PT::B_BYTES_K;
+    constexpr int CHUNKS = (A_TILE + B_BYTES) / 16;
+    constexpr int CONV_ITERS = (CHUNKS + WORK_THREADS - 1) / WORK_THREADS;
     extern __shared__ uint8_t smem_raw[];
     // The same dynamic offsets in both CTAs: the MMA reads the peer's halves
     // at the addresses the leader's descriptors name.
@@ -156,7 +169,7 @@ gemm_3xtf32_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
     int tm, tn;
     raster((int)(blockIdx.x >> 1), tiles_m, tiles_n, 8, tm, tn);
     const int m0 = tm * BMP + (int)rank * BM;        // this CTA's 128 rows
-    const int n0 = tn * BNP;                         // the pair's 256 columns
+    const int n0 = tn * BNP;                         // the pair's columns
     const int nb0 = n0 + (int)rank * HB;             // this CTA's staged B columns
     const int batch = blockIdx.y;
     const int ab = p.a_batched ? batch : 0, bb = p.b_batched ? batch : 0;
@@ -199,12 +212,12 @@ gemm_3xtf32_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
                     s_fail = 1;
                     break;
                 }
-                mbar_expect_tx(&full[s], A_TILE + B_TILE);
+                mbar_expect_tx(&full[s], A_TILE + B_BYTES);
                 const int k0 = kt * BK;
                 tma_load_3d(stage_a(s), &tmA, k0, m0, ab, &full[s]);
                 if constexpr (B_MN) {
 #pragma unroll
-                    for (int j = 0; j < HB / 32; ++j)
+                    for (int j = 0; j < B_TILE / 2048; ++j)
                         tma_load_3d(stage_b(s) + j * 2048, &tmB, nb0 + 32 * j, k0, bb, &full[s]);
                 } else {
                     tma_load_3d(stage_b(s), &tmB, k0, nb0, bb, &full[s]);
@@ -219,7 +232,7 @@ gemm_3xtf32_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
     } else if (warp == 1) {
         // ---- MMA issuer (leader only) ----------------------------------
         if (leader && lane == 0) {
-            constexpr uint32_t idesc = idesc_pair(B_MN);
+            constexpr uint32_t idesc = idesc_pair(B_MN, BNP);
             const uint32_t chunk_full_peer = map_to(smem_u32(chunk_full), peer);
             for (int kt = 0; kt < ktiles; ++kt) {
                 const int s = kt % NST;
@@ -283,8 +296,9 @@ gemm_3xtf32_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
             uint32_t bad = 0;
             uint8_t *base = stage_a(s);
 #pragma unroll
-            for (int j = 0; j < CONV_CHUNKS / WORK_THREADS; ++j) {
+            for (int j = 0; j < CONV_ITERS; ++j) {
                 const int c = wt + j * WORK_THREADS;
+                if (CHUNKS % WORK_THREADS != 0 && c >= CHUNKS) break;   // only what the TMA wrote
                 const bool in_a = c < A_TILE / 16;
                 float4 *hp = reinterpret_cast<float4 *>(base + (in_a ? c * 16 : 2 * A_TILE + (c - A_TILE / 16) * 16));
                 float4 *lp = reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(hp) + (in_a ? A_TILE : B_TILE));
@@ -381,12 +395,12 @@ gemm_3xtf32_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
 // ---------------------------------------------------------------------------
 namespace {
 
-template <bool B_MN>
+template <bool B_MN, int HB>
 cudaError_t launch_pair(Handle *h, const CUtensorMap &ma, const CUtensorMap &mb, const tc::pair::Params &pp,
                         int64_t pair_tiles, int nb) {
     using namespace tc;
     using namespace tc::pair;
-    auto k = gemm_3xtf32_pair_kernel<B_MN>;
+    auto k = gemm_3xtf32_pair_kernel<B_MN, HB>;
     cudaError_t ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (ce != cudaSuccess) return ce;
     cudaLaunchConfig_t cfg = {};
@@ -421,6 +435,14 @@ int run_gemm_tc_pair(Handle *h, const GemmParams<float> &p, const char **kernel_
     const int a_batched = (nb > 1 && a_bs > 0) ? 1 : 0;
     const int b_batched = (nb > 1 && b_bs > 0) ? 1 : 0;
     if (p.M < 2 * BM) return KX_DECLINED;
+    // pair width by the wave model (as the one-SM kernel's tile width)
+    const int64_t pm = (p.M + BMP - 1) / BMP;
+    // (the 224-wide pair stages 128 B columns for 112: weighted 5 % heavier)
+    auto cost = [&](int bnp) {
+        const int64_t ctas = 2 * pm * ((p.N + bnp - 1) / bnp) * nb;
+        return (double)((ctas + h->sm_count - 1) / h->sm_count) * (bnp + 32) * (bnp == 224 ? 1.05 : 1.0);
+    };
+    const int hb = cost(224) < cost(256) ? 112 : 128;
     CUtensorMap ma, mb;
     const uint64_t a_s2 = a_batched ? (uint64_t)a_bs * 4 : (uint64_t)((p.a_rs * 4 * (int64_t)p.M + 15) / 16 * 16);
     if (!make_map(&ma, p.A, (uint64_t)p.K, (uint64_t)p.M, a_batched ? (uint64_t)nb : 1, (uint64_t)p.a_rs * 4, a_s2,
@@ -434,7 +456,7 @@ int run_gemm_tc_pair(Handle *h, const GemmParams<float> &p, const char **kernel_
     } else {
         const uint64_t s2 = b_batched ? (uint64_t)b_bs * 4 : (uint64_t)((p.b_cs * 4 * (int64_t)p.N + 15) / 16 * 16);
         okb = make_map(&mb, p.B, (uint64_t)p.K, (uint64_t)p.N, b_batched ? (uint64_t)nb : 1, (uint64_t)p.b_cs * 4, s2,
-                       BK, HB, CU_TENSOR_MAP_SWIZZLE_64B);
+                       BK, (uint32_t)hb, CU_TENSOR_MAP_SWIZZLE_64B);
     }
     if (!okb) return KX_DECLINED;
     Params pp;
@@ -456,11 +478,18 @@ int run_gemm_tc_pair(Handle *h, const GemmParams<float> &p, const char **kernel_
     pp.a_batched = a_batched;
     pp.b_batched = b_batched;
     pp.status = h->flags + kStatusWord;
-    const int64_t pair_tiles = (int64_t)((p.M + BMP - 1) / BMP) * ((p.N + BNP - 1) / BNP);
+    const int bnp = 2 * hb;
+    const int64_t pair_tiles = pm * ((p.N + bnp - 1) / bnp);
     if (2 * pair_tiles > INT32_MAX) return KX_DECLINED;
-    const cudaError_t ce = b_mn ? launch_pair<true>(h, ma, mb, pp, pair_tiles, nb)
-                                : launch_pair<false>(h, ma, mb, pp, pair_tiles, nb);
-    *kernel_name = b_mn ? "tc_3xtf32_pair_256x256_bmn" : "tc_3xtf32_pair_256x256_bk";
+    cudaError_t ce;
+    if (b_mn)
+        ce = hb == 128 ? launch_pair<true, 128>(h, ma, mb, pp, pair_tiles, nb)
+                       : launch_pair<true, 112>(h, ma, mb, pp, pair_tiles, nb);
+    else
+        ce = hb == 128 ? launch_pair<false, 128>(h, ma, mb, pp, pair_tiles, nb)
+                       : launch_pair<false, 112>(h, ma, mb, pp, pair_tiles, nb);
+    *kernel_name = hb == 128 ? (b_mn ? "tc_3xtf32_pair_256x256_bmn" : "tc_3xtf32_pair_256x256_bk")
+                             : (b_mn ? "tc_3xtf32_pair_256x224_bmn" : "tc_3xtf32_pair_256x224_bk");
     ++h->launches;
     return ce == cudaSuccess ? KX_OK : h->cuda_fail(ce);
 }
