@@ -105,10 +105,15 @@ int run_gemm(Handle *h, GemmParams<T> p, const char **kernel_name) {
                     best1 = std::min(best1, (double)waves(tm1 * ((p.N + bn - 1) / bn) * p.nbatch) * (bn + 32));
                 bestp = 0.92 * (double)waves(2 * tmp * ((p.N + 255) / 256) * p.nbatch) * (256 + 32);
                 int rc = KX_DECLINED;
-                if (h->f32_variant != KX_F32_3XTF32_1SM && !p.C_mc && p.M >= 256 &&
+                // Short contractions over many tiles: the persistent kernel,
+                // whose epilogue overlaps the next tile.
+                const int64_t tiles128 = tm1 * ((p.N + 127) / 128) * p.nbatch;
+                if (h->f32_variant == KX_F32_AUTO && !p.C_mc && p.K <= 1024 && tiles128 >= 2LL * h->sm_count)
+                    rc = run_gemm_tc_short(h, p, kernel_name);
+                if (rc == KX_DECLINED && h->f32_variant != KX_F32_3XTF32_1SM && !p.C_mc && p.M >= 256 &&
                     (h->f32_variant == KX_F32_3XTF32 || (p.K >= 512 && bestp < best1)))
                     rc = run_gemm_tc_pair(h, p, kernel_name);
-                if (rc == KX_DECLINED) rc = run_gemm_tc(h, p, kernel_name);
+                if (rc == KX_DECLINED) rc = run_gemm_tc(h, p, kernel_name);   // one-SM tiles
                 if (rc != KX_DECLINED) return rc;
             }
         }

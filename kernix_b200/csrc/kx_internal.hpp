@@ -95,6 +95,9 @@ int run_gemm_tc(Handle *h, const GemmParams<float> &p, const char **kernel_name)
 // The same arithmetic on CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles;
 // kx_gemm_tc2.cu).  KX_DECLINED when a tensor map cannot describe the operands.
 int run_gemm_tc_pair(Handle *h, const GemmParams<float> &p, const char **kernel_name);
+// Persistent split-TF32 kernel for K <= 1024 with the epilogue overlapping the
+// next tile (kx_gemm_tc_short.cu).  KX_DECLINED for longer K or unmappable operands.
+int run_gemm_tc_short(Handle *h, const GemmParams<float> &p, const char **kernel_name);
 // conv2d as a split-TF32 implicit GEMM on the tensor cores (kx_conv_tc.cu);
 // strides of x and w in elements (singleton dims zero).  KX_DECLINED when the
 // weights are not dense tap rows or the tap count is outside its table.

@@ -185,3 +185,36 @@ def test_tc_pair_batched_and_nonfinite(kx, torch_cuda, pair_handle):
     fin = np.isfinite(got)
     assert np.array_equal(got[fin], np.full(fin.sum(), 32.0, dtype=np.float32))
     pair_handle.synchronize()
+
+
+def test_tc_short_k_persistent(kx, torch_cuda):
+    """K <= 1024 over many tiles: the persistent kernel (TMEM double-buffered,
+    epilogue overlapping the next tile) -- attention scores Q K^T with a
+    transposed K view, a ragged row-major case and inf/NaN propagation."""
+    torch = torch_cuda
+    h = kx.handle(0)
+    h.set_f32_variant(0)
+    rng = np.random.default_rng(17)
+    q = rng.standard_normal((4, 8, 512, 128)).astype(np.float32)
+    k = rng.standard_normal((4, 8, 512, 128)).astype(np.float32)
+    s = kx.matmul(torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda().transpose(2, 3)).cpu().numpy()
+    assert h.last_kernel == "tc_3xtf32_short_128x128_bk", h.last_kernel
+    for bi, hi in [(0, 0), (3, 7), (2, 5)]:
+        rows = np.array([0, 127, 128, 300, 511])
+        _check(s[bi, hi][rows], oracle.View(np.ascontiguousarray(q[bi, hi][rows]), (5, 128), (128, 1)),
+               oracle.View(k[bi, hi], (128, 512), (1, 128)))
+    a = rng.uniform(-1, 1, (4100, 300)).astype(np.float32)
+    b = rng.uniform(-1, 1, (300, 2052)).astype(np.float32)   # row pitch 8208 B: TMA-aligned
+    c = kx.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()).cpu().numpy()
+    assert h.last_kernel == "tc_3xtf32_short_128x128_bmn", h.last_kernel
+    rows = np.array([0, 1, 2047, 4095, 4096, 4099])
+    _check(c[rows], oracle.View(np.ascontiguousarray(a[rows]), (len(rows), 300), (300, 1)), oracle.View.of(b))
+    a[5, 7] = np.inf
+    a[4097, 3] = np.nan
+    c = kx.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()).cpu().numpy()
+    assert h.last_kernel == "tc_3xtf32_short_128x128_bmn", h.last_kernel
+    assert np.isnan(c[4097]).all()
+    assert np.array_equal(np.isinf(c[5]), b[7] != 0) and not np.isnan(c[5][b[7] != 0]).any()
+    fin = np.isfinite(c).all(axis=1)
+    assert fin[:5].all() and fin[6:4097].all()
+    h.synchronize()
