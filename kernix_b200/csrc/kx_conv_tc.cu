@@ -389,6 +389,333 @@ conv_3xtf32_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
     if (threadIdx.x == 0 && s_fail) atomicOr(p.status, KX_TIMEOUT_FLAG);
 }
 
+
+// ---------------------------------------------------------------------------
+// CTA pairs: tcgen05.mma.cta_group::2 on a 256-channel x 256-pixel tile.  Each
+// CTA takes 128 output channels of weights (TMA) and gathers 128 pixels of the
+// B tile, so every input element is gathered once per 256 channels instead of
+// once per 128, and each SM feeds the tensor core a third less operand data.
+// Pair protocol as in kx_gemm_tc2.cu: remote arrives on the leader's barriers,
+// the leader's completions committed to both CTAs, three cluster barriers.
+// ---------------------------------------------------------------------------
+constexpr int PAIR_NST = 6;
+constexpr int PAIR_B_TILE = 128 * BK * 4;                          // 8 KB
+constexpr int PAIR_STAGE = 2 * A_TILE + 2 * PAIR_B_TILE;           // 32 KB
+constexpr int PAIR_FIXED_SMEM = PAIR_NST * PAIR_STAGE + BAR_BYTES + 1024;
+static_assert(3 * PAIR_NST + 2 <= (BAR_BYTES - 8) / 8, "barrier area");
+
+__global__ void __launch_bounds__(NTHREADS, 1)
+conv_3xtf32_pair_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ Params p) {
+    constexpr int NST = PAIR_NST, LOOKAHEAD = NST / 2, B_TILE = PAIR_B_TILE, STAGE_BYTES = PAIR_STAGE;
+    constexpr int BNP = 256, HALF_COLS = 128;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + NST * STAGE_BYTES);
+    uint64_t *conv = full + NST;
+    uint64_t *empty = conv + NST;
+    uint64_t *chunk_full = empty + NST;
+    uint64_t *chunk_empty = chunk_full + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(chunk_empty + 1);
+    Tap *taps = reinterpret_cast<Tap *>(smem + NST * STAGE_BYTES + BAR_BYTES);
+    __shared__ int s_fail_storage;
+    __shared__ uint32_t s_nonfinite_storage;
+    volatile int &s_fail = s_fail_storage;
+    volatile uint32_t &s_nonfinite = s_nonfinite_storage;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const uint32_t peer = rank ^ 1u;
+    const int tiles_m = (int)((p.cog + 255) / 256), tiles_n = (int)((p.ncols + BNP - 1) / BNP);
+    int tm, tn;
+    raster((int)(blockIdx.x >> 1), tiles_m, tiles_n, 8, tm, tn);
+    const int m0 = tm * 256 + (int)rank * BM;            // this CTA's output channels
+    const int64_t n0 = (int64_t)tn * BNP;                // the pair's pixels
+    const int64_t nb0 = n0 + (int64_t)rank * 128;        // this CTA's gathered pixels
+    const int grp = blockIdx.y;
+    const int ktiles = (p.kk + BK - 1) / BK;
+    const int nchunks = (ktiles + KC - 1) / KC;
+
+    for (int k = threadIdx.x; k < ktiles * BK; k += NTHREADS) {
+        Tap t;
+        t.unused = 0;
+        if (k < p.kk) {
+            const int khw = p.kh * p.kw;
+            const int ci = k / khw, r = k % khw;
+            const int ky = r / p.kw, kx = r % p.kw;
+            t.r = r;
+            t.x_off = (int64_t)ci * p.xs[1] + (int64_t)(ky * p.dy) * p.xs[2] + (int64_t)(kx * p.dx) * p.xs[3];
+        } else {
+            t.r = PAD_TAP;
+            t.x_off = 0;
+        }
+        taps[k] = t;
+    }
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NST; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&conv[s], 2 * WORK_WARPS);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(chunk_full, 1);
+        mbar_init(chunk_empty, 2 * WORK_WARPS);
+        s_fail = 0;
+        s_nonfinite = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    cluster_sync_any();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    auto stage_a = [&](int s) { return smem + s * STAGE_BYTES; };
+    auto stage_b = [&](int s) { return smem + s * STAGE_BYTES + 2 * A_TILE; };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;
+            for (int kt = 0; kt < ktiles && !s_fail; ++kt) {
+                const int s = kt % NST;
+                if (kt >= NST && !mbar_wait(&empty[s], ((kt / NST) - 1) & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                mbar_expect_tx(&full[s], A_TILE);
+                tma_load_3d(stage_a(s), &tmW, kt * BK, m0, grp, &full[s]);
+                issued = kt + 1;
+            }
+            for (int s = 0; s < NST && s < issued; ++s) {
+                const int last = s + NST * ((issued - 1 - s) / NST);
+                mbar_wait(&full[s], (last / NST) & 1);
+            }
+        }
+    } else if (warp == 1) {
+        if (leader && lane == 0) {
+            constexpr uint32_t idesc = idesc_pair(false, BNP);
+            const uint32_t chunk_full_peer = map_to(smem_u32(chunk_full), peer);
+            for (int kt = 0; kt < ktiles; ++kt) {
+                const int s = kt % NST;
+                const int chunk = kt / KC, kin = kt % KC;
+                if (kin == 0 && chunk > 0 && (s_fail || !mbar_wait_cluster(chunk_empty, (chunk - 1) & 1))) {
+                    s_fail = 1;
+                    break;
+                }
+                if (s_fail || !mbar_wait_cluster(&conv[s], (kt / NST) & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_hi = smem_u32(stage_a(s)), a_lo = a_hi + A_TILE;
+                const uint32_t b_hi = smem_u32(stage_b(s)), b_lo = b_hi + B_TILE;
+#pragma unroll
+                for (int ks = 0; ks < BK / 8; ++ks) {
+                    const uint64_t dah = desc_k_sw64(a_hi + ks * 32), dal = desc_k_sw64(a_lo + ks * 32);
+                    const uint64_t dbh = desc_k_none(b_hi + ks * 256, 128, 512);
+                    const uint64_t dbl = desc_k_none(b_lo + ks * 256, 128, 512);
+                    mma_pair(tmem, dah, dbh, idesc, (kin > 0 || ks > 0) ? 1u : 0u);
+                    mma_pair(tmem + XCOL, dah, dbl, idesc, (kt > 0 || ks > 0) ? 1u : 0u);
+                    mma_pair(tmem + XCOL, dal, dbh, idesc, 1u);
+                }
+                const uint32_t e_local = smem_u32(&empty[s]);
+                commit_pair(e_local);
+                commit_pair(map_to(e_local, peer));
+                if (kin == KC - 1 || kt == ktiles - 1) {
+                    commit_pair(smem_u32(chunk_full));
+                    commit_pair(chunk_full_peer);
+                }
+            }
+            if (s_fail) {
+                commit_pair(smem_u32(chunk_full));
+                commit_pair(chunk_full_peer);
+            }
+        }
+    } else if (warp >= WORK_WARP0) {
+        const int wt = threadIdx.x - WORK_WARP0 * 32;
+        const int quarter = warp & 3;
+        const int col0 = ((warp - WORK_WARP0) >> 2) * HALF_COLS;
+        const uint32_t conv_leader0 = map_to(smem_u32(&conv[0]), 0);
+        const uint32_t chunk_empty_leader = map_to(smem_u32(chunk_empty), 0);
+        // gather ownership as the one-SM kernel at 128 pixels: 8 core
+        // matrices per warp, two pixels per thread
+        constexpr int CM = 8, NPIX = 2;
+        const int ww = warp - WORK_WARP0;
+        const int ih = (int)p.ih, iw = (int)p.iw;
+        const float *xpix[NPIX];
+        uint64_t inb[NPIX];
+#pragma unroll
+        for (int q = 0; q < NPIX; ++q) {
+            const int prow = 8 * (ww * CM / 4 + q) + (lane >> 2);
+            const int64_t gcol = nb0 + prow;
+            xpix[q] = p.x;
+            inb[q] = 0;
+            if (gcol < p.ncols) {
+                const int64_t img = gcol / p.hw, pix = gcol % p.hw;
+                const int64_t oy = pix / p.ow, ox = pix % p.ow;
+                const int iy0 = (int)(oy * p.sy - p.py), ix0 = (int)(ox * p.sx - p.px);
+                xpix[q] = p.x + img * p.xs[0] + (int64_t)grp * p.cg * p.xs[1] + (int64_t)iy0 * p.xs[2] +
+                          (int64_t)ix0 * p.xs[3];
+                for (int r = 0; r < p.kh * p.kw; ++r) {
+                    const int iy = iy0 + (r / p.kw) * p.dy, ix = ix0 + (r % p.kw) * p.dx;
+                    if (iy >= 0 && iy < ih && ix >= 0 && ix < iw) inb[q] |= 1ull << r;
+                }
+            }
+        }
+        auto gather = [&](int kt) {
+            uint8_t *bh = stage_b(kt % NST) + ww * CM * 128 + lane * 4;
+            const Tap *tk = taps + kt * BK + (lane & 3);
+#pragma unroll
+            for (int i = 0; i < CM; ++i) {
+                const Tap t = tk[4 * (i & 3)];
+                const bool ok = (inb[i >> 2] >> t.r) & 1;
+                cp4(bh + i * 128, ok ? xpix[i >> 2] + t.x_off : p.x, ok);
+            }
+        };
+        float sum[HALF_COLS];
+#pragma unroll
+        for (int j = 0; j < HALF_COLS; ++j) sum[j] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < LOOKAHEAD; ++j) {
+            if (j < ktiles) gather(j);
+            cp_commit();
+        }
+        int chunk = 0;
+        for (int kt = 0; kt < ktiles; ++kt) {
+            const int s = kt % NST;
+            cp_wait<LOOKAHEAD - 1>();
+            __syncwarp();
+            if (s_fail || !mbar_wait(&full[s], (kt / NST) & 1)) {
+                s_fail = 1;
+                break;
+            }
+            uint32_t bad = 0;
+            uint8_t *bh = stage_b(s) + ww * CM * 128, *bl = bh + B_TILE;
+#pragma unroll
+            for (int jc = 0; jc < CM / 4; ++jc) {
+                const uint32_t off = (uint32_t)(lane + 32 * jc) * 16;
+                const float4 v = *reinterpret_cast<const float4 *>(bh + off);
+                float4 l;
+                l.x = v.x - tf32_trunc(v.x);
+                l.y = v.y - tf32_trunc(v.y);
+                l.z = v.z - tf32_trunc(v.z);
+                l.w = v.w - tf32_trunc(v.w);
+                bad |= nonfinite_bits(v.x) | nonfinite_bits(v.y) | nonfinite_bits(v.z) | nonfinite_bits(v.w);
+                *reinterpret_cast<float4 *>(bl + off) = l;
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                float4 *hp = reinterpret_cast<float4 *>(stage_a(s) + (wt + j * WORK_THREADS) * 16);
+                float4 *lp = reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(hp) + A_TILE);
+                const float4 v = *hp;
+                float4 l;
+                l.x = v.x - tf32_trunc(v.x);
+                l.y = v.y - tf32_trunc(v.y);
+                l.z = v.z - tf32_trunc(v.z);
+                l.w = v.w - tf32_trunc(v.w);
+                bad |= nonfinite_bits(v.x) | nonfinite_bits(v.y) | nonfinite_bits(v.z) | nonfinite_bits(v.w);
+                *lp = l;
+            }
+            if (bad) s_nonfinite = 1u;
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(conv_leader0 + (uint32_t)(s * 8));
+            const int ahead = kt + LOOKAHEAD, prev = ahead - NST;
+            if (ahead < ktiles) {
+                if (prev >= 0 && !mbar_wait(&empty[prev % NST], (prev / NST) & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                gather(ahead);
+            }
+            cp_commit();
+            if (kt % KC == KC - 1 || kt == ktiles - 1) {
+                if (!mbar_wait(chunk_full, chunk & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                if (s_fail) break;
+                tmem_accumulate(tmem, quarter, col0, sum);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(chunk_empty_leader);
+                ++chunk;
+            }
+        }
+        cp_wait<0>();
+        tc_fence_before();
+        cluster_sync_any();     // pair-wide: both CTAs' nonfinite flags are final
+        tc_fence_after();
+        const uint32_t nonfinite = s_nonfinite | ld_cluster_u32(map_to(smem_u32((const void *)&s_nonfinite_storage), peer));
+        const int co = m0 + quarter * 32 + lane;
+        const bool row_ok = co < p.cog;
+        const int64_t co_abs = (int64_t)grp * p.cog + co;
+        if (!s_fail && chunk == nchunks) {
+            if (nonfinite) {
+                if (row_ok) {
+                    const float *wrow = p.w + co_abs * p.ws0;
+                    for (int j = 0; j < HALF_COLS; ++j) {
+                        const int64_t c = n0 + col0 + j;
+                        if (c >= p.ncols) break;
+                        const int64_t img = c / p.hw, pix = c % p.hw;
+                        const int64_t oy = pix / p.ow, ox = pix % p.ow;
+                        const int y0 = (int)(oy * p.sy - p.py), x0 = (int)(ox * p.sx - p.px);
+                        const int64_t base = img * p.xs[0] + (int64_t)grp * p.cg * p.xs[1] + (int64_t)y0 * p.xs[2] +
+                                             (int64_t)x0 * p.xs[3];
+                        float acc = 0.0f;
+                        for (int k = 0; k < p.kk; ++k) {
+                            const Tap t = taps[k];
+                            const int iy = y0 + (t.r / p.kw) * p.dy, ix = x0 + (t.r % p.kw) * p.dx;
+                            const float xv = (iy >= 0 && iy < ih && ix >= 0 && ix < iw) ? p.x[base + t.x_off] : 0.0f;
+                            acc = fmaf(wrow[k], xv, acc);
+                        }
+                        p.y[(img * p.co_total + co_abs) * p.hw + pix] = acc;
+                    }
+                }
+            } else {
+                const bool vec_ok = (p.hw % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.y) & 15) == 0);
+#pragma unroll
+                for (int c = 0; c < HALF_COLS / 16; ++c) {
+                    uint32_t r[16];
+                    tmem_ld16(tmem + XCOL + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(col0 + c * 16), r);
+                    tmem_wait_ld();
+                    if (!row_ok) continue;
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = sum[c * 16 + j] + __uint_as_float(r[j]);
+                    const int64_t c0 = n0 + col0 + c * 16;
+                    const int64_t img = c0 / p.hw, pix = c0 % p.hw;
+                    if (vec_ok && c0 + 16 <= p.ncols && pix + 16 <= p.hw) {
+                        float *dst = p.y + (img * p.co_total + co_abs) * p.hw + pix;
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4)
+                            *reinterpret_cast<float4 *>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int64_t cc = c0 + j;
+                            if (cc < p.ncols) p.y[((cc / p.hw) * p.co_total + co_abs) * p.hw + cc % p.hw] = v[j];
+                        }
+                    }
+                }
+            }
+        }
+    }
+    if (warp < WORK_WARP0) cluster_sync_any();
+    tc_fence_before();
+    cluster_sync_any();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+    if (threadIdx.x == 0 && s_fail) atomicOr(p.status, KX_TIMEOUT_FLAG);
+}
+
 // Weights [co][cg][kh][kw] under any strides -> dense rows of `pitch` floats
 // in the reference's tap order (ci, ky, kx), zero beyond the taps: the layout
 // the weight tensor map reads (16-byte aligned rows).
@@ -479,6 +806,39 @@ int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, co
     p.kk = (int)kk;
     p.ncols = ncols;
     p.status = h->flags + kStatusWord;
+    const int table_pair = (int)((kk + BK - 1) / BK * BK) * (int)sizeof(Tap);
+    // CTA pairs (256 channels x 256 pixels) when the group has 256+ output
+    // channels and the pairs fill the SMs (a 256-wide one-SM conv tile
+    // gathers every input element once per 128 channels; a pair once per 256)
+    {
+        const int64_t pm = cog / 256;   // whole channel pairs only
+        const int64_t pair_ctas = 2 * pm * ((ncols + 255) / 256) * groups;
+        if (pm >= 1 && cog % 256 == 0 && (pair_ctas >= 4LL * h->sm_count || h->f32_variant == KX_F32_3XTF32) &&
+            PAIR_FIXED_SMEM + table_pair <= SMEM_LIMIT) {
+            const int smem = PAIR_FIXED_SMEM + table_pair;
+            auto k = conv_3xtf32_pair_kernel;
+            cudaError_t ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (ce == cudaSuccess) {
+                cudaLaunchConfig_t cfg = {};
+                cfg.gridDim = dim3((unsigned)pair_ctas / (unsigned)groups, (unsigned)groups, 1);
+                cfg.blockDim = dim3(NTHREADS, 1, 1);
+                cfg.dynamicSmemBytes = smem;
+                cfg.stream = h->stream;
+                cudaLaunchAttribute attr[1];
+                attr[0].id = cudaLaunchAttributeClusterDimension;
+                attr[0].val.clusterDim.x = 2;
+                attr[0].val.clusterDim.y = 1;
+                attr[0].val.clusterDim.z = 1;
+                cfg.attrs = attr;
+                cfg.numAttrs = 1;
+                ce = cudaLaunchKernelEx(&cfg, k, mw, p);
+                if (ce == cudaSuccess) ce = cudaGetLastError();
+            }
+            *kernel_name = "conv_tc_3xtf32_pair_256x256";
+            ++h->launches;
+            return ce == cudaSuccess ? KX_OK : h->cuda_fail(ce);
+        }
+    }
     // tile width from the wave model (as the GEMM's), within shared memory
     const int64_t tm = (cog + BM - 1) / BM;
     auto cost = [&](int bn) {

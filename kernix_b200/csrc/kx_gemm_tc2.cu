@@ -66,77 +66,6 @@ struct Params {
     uint32_t *status;
 };
 
-// f32 accumulate, tf32 A and B, M = 256 (the pair), N = the pair's width.
-__host__ __device__ constexpr uint32_t idesc_pair(bool b_mn_major, int bnp) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(bnp >> 3) << 17) |
-           ((uint32_t)(BMP >> 4) << 24);
-}
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-// Address of the same shared-memory location in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t map_to(uint32_t local, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
-    return r;
-}
-// Every thread of both CTAs arrives once per phase; threads may reach it
-// from divergent paths (no .aligned).
-__device__ __forceinline__ void cluster_sync_any() {
-    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
-// Arrive on a barrier of either CTA of the pair (default semantics; the
-// shared-memory writes it publishes were made visible to the tensor core's
-// proxy by the writer's fence.proxy.async).  An explicit .release.cluster
-// here cost a cluster-scope memory barrier per warp and k-tile.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-__device__ __forceinline__ void mma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-    const uint32_t z = 0;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}"
-        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z), "r"(z),
-          "r"(z), "r"(z), "r"(z)
-        : "memory");
-}
-// Completion of the leader's MMAs issued so far -> one arrive on the barrier
-// at `cluster_addr` (in either CTA of the pair).
-__device__ __forceinline__ void commit_pair(uint32_t cluster_addr) {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
-                 : "memory");
-}
-// Bounded wait with cluster-scope acquire: the arrivals come from both CTAs
-// (remote arrives carry release.cluster).
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity) {
-    const uint32_t a = smem_u32(bar);
-    uint64_t deadline = 0;
-    while (true) {
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(done)
-            : "r"(a), "r"(parity)
-            : "memory");
-        if (done) return true;
-        const uint64_t now = globaltimer();
-        if (deadline == 0) deadline = now + WAIT_NS;
-        else if (now > deadline) return false;
-    }
-}
-__device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t cluster_addr) {
-    uint32_t v;
-    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(cluster_addr) : "memory");
-    return v;
-}
-
 template <bool B_MN, int HB>
 __global__ void __launch_bounds__(NTHREADS, 1)
 gemm_3xtf32_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,

@@ -44,6 +44,8 @@ GEOMETRIES = [
     ((2, 64, 9, 11), (130, 1, 1), dict(stride=(1, 1), padding=(0, 0), dilation=(1, 1), groups=1)),
     ((1, 8, 30, 30), (16, 5, 5), dict(stride=(3, 3), padding=(2, 2), dilation=(1, 1), groups=1)),
     ((2, 3, 40, 40), (64, 7, 7), dict(stride=(2, 2), padding=(3, 3), dilation=(1, 1), groups=1)),
+    ((3, 40, 13, 11), (512, 3, 3), dict(stride=(1, 1), padding=(1, 1), dilation=(1, 1), groups=1)),
+    ((2, 32, 9, 9), (512, 3, 3), dict(stride=(1, 1), padding=(0, 1), dilation=(1, 1), groups=2)),
 ]
 
 
@@ -55,7 +57,8 @@ def test_conv_tc_geometries(kx, torch_cuda, tc, xs, ws, opts):
     x = rng.uniform(-1, 1, xs).astype(np.float32)
     wt = rng.normal(0, math.sqrt(2 / (c // opts["groups"] * kh * kw)), (co, c // opts["groups"], kh, kw)).astype(np.float32)
     _check(kx, torch_cuda, x, wt, opts)
-    assert tc.last_kernel == "conv_tc_3xtf32_128x128", tc.last_kernel
+    expect = "conv_tc_3xtf32_pair_256x256" if (co // opts["groups"]) % 256 == 0 else "conv_tc_3xtf32_128x128"
+    assert tc.last_kernel == expect, tc.last_kernel
 
 
 def test_conv_tc_reversed_and_strided_input(kx, torch_cuda, tc):
@@ -74,15 +77,17 @@ def test_conv_tc_reversed_and_strided_input(kx, torch_cuda, tc):
     assert tc.last_kernel == "conv_tc_3xtf32_128x128"
 
 
-def test_conv_tc_nonfinite_input_tiles(kx, torch_cuda, tc):
+@pytest.mark.parametrize("co", [40, 256])
+def test_conv_tc_nonfinite_input_tiles(kx, torch_cuda, tc, co):
     """inf/NaN in the input: the affected tiles are recomputed with FMA, so
-    the result keeps IEEE propagation (no NaN from inf * 0 in a cross term)."""
+    the result keeps IEEE propagation (no NaN from inf * 0 in a cross term);
+    256 output channels take the CTA-pair kernel."""
     torch = torch_cuda
     rng = np.random.default_rng(4)
     x = rng.uniform(-1, 1, (2, 32, 12, 12)).astype(np.float32)
     x[0, 3, 5, 5] = np.inf
     x[1, 7, 0, 0] = np.nan
-    wt = np.abs(rng.normal(0, 0.1, (40, 32, 3, 3))).astype(np.float32)
+    wt = np.abs(rng.normal(0, 0.1, (co, 32, 3, 3))).astype(np.float32)
     opts = kx.Conv2dOptions(padding=(1, 1))
     got = kx.conv2d(to_dev(x, torch), to_dev(wt, torch), opts).cpu().numpy()
     tc.set_f32_variant(1)
