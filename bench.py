@@ -501,23 +501,48 @@ def run_reference(args, rank, world):
 
 
 # ---------------------------------------------------------------------------
-# the other workloads (one GPU): c1..c4
+# the other workloads: c1, c2 (one GPU), c3, c4 (batch split over the ranks)
 # ---------------------------------------------------------------------------
-def _timed(fn, steps, warmup, dev):
+def _timed(fn, steps, warmup, dev, world=1, handle=None):
     """Average ms per call over ``steps`` after ``warmup`` calls, CUDA events
-    on the current stream, with the clock record of the timed region."""
+    on the current stream, with the clock record of the timed region and the
+    number of kernels ``handle`` launched in it; with several ranks the region
+    is bracketed by barriers and the time is the maximum over ranks."""
     import torch
+    import torch.distributed as dist
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[dev.index])
+        torch.cuda.synchronize(dev)
     for _ in range(warmup):
         fn()
-    torch.cuda.synchronize(dev)
+    barrier()
+    launches0 = handle.launches if handle is not None else 0
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index or 0) as clk:
         s.record()
         for _ in range(steps):
             fn()
         e.record()
-        e.synchronize()
-    return s.elapsed_time(e) / steps, clk.summary()
+        barrier()
+    ms = s.elapsed_time(e) / steps
+    launches = handle.launches - launches0 if handle is not None else None
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, clk.summary(), launches
+
+
+def _max_over_ranks(values: list[float], world: int, dev) -> list[float]:
+    if world == 1:
+        return values
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(values, dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t.tolist()]
 
 
 def _pipe_of(kernel: str) -> str:
@@ -528,25 +553,33 @@ def _pipe_of(kernel: str) -> str:
     return "fp32-simt"
 
 
-def run_workload(args):
-    """Measure c1..c4 on cuda:0 and check the timed output against the oracle."""
+def run_workload(args, rank=0, world=1, local=0):
+    """Measure c1..c4 and check the timed output against the oracle.
+
+    c1 and c2 run on one GPU (replicas only). c3 and c4 shard their batch
+    across the ranks (contiguous images, or (batch, head) units in whole
+    batches), every rank generating its own window of the seeded stream; no
+    collective touches the data, the time is the maximum over ranks and the
+    value the whole job's FLOPs over it (strong scaling)."""
     import torch
     import kernix_b200 as kx
     import oracle
     from kernix_b200 import rng
-    dev = torch.device("cuda", 0)
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    h = kx.handle(0)
-    peaks, _ = measured_peaks()
+    h = kx.handle(local)
+    peaks, peak_src = measured_peaks()
     w = args.workload
-    res = {"metric": METRIC, "workload": f"{w}: {CONFIG_TEXT[w]}", "n_gpus": 1, "steps": args.steps,
+    if world > 1 and w in ("c1", "c2"):
+        raise SystemExit(f"{w} is a single-GPU workload (replicas only): run it with one process")
+    res = {"metric": METRIC, "workload": f"{w}: {CONFIG_TEXT[w]}", "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "data": f"synthetic (SplitMix64 seed(s) {SEEDS[w]})"}
     if w == "c1":
         v = rng.uniform(SEEDS["c1"][0], 2 * 512 * 512, -1.0, 1.0, np.float32)
         a_np, b_np = v[:512 * 512].reshape(512, 512), v[512 * 512:].reshape(512, 512)
         a, b = torch.from_numpy(a_np).to(dev), torch.from_numpy(b_np).to(dev)
         c = torch.empty(512, 512, device=dev)
-        ms, clocks = _timed(lambda: kx.matmul_into(a, b, c), args.steps, args.warmup, dev)
+        ms, clocks, launches = _timed(lambda: kx.matmul_into(a, b, c), args.steps, args.warmup, dev, 1, h)
         flops = 2.0 * 512 ** 3
         exp, ab = oracle.gemm_dot2(oracle.View.of(a_np), oracle.View.of(b_np))
         err = float(np.max(np.abs(c.cpu().numpy().astype(np.float64) - exp) / ab))
@@ -559,7 +592,7 @@ def run_workload(args):
         a_np, bt_np = v[:n * n].reshape(n, n), v[n * n:].reshape(n, n)
         a, bt = torch.from_numpy(a_np).to(dev), torch.from_numpy(bt_np).to(dev)
         c = torch.empty(n, n, dtype=torch.float64, device=dev)
-        ms, clocks = _timed(lambda: kx.matmul_into(a, bt.t(), c), args.steps, args.warmup, dev)
+        ms, clocks, launches = _timed(lambda: kx.matmul_into(a, bt.t(), c), args.steps, args.warmup, dev, 1, h)
         flops = 2.0 * n ** 3
         worst = 0.0
         for r in (0, n // 3, n - 1):
@@ -569,11 +602,19 @@ def run_workload(args):
         res.update(dtype="f64", config={"workload": "c2", "M": n, "N": n, "K": n, "b_layout": "transposed view",
                                         "l2": "inputs larger than L2 (268 MB each)"})
     elif w == "c3":
-        nb = args.batch or 16
+        total = args.batch or 16
+        if total % world:
+            raise SystemExit(f"c3: batch {total} does not split over {world} ranks")
+        nb = total // world
         shape = (nb, 32, 2048, 128)
         cnt = int(np.prod(shape))
+        # Q, K and V are consecutive windows of one stream of total * 32 * 2048 * 128
+        # values each; this rank's batches start at rank * cnt inside each
         host = torch.empty(3 * cnt, dtype=torch.float32, pin_memory=True)
-        rng.normal(SEEDS["c3"][0], 3 * cnt, 1.0, np.float32, out=host.numpy())
+        hv = host.numpy()
+        for j in range(3):
+            rng.normal(SEEDS["c3"][0], cnt, 1.0, np.float32, out=hv[j * cnt:(j + 1) * cnt],
+                       start=j * cnt * world + rank * cnt)
         q = host[:cnt].view(shape).to(dev)
         k_ = host[cnt:2 * cnt].view(shape).to(dev)
         v_ = host[2 * cnt:].view(shape).to(dev)
@@ -586,12 +627,12 @@ def run_workload(args):
             kx.matmul_into(q, k_.transpose(2, 3), sc)
             kx.softmax_temperature_into(sc, -1, t, pr)
             kx.matmul_into(pr, v_, o)
-        ms, clocks = _timed(step, args.steps, args.warmup, dev)
-        qk_ms, _ = _timed(lambda: kx.matmul_into(q, k_.transpose(2, 3), sc), 2, 1, dev)
+        ms, clocks, launches = _timed(step, args.steps, args.warmup, dev, world, h)
+        qk_ms, _, _ = _timed(lambda: kx.matmul_into(q, k_.transpose(2, 3), sc), 2, 1, dev, world)
         qk_kernel = h.last_kernel
-        sm_ms, _ = _timed(lambda: kx.softmax_temperature_into(sc, -1, t, pr), 2, 1, dev)
-        pv_ms, _ = _timed(lambda: kx.matmul_into(pr, v_, o), 2, 1, dev)
-        flops = 2.0 * 2 * nb * 32 * 2048 * 2048 * 128
+        sm_ms, _, _ = _timed(lambda: kx.softmax_temperature_into(sc, -1, t, pr), 2, 1, dev, world)
+        pv_ms, _, _ = _timed(lambda: kx.matmul_into(pr, v_, o), 2, 1, dev, world)
+        flops = 2.0 * 2 * total * 32 * 2048 * 2048 * 128
         # parity: two heads, three rows each
         worst_s = worst_o = worst_p = 0.0
         for bi, hi in ((0, 0), (nb - 1, 31)):
@@ -608,33 +649,45 @@ def run_workload(args):
                 worst_p = max(worst_p, float(np.max(np.abs(prow - truth).astype(np.float64) / (tol * np.abs(truth).astype(np.float64) + 1e-38))))
                 exp, ab = oracle.gemm_dot2(oracle.View(prow, (1, 2048), (2048, 1)), oracle.View.of(vh))
                 worst_o = max(worst_o, float(np.max(np.abs(o[bi, hi, r].cpu().numpy() - exp[0]) / ab[0])))
-        check = {"heads_checked": 2, "rows_per_head": 3, "S_max_err_over_sum_abs": worst_s,
+        worst_s, worst_p, worst_o = _max_over_ranks([worst_s, worst_p, worst_o], world, dev)
+        check = {"heads_checked": 2 * world, "rows_per_head": 3, "S_max_err_over_sum_abs": worst_s,
                  "P_max_err_over_tolerance": worst_p, "O_max_err_over_sum_abs": worst_o,
                  "pass": worst_s <= 2e-6 and worst_o <= 2e-6 and worst_p <= 1.0}
-        sm_bytes = 2.0 * sc.numel() * 4
+        sm_bytes = 2.0 * sc.numel() * 4 * world
         res["parts"] = {"qk_ms": round(qk_ms, 3), "qk_tflops": round(flops / 2 / qk_ms / 1e9, 2), "qk_kernel": qk_kernel,
                         "softmax_ms": round(sm_ms, 3), "softmax_gbs": round(sm_bytes / sm_ms / 1e6, 1),
                         "softmax_frac_of_hbm": round(sm_bytes / sm_ms / 1e6 / peaks["hbm_gbs"], 3),
                         "pv_ms": round(pv_ms, 3), "pv_tflops": round(flops / 2 / pv_ms / 1e9, 2),
                         "pv_kernel": h.last_kernel}
-        res.update(dtype="f32", config={"workload": "c3", "batch": nb, "heads": 32, "seq": 2048, "d": 128,
+        res.update(dtype="f32", config={"workload": "c3", "batch": total, "heads": 32, "seq": 2048, "d": 128,
+                                        "parallelism": f"batch{world}: {nb} batches x 32 heads per rank, "
+                                                       "no collective" if world > 1 else "one GPU",
                                         "l2": "inputs larger than L2 (S and P 8.6 GB at batch 16)"})
     elif w == "c4":
-        nb = args.batch or 64
+        total = args.batch or 64
+        if total % world:
+            raise SystemExit(f"c4: batch {total} does not split over {world} ranks")
+        nb = total // world
         xn = nb * 128 * 56 * 56
-        x_np = rng.uniform(SEEDS["c4"][0], 64 * 128 * 56 * 56, -1.0, 1.0, np.float32)[:xn].reshape(nb, 128, 56, 56)
+        # this rank's images: a window of the input stream; weights on every rank
+        x_np = rng.uniform(SEEDS["c4"][0], xn, -1.0, 1.0, np.float32, start=rank * xn).reshape(nb, 128, 56, 56)
         w_np = rng.normal(SEEDS["c4"][1], 256 * 128 * 9, math.sqrt(2.0 / 1152.0), np.float32).reshape(256, 128, 3, 3)
         x, wt = torch.from_numpy(x_np).to(dev), torch.from_numpy(w_np).to(dev)
         opts = kx.Conv2dOptions(padding=(1, 1))
         y = kx.conv2d(x, wt, opts)
-        ms, clocks = _timed(lambda: kx.conv2d_into(x, wt, y, opts), args.steps, args.warmup, dev)
-        flops = 2.0 * 256 * 1152 * nb * 56 * 56
+        ms, clocks, launches = _timed(lambda: kx.conv2d_into(x, wt, y, opts), args.steps, args.warmup, dev,
+                                      world, h)
+        flops = 2.0 * 256 * 1152 * total * 56 * 56
         sub = np.ascontiguousarray(w_np[[0, 255]])
         d2, ab = oracle.conv2d_dot2(oracle.View.of(x_np[:1]), oracle.View.of(sub), padding=(1, 1))
         got = y[:1, [0, 255]].cpu().numpy().astype(np.float64)
         err = float(np.max(np.abs(got - d2) / np.maximum(ab, 1e-300)))
-        check = {"outputs_checked": int(got.size), "max_err_over_sum_abs": err, "bound": 2e-6, "pass": err <= 2e-6}
-        res.update(dtype="f32", config={"workload": "c4", "batch": nb, "c_in": 128, "hw": 56, "c_out": 256,
+        err, = _max_over_ranks([err], world, dev)
+        check = {"outputs_checked": int(got.size) * world, "max_err_over_sum_abs": err, "bound": 2e-6,
+                 "pass": err <= 2e-6}
+        res.update(dtype="f32", config={"workload": "c4", "batch": total, "c_in": 128, "hw": 56, "c_out": 256,
+                                        "parallelism": f"batch{world}: {nb} images per rank, weights on every "
+                                                       "rank, no collective" if world > 1 else "one GPU",
                                         "kernel_hw": 3, "stride": 1, "pad": 1,
                                         "l2": "x 103 MB + y 206 MB at batch 64: larger than L2"})
     else:
@@ -646,11 +699,13 @@ def run_workload(args):
     sm_max = clocks.get("sm_max_mhz") or peaks.get("sm_max_mhz", 1965.0)
     peak, basis = pipe_peak(pipe, peaks, float(sm_max))
     res.update(value=round(tflops, 3), unit="TFLOP/s", ms_per_step=round(ms, 4), higher_is_better=True,
+               scaling="strong", vs_baseline=None, gpu_launches=launches,
                kernel=kernel, clocks=clocks, check=check,
                roofline={"bound": "tensor" if pipe != "fp32-simt" else "fp32 pipe", "pipe": pipe,
-                         "achieved": round(tflops, 3), "peak": round(peak, 3), "unit": "TFLOP/s",
-                         "frac": round(tflops / peak, 4), "peak_basis": basis})
-    return res
+                         "achieved": round(tflops / world, 3), "peak": round(peak, 3), "unit": "TFLOP/s",
+                         "frac": round(tflops / world / peak, 4), "per": "GPU",
+                         "peak_basis": basis + (" (of measured)" if peak_src == "measured" else "")})
+    return res if rank == 0 else None
 
 
 def main():
@@ -670,7 +725,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
     ap.add_argument("--workload", choices=["c5", "c1", "c2", "c3", "c4"], default="c5",
-                    help="c5 is the headline (this bench line); c1..c4 print their own measurement on one GPU")
+                    help="c5 is the headline (this bench line); c1..c4 print their own measurement (c3 and c4 "
+                         "split their batch over the ranks under torchrun)")
     ap.add_argument("--batch", type=int, default=0, help="c3/c4: batch size (default: the workload's)")
     ap.add_argument("--size", type=int, default=8192,
                     help="profiling aid: M=N=K=size with row stride size+512 (8192 is the workload)")
@@ -683,7 +739,25 @@ def main():
     if args.workload != "c5":
         if args.size == 8192:
             args.size = 0
-        print(json.dumps(run_workload(args)), flush=True)
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "workload": args.workload,
+                                  "unavailable": "the reference arm times the headline workload (c5) only"}))
+            return
+        import torch
+        import torch.distributed as dist
+        if world > 1:
+            from datetime import timedelta
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+        try:
+            res = run_workload(args, rank, world, local)
+            if res is not None:
+                print(json.dumps(res), flush=True)
+        finally:
+            if world > 1:
+                dist.barrier(device_ids=[local])
+                dist.destroy_process_group()
         return
     if world != args.gpus:
         print(f"warning: WORLD_SIZE={world} but --gpus {args.gpus}", file=sys.stderr)

@@ -47,15 +47,20 @@ def uniform(seed: int, n: int, low: float, high: float, dtype=np.float32, out: n
     return out
 
 
-def normal(seed: int, n: int, std: float = 1.0, dtype=np.float32, out: np.ndarray | None = None) -> np.ndarray:
-    """Standard normals (times ``std``) by Box-Muller over the seeded stream."""
+def normal(seed: int, n: int, std: float = 1.0, dtype=np.float32, out: np.ndarray | None = None,
+           start: int = 0) -> np.ndarray:
+    """Standard normals (times ``std``) by Box-Muller over the seeded stream;
+    ``start`` (even: values come in pairs) skips that many values, so a
+    window of the stream is generated directly."""
+    if start % 2:
+        raise ValueError("normal(): start must be even")
     if out is None:
         out = np.empty(n, dtype=dtype)
     pairs = (n + 1) // 2
     step = _CHUNK // 2
     for s in range(0, pairs, step):
         c = min(step, pairs - s)
-        f = fractions(seed, 2 * s, 2 * c)
+        f = fractions(seed, start + 2 * s, 2 * c)
         u1, u2 = f[0::2], f[1::2]
         r = np.sqrt(-2.0 * np.log1p(-u1)) * float(std)
         z = np.empty(2 * c, dtype=np.float64)

@@ -78,3 +78,22 @@ def test_sharded_matmul_gathers_full_product(world, m, piece):
     for rank, err, has_nan in results:
         assert not has_nan, rank
         assert err < 1e-5, (rank, err)
+
+
+def test_stream_windows_reassemble_the_unsharded_inputs():
+    """The batch-sharded attention and conv measurements have every rank
+    generate its own window of the seeded streams; the windows of all ranks
+    put together must be the single-process inputs."""
+    from kernix_b200 import rng
+    total, world = 12, 4            # values per batch element: 6 (even, as normal() pairs them)
+    per = 6
+    full = rng.normal(7, 3 * total * per, 1.0, np.float64)
+    cnt = total // world * per
+    for j in range(3):              # Q, K, V: consecutive segments of one stream
+        parts = [rng.normal(7, cnt, 1.0, np.float64, start=j * cnt * world + r * cnt) for r in range(world)]
+        assert np.array_equal(np.concatenate(parts), full[j * total * per:(j + 1) * total * per])
+    full_u = rng.uniform(8, total * per, -1.0, 1.0, np.float32)
+    parts = [rng.uniform(8, cnt, -1.0, 1.0, np.float32, start=r * cnt) for r in range(world)]
+    assert np.array_equal(np.concatenate(parts), full_u)
+    with pytest.raises(ValueError):
+        rng.normal(7, 4, start=3)
