@@ -22,6 +22,7 @@
 // the nonfinite fallback are those of the GEMM kernel (kx_gemm_tc.cu): with
 // inf/NaN in a tile's inputs the tile is recomputed with f32 FMA in k order,
 // as the SIMT implicit GEMM does.  Every mbarrier wait is bounded.
+#include <algorithm>
 #include <cstring>
 
 #include "gemm_simt.cuh"
@@ -716,6 +717,355 @@ conv_3xtf32_pair_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_co
     if (threadIdx.x == 0 && s_fail) atomicOr(p.status, KX_TIMEOUT_FLAG);
 }
 
+// ---------------------------------------------------------------------------
+// Patch-staged CTA pair: 256 output channels x 224 pixels of one image.
+//
+// The gathered kernels above read every input element once per tap from L2
+// (nine times for a 3x3 filter).  Here each CTA stages, per 16 input
+// channels, the input rows under its 112 output pixels with ONE TMA box
+// (zero-filled outside the image, which is the padding), and the worker warps
+// build each k-tile's im2col tile from shared memory.  16 channels are
+// exactly kh*kw k-tiles, so the k-tiles of a chunk never straddle two chunks;
+// two chunk buffers let the next chunk's box land while this one is used.
+// Needs a unit inner input stride, the other strides 16-byte multiples, and
+// a patch row (the output row's input columns, widened to 16-byte bounds) of
+// at most 256 floats.
+//   warp 0   weight tiles by TMA (as above)
+//   warp 1   TMEM owner; the pair leader's lane 0 issues the MMAs (N = 224)
+//   warp 2   patch boxes by TMA
+//   warps 4..11  build B hi/lo from the patch, split A's lo part, fold the
+//            hi*hi chunks, store the output
+// ---------------------------------------------------------------------------
+constexpr int PP_HB = 112;                               // pixels per CTA (half the pair's 224)
+constexpr int PP_B_TILE = PP_HB * BK * 4;                // 7 KB
+constexpr int PP_STAGE = 2 * A_TILE + 2 * PP_B_TILE;     // 30 KB
+constexpr int PP_NST = 6;                                // most stages; fewer when the patch buffers are large
+constexpr int PP_CH = 16;                                // input channels per patch chunk
+constexpr int PP_ITERS = PP_HB * BK / WORK_THREADS;      // B elements per worker thread and k-tile
+static_assert(PP_HB * BK == PP_ITERS * WORK_THREADS, "B tile split");
+static_assert(PP_STAGE % 1024 == 0, "stage alignment");
+static_assert(3 * PP_NST + 2 + 4 + 1 <= BAR_BYTES / 8, "barrier area");
+
+struct PatchGeom {
+    int x0;                  // first input column of every patch (a multiple of 4; negative on left padding)
+    int pitch;               // floats per patch row (a multiple of 4, at most 256)
+    int prows;               // input rows per patch
+    int tpi;                 // pair tiles per image
+    int nimg;                // images
+    uint32_t patch_bytes;    // one chunk: PP_CH * prows * pitch * 4
+    uint32_t patch_stride;   // patch_bytes rounded up to 1 KB
+};
+
+template <int NST>
+__global__ void __launch_bounds__(NTHREADS, 1)
+conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                         const __grid_constant__ Params p, const __grid_constant__ PatchGeom g) {
+    constexpr int HB = PP_HB, BNP = 2 * PP_HB, B_TILE = PP_B_TILE, STAGE_BYTES = PP_STAGE;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *patch = smem + NST * STAGE_BYTES;
+    uint64_t *full = reinterpret_cast<uint64_t *>(patch + 2 * g.patch_stride);
+    uint64_t *conv = full + NST;
+    uint64_t *empty = conv + NST;
+    uint64_t *chunk_full = empty + NST;
+    uint64_t *chunk_empty = chunk_full + 1;
+    uint64_t *pfull = chunk_empty + 1;      // [2]: patch chunk landed
+    uint64_t *pempty = pfull + 2;           // [2]: patch chunk read by every worker warp
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pempty + 2);
+    int32_t *tap_off = reinterpret_cast<int32_t *>(reinterpret_cast<uint8_t *>(full) + BAR_BYTES);
+    __shared__ int s_fail_storage;
+    __shared__ uint32_t s_nonfinite_storage;
+    volatile int &s_fail = s_fail_storage;
+    volatile uint32_t &s_nonfinite = s_nonfinite_storage;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const uint32_t peer = rank ^ 1u;
+    const int tiles_m = (int)(p.cog / 256), tiles_n = g.nimg * g.tpi;
+    int tm, tn;
+    raster((int)(blockIdx.x >> 1), tiles_m, tiles_n, 8, tm, tn);
+    const int m0 = tm * 256 + (int)rank * BM;            // this CTA's output channels
+    const int img = tn / g.tpi;
+    const int hw = (int)p.hw, ow = (int)p.ow;
+    const int p0 = (tn % g.tpi) * BNP;                   // the pair's first pixel in the image
+    const int q0 = p0 + (int)rank * HB;                  // this CTA's first pixel
+    const int iy0 = (min(q0, hw - 1) / ow) * p.sy - p.py;   // the patch's first input row
+    const int grp = blockIdx.y;
+    const int khw = p.kh * p.kw;
+    const int ktiles = (p.kk + BK - 1) / BK;
+    const int nchunks = (ktiles + KC - 1) / KC;
+    const int npatch = (ktiles + khw - 1) / khw;
+    const int ch_floats = g.prows * g.pitch;
+
+    // patch offset of chunk-local tap kl = (ci, ky, kx)
+    for (int kl = threadIdx.x; kl < PP_CH * khw; kl += NTHREADS) {
+        const int ci = kl / khw, r = kl % khw;
+        tap_off[kl] = ci * ch_floats + (r / p.kw) * p.dy * g.pitch + (r % p.kw) * p.dx;
+    }
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NST; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&conv[s], 2 * WORK_WARPS);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(chunk_full, 1);
+        mbar_init(chunk_empty, 2 * WORK_WARPS);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&pfull[b], 1);
+            mbar_init(&pempty[b], WORK_WARPS);
+        }
+        s_fail = 0;
+        s_nonfinite = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    cluster_sync_any();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    auto stage_a = [&](int s) { return smem + s * STAGE_BYTES; };
+    auto stage_b = [&](int s) { return smem + s * STAGE_BYTES + 2 * A_TILE; };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;
+            for (int kt = 0; kt < ktiles && !s_fail; ++kt) {
+                const int s = kt % NST;
+                if (kt >= NST && !mbar_wait(&empty[s], ((kt / NST) - 1) & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                mbar_expect_tx(&full[s], A_TILE);
+                tma_load_3d(stage_a(s), &tmW, kt * BK, m0, grp, &full[s]);
+                issued = kt + 1;
+            }
+            for (int s = 0; s < NST && s < issued; ++s) {
+                const int last = s + NST * ((issued - 1 - s) / NST);
+                mbar_wait(&full[s], (last / NST) & 1);
+            }
+        }
+    } else if (warp == 1) {
+        if (leader && lane == 0) {
+            constexpr uint32_t idesc = idesc_pair(false, BNP);
+            const uint32_t chunk_full_peer = map_to(smem_u32(chunk_full), peer);
+            for (int kt = 0; kt < ktiles; ++kt) {
+                const int s = kt % NST;
+                const int chunk = kt / KC, kin = kt % KC;
+                if (kin == 0 && chunk > 0 && (s_fail || !mbar_wait_cluster(chunk_empty, (chunk - 1) & 1))) {
+                    s_fail = 1;
+                    break;
+                }
+                if (s_fail || !mbar_wait_cluster(&conv[s], (kt / NST) & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_hi = smem_u32(stage_a(s)), a_lo = a_hi + A_TILE;
+                const uint32_t b_hi = smem_u32(stage_b(s)), b_lo = b_hi + B_TILE;
+#pragma unroll
+                for (int ks = 0; ks < BK / 8; ++ks) {
+                    const uint64_t dah = desc_k_sw64(a_hi + ks * 32), dal = desc_k_sw64(a_lo + ks * 32);
+                    const uint64_t dbh = desc_k_sw64(b_hi + ks * 32), dbl = desc_k_sw64(b_lo + ks * 32);
+                    mma_pair(tmem, dah, dbh, idesc, (kin > 0 || ks > 0) ? 1u : 0u);
+                    mma_pair(tmem + XCOL, dah, dbl, idesc, (kt > 0 || ks > 0) ? 1u : 0u);
+                    mma_pair(tmem + XCOL, dal, dbh, idesc, 1u);
+                }
+                const uint32_t e_local = smem_u32(&empty[s]);
+                commit_pair(e_local);
+                commit_pair(map_to(e_local, peer));
+                if (kin == KC - 1 || kt == ktiles - 1) {
+                    commit_pair(smem_u32(chunk_full));
+                    commit_pair(chunk_full_peer);
+                }
+            }
+            if (s_fail) {
+                commit_pair(smem_u32(chunk_full));
+                commit_pair(chunk_full_peer);
+            }
+        }
+    } else if (warp == 2) {
+        if (lane == 0) {
+            int issued = 0;
+            const int c0 = grp * (int)p.cg;
+            for (int j = 0; j < npatch && !s_fail; ++j) {
+                const int b = j & 1;
+                if (j >= 2 && !mbar_wait(&pempty[b], ((j >> 1) - 1) & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                mbar_expect_tx(&pfull[b], g.patch_bytes);
+                tma_load_4d(patch + b * g.patch_stride, &tmX, g.x0, iy0, c0 + PP_CH * j, img, &pfull[b]);
+                issued = j + 1;
+            }
+            for (int b = 0; b < 2 && b < issued; ++b) {
+                const int last = b + 2 * ((issued - 1 - b) / 2);
+                mbar_wait(&pfull[b], (last >> 1) & 1);
+            }
+        }
+    } else if (warp >= WORK_WARP0) {
+        const int wt = threadIdx.x - WORK_WARP0 * 32;
+        const int ww = warp - WORK_WARP0;
+        const int quarter = warp & 3;
+        const int col0 = (ww >> 2) * HB;
+        const uint32_t conv_leader0 = map_to(smem_u32(&conv[0]), 0);
+        const uint32_t chunk_empty_leader = map_to(smem_u32(chunk_empty), 0);
+        // Element i of this thread in every B tile: pixel row r = 8 * (2i + ww/4) + lane/4,
+        // tap k = 4 * (ww%4) + lane%4 of the k-tile.  The tile is K-major with the
+        // 64-byte swizzle (as the TMA writes A): (r, k) at byte 64 r + 16 ((k/4) ^ ((r/2)%4))
+        // + 4 (k%4), here 1024 i + 512 (ww/4) + 64 (lane/4) + 16 ((ww%4) ^ (lane/8)) + 4 (lane%4):
+        // each warp store covers 32 distinct banks.
+        const int kq = 4 * (ww & 3) + (lane & 3);
+        int pix[PP_ITERS];
+        {
+            const int oy_a = min(q0, hw - 1) / ow;
+#pragma unroll
+            for (int i = 0; i < PP_ITERS; ++i) {
+                const int q = q0 + 8 * (2 * i + (ww >> 2)) + (lane >> 2);
+                pix[i] = -1;
+                if (q < hw) {
+                    const int oy = q / ow, ox = q % ow;
+                    pix[i] = (oy - oy_a) * p.sy * g.pitch + (ox * p.sx - p.px - g.x0);
+                }
+            }
+        }
+        float sum[HB];
+#pragma unroll
+        for (int j = 0; j < HB; ++j) sum[j] = 0.0f;
+        int chunk = 0;
+        for (int kt = 0; kt < ktiles; ++kt) {
+            const int s = kt % NST;
+            const int j = kt / khw, kin_p = kt - j * khw;
+            if (kt >= NST && (s_fail || !mbar_wait(&empty[s], ((kt / NST) - 1) & 1))) {
+                s_fail = 1;
+                break;
+            }
+            if (kin_p == 0 && (s_fail || !mbar_wait(&pfull[j & 1], (j >> 1) & 1))) {
+                s_fail = 1;
+                break;
+            }
+            const float *pt = reinterpret_cast<const float *>(patch + (j & 1) * g.patch_stride);
+            const int tof = kt * BK + kq < p.kk ? tap_off[kin_p * BK + kq] : -1;
+            uint32_t bad = 0;
+            uint8_t *bh = stage_b(s) + (ww >> 2) * 512 + (lane >> 2) * 64 + (((ww & 3) ^ (lane >> 3)) << 4) +
+                          (lane & 3) * 4,
+                    *bl = bh + B_TILE;
+#pragma unroll
+            for (int i = 0; i < PP_ITERS; ++i) {
+                const float v = (tof >= 0 && pix[i] >= 0) ? pt[tof + pix[i]] : 0.0f;
+                bad |= nonfinite_bits(v);
+                *reinterpret_cast<float *>(bh + i * 1024) = v;
+                *reinterpret_cast<float *>(bl + i * 1024) = v - tf32_trunc(v);
+            }
+            __syncwarp();
+            if (lane == 0 && (kin_p == khw - 1 || kt == ktiles - 1)) mbar_arrive(&pempty[j & 1]);
+            if (s_fail || !mbar_wait(&full[s], (kt / NST) & 1)) {
+                s_fail = 1;
+                break;
+            }
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+                float4 *hp = reinterpret_cast<float4 *>(stage_a(s) + (wt + jj * WORK_THREADS) * 16);
+                float4 *lp = reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(hp) + A_TILE);
+                const float4 v = *hp;
+                float4 l;
+                l.x = v.x - tf32_trunc(v.x);
+                l.y = v.y - tf32_trunc(v.y);
+                l.z = v.z - tf32_trunc(v.z);
+                l.w = v.w - tf32_trunc(v.w);
+                bad |= nonfinite_bits(v.x) | nonfinite_bits(v.y) | nonfinite_bits(v.z) | nonfinite_bits(v.w);
+                *lp = l;
+            }
+            if (bad) s_nonfinite = 1u;
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(conv_leader0 + (uint32_t)(s * 8));
+            if (kt % KC == KC - 1 || kt == ktiles - 1) {
+                if (!mbar_wait(chunk_full, chunk & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                if (s_fail) break;
+                tmem_accumulate(tmem, quarter, col0, sum);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(chunk_empty_leader);
+                ++chunk;
+            }
+        }
+        tc_fence_before();
+        cluster_sync_any();     // pair-wide: both CTAs' nonfinite flags are final
+        tc_fence_after();
+        const uint32_t nonfinite = s_nonfinite | ld_cluster_u32(map_to(smem_u32((const void *)&s_nonfinite_storage), peer));
+        const int co = m0 + quarter * 32 + lane;
+        const bool row_ok = co < p.cog;
+        const int64_t co_abs = (int64_t)grp * p.cog + co;
+        float *yrow = p.y + ((int64_t)img * p.co_total + co_abs) * p.hw;
+        if (!s_fail && chunk == nchunks) {
+            if (nonfinite) {
+                // the tile again with f32 FMA in tap order, as the SIMT implicit GEMM computes it
+                if (row_ok) {
+                    const float *wrow = p.w + co_abs * p.ws0;
+                    const int ih = (int)p.ih, iw = (int)p.iw;
+                    const float *ximg = p.x + (int64_t)img * p.xs[0] + (int64_t)grp * p.cg * p.xs[1];
+                    for (int jj = 0; jj < HB; ++jj) {
+                        const int q = p0 + col0 + jj;
+                        if (q >= hw) break;
+                        const int y0 = (q / ow) * p.sy - p.py, x0 = (q % ow) * p.sx - p.px;
+                        float acc = 0.0f;
+                        for (int k = 0; k < p.kk; ++k) {
+                            const int ci = k / khw, r = k % khw;
+                            const int iy = y0 + (r / p.kw) * p.dy, ix = x0 + (r % p.kw) * p.dx;
+                            const float xv = (iy >= 0 && iy < ih && ix >= 0 && ix < iw)
+                                                 ? ximg[(int64_t)ci * p.xs[1] + (int64_t)iy * p.xs[2] + (int64_t)ix * p.xs[3]]
+                                                 : 0.0f;
+                            acc = fmaf(wrow[k], xv, acc);
+                        }
+                        yrow[q] = acc;
+                    }
+                }
+            } else {
+                const bool vec_ok = (p.hw % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.y) & 15) == 0);
+#pragma unroll
+                for (int c = 0; c < HB / 16; ++c) {
+                    uint32_t r[16];
+                    tmem_ld16(tmem + XCOL + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(col0 + c * 16), r);
+                    tmem_wait_ld();
+                    if (!row_ok) continue;
+                    float v[16];
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) v[jj] = sum[c * 16 + jj] + __uint_as_float(r[jj]);
+                    const int q = p0 + col0 + c * 16;
+                    if (vec_ok && q + 16 <= hw) {
+#pragma unroll
+                        for (int jj = 0; jj < 16; jj += 4)
+                            *reinterpret_cast<float4 *>(yrow + q + jj) = make_float4(v[jj], v[jj + 1], v[jj + 2], v[jj + 3]);
+                    } else {
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj)
+                            if (q + jj < hw) yrow[q + jj] = v[jj];
+                    }
+                }
+            }
+        }
+    }
+    if (warp < WORK_WARP0) cluster_sync_any();
+    tc_fence_before();
+    cluster_sync_any();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+    if (threadIdx.x == 0 && s_fail) atomicOr(p.status, KX_TIMEOUT_FLAG);
+}
+
 // Weights [co][cg][kh][kw] under any strides -> dense rows of `pitch` floats
 // in the reference's tap order (ci, ky, kx), zero beyond the taps: the layout
 // the weight tensor map reads (16-byte aligned rows).
@@ -806,6 +1156,79 @@ int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, co
     p.kk = (int)kk;
     p.ncols = ncols;
     p.status = h->flags + kStatusWord;
+    // Patch-staged CTA pairs (256 channels x 224 pixels of one image) when
+    // TMA can box the input rows: unit column stride, 16-byte row, channel and
+    // image strides, a patch row of at most 256 floats, both chunk buffers
+    // beside the stages in shared memory.
+    // Size-1 dimensions arrive with stride 0; the map gets any 16-byte
+    // multiple there (only coordinate 0 is read).
+    int64_t ts[3] = {xs[2], xs[1], xs[0]};   // row, channel, image strides
+    if (ih <= 1 && ts[0] == 0) ts[0] = (iw + 3) / 4 * 4;
+    if (c <= 1 && ts[1] == 0) ts[1] = ts[0] * ih;
+    if (n <= 1 && ts[2] == 0) ts[2] = ts[1] * c;
+    if (cog % 256 == 0 && (xs[3] == 1 || iw == 1) && ts[0] > 0 && ts[1] > 0 && ts[2] > 0 && (ts[0] * 4) % 16 == 0 &&
+        (ts[1] * 4) % 16 == 0 && (ts[2] * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+        n * oh * ow < (1LL << 31) && oh * ow < (1LL << 30)) {
+        const int64_t hw = oh * ow;
+        const int64_t x0 = -((px + 3) / 4) * 4;
+        const int64_t xmax = (ow - 1) * sx - px + (kw - 1) * dx;
+        const int64_t pitch = (xmax - x0 + 1 + 3) / 4 * 4;
+        const int64_t tpi = (hw + 2 * PP_HB - 1) / (2 * PP_HB);
+        int64_t span = 0;
+        for (int64_t q0 = 0; q0 < hw; q0 += PP_HB) {
+            const int64_t qb = std::min(q0 + PP_HB, hw) - 1;
+            span = std::max(span, qb / ow - q0 / ow);
+        }
+        const int64_t prows = span * sy + (kh - 1) * dy + 1;
+        const int64_t patch_bytes = (int64_t)PP_CH * prows * pitch * 4;
+        const int64_t patch_stride = (patch_bytes + 1023) / 1024 * 1024;
+        const int64_t smem_fixed = 2 * patch_stride + BAR_BYTES + PP_CH * kh * kw * 4 + 1024;
+        // as many stages as fit: the weight tile of k-tile kt is fetched when
+        // the MMAs of kt - nst have freed its stage
+        int nst = PP_NST;
+        while (nst > 3 && smem_fixed + (int64_t)nst * PP_STAGE > SMEM_LIMIT) --nst;
+        const int64_t smem = smem_fixed + (int64_t)nst * PP_STAGE;
+        const int64_t pairs = (cog / 256) * n * tpi * groups;
+        CUtensorMap mx;
+        const uint64_t dims[4] = {(uint64_t)iw, (uint64_t)ih, (uint64_t)c, (uint64_t)n};
+        const uint64_t strides[3] = {(uint64_t)ts[0] * 4, (uint64_t)ts[1] * 4, (uint64_t)ts[2] * 4};
+        const uint32_t box[4] = {(uint32_t)pitch, (uint32_t)prows, (uint32_t)PP_CH, 1};
+        if (pitch <= 256 && prows <= 256 && smem <= SMEM_LIMIT && 2 * pairs <= INT32_MAX &&
+            (2 * pairs >= h->sm_count || h->f32_variant == KX_F32_3XTF32) && make_map4(&mx, x, dims, strides, box)) {
+            PatchGeom g;
+            g.x0 = (int)x0;
+            g.pitch = (int)pitch;
+            g.prows = (int)prows;
+            g.tpi = (int)tpi;
+            g.nimg = (int)n;
+            g.patch_bytes = (uint32_t)patch_bytes;
+            g.patch_stride = (uint32_t)patch_stride;
+            auto k = nst == 6 ? conv_3xtf32_patch_kernel<6>
+                     : nst == 5 ? conv_3xtf32_patch_kernel<5>
+                     : nst == 4 ? conv_3xtf32_patch_kernel<4>
+                                : conv_3xtf32_patch_kernel<3>;
+            cudaError_t ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (ce == cudaSuccess) {
+                cudaLaunchConfig_t cfg = {};
+                cfg.gridDim = dim3((unsigned)(2 * pairs / groups), (unsigned)groups, 1);
+                cfg.blockDim = dim3(NTHREADS, 1, 1);
+                cfg.dynamicSmemBytes = (size_t)smem;
+                cfg.stream = h->stream;
+                cudaLaunchAttribute attr[1];
+                attr[0].id = cudaLaunchAttributeClusterDimension;
+                attr[0].val.clusterDim.x = 2;
+                attr[0].val.clusterDim.y = 1;
+                attr[0].val.clusterDim.z = 1;
+                cfg.attrs = attr;
+                cfg.numAttrs = 1;
+                ce = cudaLaunchKernelEx(&cfg, k, mw, mx, p, g);
+                if (ce == cudaSuccess) ce = cudaGetLastError();
+            }
+            *kernel_name = "conv_tc_3xtf32_patch_256x224";
+            ++h->launches;
+            return ce == cudaSuccess ? KX_OK : h->cuda_fail(ce);
+        }
+    }
     const int table_pair = (int)((kk + BK - 1) / BK * BK) * (int)sizeof(Tap);
     // CTA pairs (256 channels x 256 pixels) when the group has 256+ output
     // channels and the pairs fill the SMs (a 256-wide one-SM conv tile

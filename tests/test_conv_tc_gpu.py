@@ -49,7 +49,26 @@ GEOMETRIES = [
 ]
 
 
-@pytest.mark.parametrize("xs,ws,opts", GEOMETRIES)
+# Input rows whose width is a multiple of 4 floats (16-byte rows) are boxed
+# by TMA: with 256-channel groups they take the patch-staged pair kernel.
+PATCH_GEOMETRIES = [
+    ((2, 20, 12, 12), (256, 3, 3), dict(stride=(1, 1), padding=(1, 1), dilation=(1, 1), groups=1)),
+    ((1, 24, 17, 20), (512, 3, 3), dict(stride=(2, 1), padding=(1, 2), dilation=(2, 1), groups=2)),
+    ((1, 8, 30, 28), (256, 5, 5), dict(stride=(1, 1), padding=(2, 2), dilation=(1, 1), groups=1)),
+    ((1, 16, 9, 8), (256, 1, 1), dict(stride=(1, 1), padding=(0, 0), dilation=(1, 1), groups=1)),
+    ((1, 3, 40, 40), (256, 7, 7), dict(stride=(2, 2), padding=(3, 3), dilation=(1, 1), groups=1)),
+    ((1, 32, 56, 56), (256, 3, 3), dict(stride=(1, 1), padding=(1, 1), dilation=(1, 1), groups=1)),
+    ((3, 64, 24, 36), (512, 3, 3), dict(stride=(1, 1), padding=(1, 1), dilation=(1, 1), groups=1)),
+]
+
+
+def expected_kernel(xs, ws, opts):
+    if (ws[0] // opts["groups"]) % 256:
+        return "conv_tc_3xtf32_128x128"
+    return "conv_tc_3xtf32_patch_256x224" if xs[3] % 4 == 0 else "conv_tc_3xtf32_pair_256x256"
+
+
+@pytest.mark.parametrize("xs,ws,opts", GEOMETRIES + PATCH_GEOMETRIES)
 def test_conv_tc_geometries(kx, torch_cuda, tc, xs, ws, opts):
     rng = np.random.default_rng(sum(xs) + sum(ws))
     n, c, h, w = xs
@@ -57,8 +76,22 @@ def test_conv_tc_geometries(kx, torch_cuda, tc, xs, ws, opts):
     x = rng.uniform(-1, 1, xs).astype(np.float32)
     wt = rng.normal(0, math.sqrt(2 / (c // opts["groups"] * kh * kw)), (co, c // opts["groups"], kh, kw)).astype(np.float32)
     _check(kx, torch_cuda, x, wt, opts)
-    expect = "conv_tc_3xtf32_pair_256x256" if (co // opts["groups"]) % 256 == 0 else "conv_tc_3xtf32_128x128"
-    assert tc.last_kernel == expect, tc.last_kernel
+    assert tc.last_kernel == expected_kernel(xs, ws, opts), tc.last_kernel
+
+
+def test_conv_patch_channel_and_image_strides(kx, torch_cuda, tc):
+    """The patch boxes follow the caller's channel and image strides: the
+    input is every other channel of a wider buffer, images two apart."""
+    torch = torch_cuda
+    rng = np.random.default_rng(17)
+    buf = rng.uniform(-1, 1, (4, 40, 14, 16)).astype(np.float32)
+    x = buf[::2, ::2]                                   # 2 images x 20 channels, strided
+    wt = rng.normal(0, 0.1, (256, 20, 3, 3)).astype(np.float32)
+    dev = to_dev(buf, torch).reshape(-1)
+    xv = kx.TensorView(dev, (2, 20, 14, 16), (2 * 40 * 14 * 16, 2 * 14 * 16, 16, 1), 0)
+    _check(kx, torch, np.ascontiguousarray(x), wt, dict(stride=(1, 1), padding=(1, 1), dilation=(1, 1), groups=1),
+           x_dev=xv)
+    assert tc.last_kernel == "conv_tc_3xtf32_patch_256x224"
 
 
 def test_conv_tc_reversed_and_strided_input(kx, torch_cuda, tc):
@@ -77,19 +110,21 @@ def test_conv_tc_reversed_and_strided_input(kx, torch_cuda, tc):
     assert tc.last_kernel == "conv_tc_3xtf32_128x128"
 
 
-@pytest.mark.parametrize("co", [40, 256])
-def test_conv_tc_nonfinite_input_tiles(kx, torch_cuda, tc, co):
+@pytest.mark.parametrize("co,width", [(40, 12), (256, 13), (256, 12)])
+def test_conv_tc_nonfinite_input_tiles(kx, torch_cuda, tc, co, width):
     """inf/NaN in the input: the affected tiles are recomputed with FMA, so
     the result keeps IEEE propagation (no NaN from inf * 0 in a cross term);
-    256 output channels take the CTA-pair kernel."""
+    256 output channels take the CTA-pair kernel (gathered at width 13,
+    patch-staged at width 12)."""
     torch = torch_cuda
     rng = np.random.default_rng(4)
-    x = rng.uniform(-1, 1, (2, 32, 12, 12)).astype(np.float32)
+    x = rng.uniform(-1, 1, (2, 32, 12, width)).astype(np.float32)
     x[0, 3, 5, 5] = np.inf
     x[1, 7, 0, 0] = np.nan
     wt = np.abs(rng.normal(0, 0.1, (co, 32, 3, 3))).astype(np.float32)
     opts = kx.Conv2dOptions(padding=(1, 1))
     got = kx.conv2d(to_dev(x, torch), to_dev(wt, torch), opts).cpu().numpy()
+    assert tc.last_kernel == expected_kernel(x.shape, wt.shape, dict(groups=1)), tc.last_kernel
     tc.set_f32_variant(1)
     ref = kx.conv2d(to_dev(x, torch), to_dev(wt, torch), opts).cpu().numpy()
     assert np.array_equal(np.isnan(got), np.isnan(ref))
