@@ -733,16 +733,18 @@ conv_3xtf32_pair_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_co
 //   warp 0   weight tiles by TMA (as above)
 //   warp 1   TMEM owner; the pair leader's lane 0 issues the MMAs (N = 224)
 //   warp 2   patch boxes by TMA
-//   warps 4..11  build B hi/lo from the patch, split A's lo part, fold the
-//            hi*hi chunks, store the output
+//   warp 3   scans each patch for inf/NaN
+//   warps 4..11  build B hi/lo from the patch, fold the hi*hi chunks, store
+//            the output
+// The weights' lo parts are split once per call (split_weights_kernel) and
+// come by TMA beside the hi tile.
 // ---------------------------------------------------------------------------
 constexpr int PP_HB = 112;                               // pixels per CTA (half the pair's 224)
 constexpr int PP_B_TILE = PP_HB * BK * 4;                // 7 KB
 constexpr int PP_STAGE = 2 * A_TILE + 2 * PP_B_TILE;     // 30 KB
 constexpr int PP_NST = 6;                                // most stages; fewer when the patch buffers are large
 constexpr int PP_CH = 16;                                // input channels per patch chunk
-constexpr int PP_ITERS = PP_HB * BK / WORK_THREADS;      // B elements per worker thread and k-tile
-static_assert(PP_HB * BK == PP_ITERS * WORK_THREADS, "B tile split");
+static_assert(PP_HB == 2 * 56 && WORK_WARPS == 8, "B build: 8 warps = 4 tap groups x 2 halves of 56 pixels");
 static_assert(PP_STAGE % 1024 == 0, "stage alignment");
 static_assert(3 * PP_NST + 2 + 4 + 1 <= BAR_BYTES / 8, "barrier area");
 
@@ -754,12 +756,14 @@ struct PatchGeom {
     int nimg;                // images
     uint32_t patch_bytes;    // one chunk: PP_CH * prows * pitch * 4
     uint32_t patch_stride;   // patch_bytes rounded up to 1 KB
+    const uint32_t *wflag;   // nonzero: some weight is NaN or infinite (set by split_weights_kernel)
 };
 
 template <int NST>
 __global__ void __launch_bounds__(NTHREADS, 1)
-conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-                         const __grid_constant__ Params p, const __grid_constant__ PatchGeom g) {
+conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmWlo,
+                         const __grid_constant__ CUtensorMap tmX, const __grid_constant__ Params p,
+                         const __grid_constant__ PatchGeom g) {
     constexpr int HB = PP_HB, BNP = 2 * PP_HB, B_TILE = PP_B_TILE, STAGE_BYTES = PP_STAGE;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -813,10 +817,10 @@ conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_c
         mbar_init(chunk_empty, 2 * WORK_WARPS);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&pfull[b], 1);
-            mbar_init(&pempty[b], WORK_WARPS);
+            mbar_init(&pempty[b], WORK_WARPS + 1);     // the workers and the scanning warp
         }
         s_fail = 0;
-        s_nonfinite = 0;
+        s_nonfinite = *g.wflag != 0u;   // written by the weight split earlier in the stream
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
@@ -842,8 +846,9 @@ conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_c
                     s_fail = 1;
                     break;
                 }
-                mbar_expect_tx(&full[s], A_TILE);
+                mbar_expect_tx(&full[s], 2 * A_TILE);
                 tma_load_3d(stage_a(s), &tmW, kt * BK, m0, grp, &full[s]);
+                tma_load_3d(stage_a(s) + A_TILE, &tmWlo, kt * BK, m0, grp, &full[s]);
                 issued = kt + 1;
             }
             for (int s = 0; s < NST && s < issued; ++s) {
@@ -909,39 +914,64 @@ conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_c
                 mbar_wait(&pfull[b], (last >> 1) & 1);
             }
         }
+    } else if (warp == 3) {
+        // Scan each patch chunk for inf/NaN once it has landed, then release
+        // it with the workers (an element no output uses can only send the
+        // tile to the FMA fallback, which is exact).
+        for (int j = 0; j < npatch; ++j) {
+            if (s_fail || !mbar_wait(&pfull[j & 1], (j >> 1) & 1)) {
+                s_fail = 1;
+                break;
+            }
+            const float4 *pv = reinterpret_cast<const float4 *>(patch + (j & 1) * g.patch_stride);
+            float probe = 0.0f;     // becomes NaN iff the chunk holds an inf or NaN
+            for (uint32_t e = lane; e < g.patch_bytes / 16; e += 32) {
+                const float4 v = pv[e];
+                probe = fmaf(v.x, 0.0f, probe);
+                probe = fmaf(v.y, 0.0f, probe);
+                probe = fmaf(v.z, 0.0f, probe);
+                probe = fmaf(v.w, 0.0f, probe);
+            }
+            if (__any_sync(0xffffffffu, probe != probe) && lane == 0) s_nonfinite = 1u;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pempty[j & 1]);
+        }
     } else if (warp >= WORK_WARP0) {
-        const int wt = threadIdx.x - WORK_WARP0 * 32;
         const int ww = warp - WORK_WARP0;
         const int quarter = warp & 3;
         const int col0 = (ww >> 2) * HB;
         const uint32_t conv_leader0 = map_to(smem_u32(&conv[0]), 0);
         const uint32_t chunk_empty_leader = map_to(smem_u32(chunk_empty), 0);
-        // Element i of this thread in every B tile: pixel row r = 8 * (2i + ww/4) + lane/4,
-        // tap k = 4 * (ww%4) + lane%4 of the k-tile.  The tile is K-major with the
-        // 64-byte swizzle (as the TMA writes A): (r, k) at byte 64 r + 16 ((k/4) ^ ((r/2)%4))
-        // + 4 (k%4), here 1024 i + 512 (ww/4) + 64 (lane/4) + 16 ((ww%4) ^ (lane/8)) + 4 (lane%4):
-        // each warp store covers 32 distinct banks.
-        const int kq = 4 * (ww & 3) + (lane & 3);
-        int pix[PP_ITERS];
-        {
-            const int oy_a = min(q0, hw - 1) / ow;
-#pragma unroll
-            for (int i = 0; i < PP_ITERS; ++i) {
-                const int q = q0 + 8 * (2 * i + (ww >> 2)) + (lane >> 2);
-                pix[i] = -1;
-                if (q < hw) {
-                    const int oy = q / ow, ox = q % ow;
-                    pix[i] = (oy - oy_a) * p.sy * g.pitch + (ox * p.sx - p.px - g.x0);
-                }
-            }
-        }
+        // B build: lane = pixel, thread = 4 consecutive taps, i.e. one 16-byte
+        // row segment of the K-major tile with the 64-byte swizzle (as the TMA
+        // writes A): pixel r, taps 4g..4g+3 at byte 64 r + 16 (g ^ ((r/2)%4)).
+        // Warp ww writes tap group g = ww%4 of pixels 56 (ww/4) + [0, 56):
+        // lanes 0..31, then lanes 0..23.  Each quarter-warp store covers 32
+        // distinct banks; the patch reads of a warp are consecutive pixels.
+        // Rows of pixels past the image read the last pixel (their outputs are
+        // never stored) and taps past the group read whatever the patch holds
+        // there (their weights are zero).  Warp 3 scans every patch chunk for
+        // inf/NaN, so neither reaches a stored result.
+        const int kg = ww & 3;
+        const int r0 = 56 * (ww >> 2) + lane, r1 = r0 + 32;
+        const bool two = lane < 24;
+        const int oy_a = min(q0, hw - 1) / ow;
+        auto pix_of = [&](int r) {
+            const int q = min(q0 + r, hw - 1);
+            const int oy = q / ow, ox = q % ow;
+            return (oy - oy_a) * p.sy * g.pitch + (ox * p.sx - p.px - g.x0);
+        };
+        const int pix0 = pix_of(r0), pix1 = pix_of(r1);
+        const uint32_t bo0 = (uint32_t)r0 * 64 + ((uint32_t)(kg ^ ((r0 >> 1) & 3)) << 4);
+        const uint32_t bo1 = (uint32_t)r1 * 64 + ((uint32_t)(kg ^ ((r1 >> 1) & 3)) << 4);
+        const int4 *tap4 = reinterpret_cast<const int4 *>(tap_off);
         float sum[HB];
 #pragma unroll
         for (int j = 0; j < HB; ++j) sum[j] = 0.0f;
         int chunk = 0;
+        int j = 0, kin_p = 0;     // patch chunk of k-tile kt and its k-tile within the chunk
         for (int kt = 0; kt < ktiles; ++kt) {
             const int s = kt % NST;
-            const int j = kt / khw, kin_p = kt - j * khw;
             if (kt >= NST && (s_fail || !mbar_wait(&empty[s], ((kt / NST) - 1) & 1))) {
                 s_fail = 1;
                 break;
@@ -951,38 +981,22 @@ conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_c
                 break;
             }
             const float *pt = reinterpret_cast<const float *>(patch + (j & 1) * g.patch_stride);
-            const int tof = kt * BK + kq < p.kk ? tap_off[kin_p * BK + kq] : -1;
-            uint32_t bad = 0;
-            uint8_t *bh = stage_b(s) + (ww >> 2) * 512 + (lane >> 2) * 64 + (((ww & 3) ^ (lane >> 3)) << 4) +
-                          (lane & 3) * 4,
-                    *bl = bh + B_TILE;
-#pragma unroll
-            for (int i = 0; i < PP_ITERS; ++i) {
-                const float v = (tof >= 0 && pix[i] >= 0) ? pt[tof + pix[i]] : 0.0f;
-                bad |= nonfinite_bits(v);
-                *reinterpret_cast<float *>(bh + i * 1024) = v;
-                *reinterpret_cast<float *>(bl + i * 1024) = v - tf32_trunc(v);
-            }
+            const int4 t4 = tap4[kin_p * 4 + kg];
+            uint8_t *bt = stage_b(s);
+            auto unit = [&](int pix, uint32_t bo) {
+                const float v0 = pt[t4.x + pix], v1 = pt[t4.y + pix], v2 = pt[t4.z + pix], v3 = pt[t4.w + pix];
+                *reinterpret_cast<float4 *>(bt + bo) = make_float4(v0, v1, v2, v3);
+                *reinterpret_cast<float4 *>(bt + B_TILE + bo) =
+                    make_float4(v0 - tf32_trunc(v0), v1 - tf32_trunc(v1), v2 - tf32_trunc(v2), v3 - tf32_trunc(v3));
+            };
+            unit(pix0, bo0);
+            if (two) unit(pix1, bo1);
             __syncwarp();
             if (lane == 0 && (kin_p == khw - 1 || kt == ktiles - 1)) mbar_arrive(&pempty[j & 1]);
             if (s_fail || !mbar_wait(&full[s], (kt / NST) & 1)) {
                 s_fail = 1;
                 break;
             }
-#pragma unroll
-            for (int jj = 0; jj < 2; ++jj) {
-                float4 *hp = reinterpret_cast<float4 *>(stage_a(s) + (wt + jj * WORK_THREADS) * 16);
-                float4 *lp = reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(hp) + A_TILE);
-                const float4 v = *hp;
-                float4 l;
-                l.x = v.x - tf32_trunc(v.x);
-                l.y = v.y - tf32_trunc(v.y);
-                l.z = v.z - tf32_trunc(v.z);
-                l.w = v.w - tf32_trunc(v.w);
-                bad |= nonfinite_bits(v.x) | nonfinite_bits(v.y) | nonfinite_bits(v.z) | nonfinite_bits(v.w);
-                *lp = l;
-            }
-            if (bad) s_nonfinite = 1u;
             fence_proxy_async();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(conv_leader0 + (uint32_t)(s * 8));
@@ -998,6 +1012,10 @@ conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_c
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cluster(chunk_empty_leader);
                 ++chunk;
+            }
+            if (++kin_p == khw) {
+                kin_p = 0;
+                ++j;
             }
         }
         tc_fence_before();
@@ -1085,6 +1103,31 @@ __global__ void pack_weights_kernel(const float *__restrict__ w, int64_t ws0, in
     }
 }
 
+// The patch-staged kernel's weights: dense hi rows (when `hi` is given; the
+// caller's rows are used in place otherwise) and their lo parts w - tf32(w),
+// `pitch` floats per output channel in tap order, zero beyond the taps.  A
+// NaN or infinite weight sets *flag.
+__global__ void split_weights_kernel(const float *__restrict__ w, int64_t ws0, int64_t ws1, int64_t ws2, int64_t ws3,
+                                     int64_t co, int kh, int kw, int kk, int pitch, float *__restrict__ hi,
+                                     float *__restrict__ lo, uint32_t *flag) {
+    const int64_t total = co * pitch;
+    bool bad = false;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t o = e / pitch;
+        const int k = (int)(e % pitch);
+        float v = 0.0f;
+        if (k < kk) {
+            const int khw = kh * kw;
+            const int ci = k / khw, r = k % khw;
+            v = w[o * ws0 + ci * ws1 + (r / kw) * ws2 + (r % kw) * ws3];
+        }
+        if (hi) hi[e] = v;
+        lo[e] = v - tf32_trunc(v);
+        bad |= !isfinite(v);
+    }
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(flag, 1u);
+}
+
 }  // namespace conv
 }  // namespace tc
 
@@ -1102,60 +1145,39 @@ int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, co
     (void)c;
     const int64_t kk = cg * kh * kw;
     const int64_t cog = co / groups;
-    if (kk < 16 || kh * kw > PAD_TAP || (kk + BK) * (int64_t)sizeof(Tap) + Tile<128>::FIXED_SMEM > SMEM_LIMIT)
-        return KX_DECLINED;
-    if (groups > 65535) return KX_DECLINED;
+    if (kk < 16 || groups > 65535) return KX_DECLINED;
     const bool taps_dense = (kw == 1 || ws[3] == 1) && (kh == 1 || ws[2] == kw) && (cg == 1 || ws[1] == kh * kw);
-    int64_t w_pitch = ws[0];
-    if (!taps_dense || ws[0] < kk || (ws[0] * 4) % 16 || (reinterpret_cast<uintptr_t>(w) & 15)) {
-        // repack into dense, 16-byte aligned tap rows in the handle's workspace
-        const int pitch = (int)((kk + 3) / 4 * 4);
-        void *buf = nullptr;
-        int rc = h->workspace((uint64_t)co * pitch * sizeof(float), &buf);
-        if (rc) return rc;
-        int64_t blocks = (co * pitch + 255) / 256;
-        if (blocks > 4LL * h->sm_count) blocks = 4LL * h->sm_count;
-        pack_weights_kernel<<<(unsigned)blocks, 256, 0, h->stream>>>(w, ws[0], ws[1], ws[2], ws[3], co, (int)kh,
-                                                                      (int)kw, (int)kk, pitch,
-                                                                      static_cast<float *>(buf));
-        ++h->launches;
-        cudaError_t ce = cudaGetLastError();
-        if (ce != cudaSuccess) return h->cuda_fail(ce);
-        w = static_cast<const float *>(buf);
-        w_pitch = pitch;
-    }
+    // dense, 16-byte aligned tap rows are read in place; anything else is repacked
+    const bool repack = !taps_dense || ws[0] < kk || (ws[0] * 4) % 16 || (reinterpret_cast<uintptr_t>(w) & 15);
     const int64_t ncols = n * oh * ow;
-    if (((cog + BM - 1) / BM) * ((ncols + 127) / 128) > INT32_MAX) return KX_DECLINED;
-    CUtensorMap mw;
-    if (!make_map(&mw, w, (uint64_t)kk, (uint64_t)cog, (uint64_t)groups, (uint64_t)w_pitch * 4,
-                  (uint64_t)(w_pitch * cog) * 4, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B))
-        return KX_DECLINED;
     Params p;
-    std::memset(&p, 0, sizeof(p));
-    p.x = x;
-    p.w = w;
-    p.y = y;
-    for (int i = 0; i < 4; ++i) p.xs[i] = xs[i];
-    p.ws0 = w_pitch;
-    p.ih = ih;
-    p.iw = iw;
-    p.oh = oh;
-    p.ow = ow;
-    p.hw = oh * ow;
-    p.co_total = co;
-    p.cog = cog;
-    p.cg = cg;
-    p.kh = (int)kh;
-    p.kw = (int)kw;
-    p.sy = (int)sy;
-    p.sx = (int)sx;
-    p.py = (int)py;
-    p.px = (int)px;
-    p.dy = (int)dy;
-    p.dx = (int)dx;
-    p.kk = (int)kk;
-    p.ncols = ncols;
-    p.status = h->flags + kStatusWord;
+    auto fill = [&](const float *wp, int64_t pitch) {
+        std::memset(&p, 0, sizeof(p));
+        p.x = x;
+        p.w = wp;
+        p.y = y;
+        for (int i = 0; i < 4; ++i) p.xs[i] = xs[i];
+        p.ws0 = pitch;
+        p.ih = ih;
+        p.iw = iw;
+        p.oh = oh;
+        p.ow = ow;
+        p.hw = oh * ow;
+        p.co_total = co;
+        p.cog = cog;
+        p.cg = cg;
+        p.kh = (int)kh;
+        p.kw = (int)kw;
+        p.sy = (int)sy;
+        p.sx = (int)sx;
+        p.py = (int)py;
+        p.px = (int)px;
+        p.dy = (int)dy;
+        p.dx = (int)dx;
+        p.kk = (int)kk;
+        p.ncols = ncols;
+        p.status = h->flags + kStatusWord;
+    };
     // Patch-staged CTA pairs (256 channels x 224 pixels of one image) when
     // TMA can box the input rows: unit column stride, 16-byte row, channel and
     // image strides, a patch row of at most 256 floats, both chunk buffers
@@ -1195,6 +1217,35 @@ int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, co
         const uint32_t box[4] = {(uint32_t)pitch, (uint32_t)prows, (uint32_t)PP_CH, 1};
         if (pitch <= 256 && prows <= 256 && smem <= SMEM_LIMIT && 2 * pairs <= INT32_MAX &&
             (2 * pairs >= h->sm_count || h->f32_variant == KX_F32_3XTF32) && make_map4(&mx, x, dims, strides, box)) {
+            // The weights' lo parts (and the dense hi rows when the caller's
+            // layout is not) go to the workspace once per call; the kernel
+            // loads both by TMA.  A nonfinite weight raises the flag word,
+            // which sends every tile to the FMA fallback.
+            const int64_t wp = repack ? (kk + 3) / 4 * 4 : ws[0];
+            const uint64_t part = (uint64_t)co * wp * sizeof(float);
+            void *buf = nullptr;
+            int rc = h->workspace((repack ? 2 : 1) * part, &buf);
+            if (rc) return rc;
+            float *hi = repack ? static_cast<float *>(buf) : nullptr;
+            float *lo = static_cast<float *>(buf) + (repack ? co * wp : 0);
+            const float *whi = repack ? hi : w;
+            cudaError_t ce = cudaMemsetAsync(h->flags + kConvLoWord, 0, sizeof(uint32_t), h->stream);
+            if (ce == cudaSuccess) {
+                int64_t blocks = (co * wp + 255) / 256;
+                if (blocks > 4LL * h->sm_count) blocks = 4LL * h->sm_count;
+                split_weights_kernel<<<(unsigned)blocks, 256, 0, h->stream>>>(
+                    w, ws[0], ws[1], ws[2], ws[3], co, (int)kh, (int)kw, (int)kk, (int)wp, hi, lo, h->flags + kConvLoWord);
+                ++h->launches;
+                ce = cudaGetLastError();
+            }
+            if (ce != cudaSuccess) return h->cuda_fail(ce);
+            CUtensorMap mw, mwlo;
+            if (!make_map(&mw, whi, (uint64_t)kk, (uint64_t)cog, (uint64_t)groups, (uint64_t)wp * 4,
+                          (uint64_t)(wp * cog) * 4, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B) ||
+                !make_map(&mwlo, lo, (uint64_t)kk, (uint64_t)cog, (uint64_t)groups, (uint64_t)wp * 4,
+                          (uint64_t)(wp * cog) * 4, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B))
+                return KX_DECLINED;
+            fill(whi, wp);
             PatchGeom g;
             g.x0 = (int)x0;
             g.pitch = (int)pitch;
@@ -1203,11 +1254,12 @@ int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, co
             g.nimg = (int)n;
             g.patch_bytes = (uint32_t)patch_bytes;
             g.patch_stride = (uint32_t)patch_stride;
+            g.wflag = h->flags + kConvLoWord;
             auto k = nst == 6 ? conv_3xtf32_patch_kernel<6>
                      : nst == 5 ? conv_3xtf32_patch_kernel<5>
                      : nst == 4 ? conv_3xtf32_patch_kernel<4>
                                 : conv_3xtf32_patch_kernel<3>;
-            cudaError_t ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             if (ce == cudaSuccess) {
                 cudaLaunchConfig_t cfg = {};
                 cfg.gridDim = dim3((unsigned)(2 * pairs / groups), (unsigned)groups, 1);
@@ -1221,7 +1273,7 @@ int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, co
                 attr[0].val.clusterDim.z = 1;
                 cfg.attrs = attr;
                 cfg.numAttrs = 1;
-                ce = cudaLaunchKernelEx(&cfg, k, mw, mx, p, g);
+                ce = cudaLaunchKernelEx(&cfg, k, mw, mwlo, mx, p, g);
                 if (ce == cudaSuccess) ce = cudaGetLastError();
             }
             *kernel_name = "conv_tc_3xtf32_patch_256x224";
@@ -1229,6 +1281,33 @@ int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, co
             return ce == cudaSuccess ? KX_OK : h->cuda_fail(ce);
         }
     }
+    // the gathered kernels keep a (ci, ky, kx) table of all taps in shared memory
+    if (kh * kw > PAD_TAP || (kk + BK) * (int64_t)sizeof(Tap) + Tile<128>::FIXED_SMEM > SMEM_LIMIT)
+        return KX_DECLINED;
+    int64_t w_pitch = ws[0];
+    if (repack) {
+        // repack into dense, 16-byte aligned tap rows in the handle's workspace
+        const int pitch = (int)((kk + 3) / 4 * 4);
+        void *buf = nullptr;
+        int rc = h->workspace((uint64_t)co * pitch * sizeof(float), &buf);
+        if (rc) return rc;
+        int64_t blocks = (co * pitch + 255) / 256;
+        if (blocks > 4LL * h->sm_count) blocks = 4LL * h->sm_count;
+        pack_weights_kernel<<<(unsigned)blocks, 256, 0, h->stream>>>(w, ws[0], ws[1], ws[2], ws[3], co, (int)kh,
+                                                                      (int)kw, (int)kk, pitch,
+                                                                      static_cast<float *>(buf));
+        ++h->launches;
+        cudaError_t ce = cudaGetLastError();
+        if (ce != cudaSuccess) return h->cuda_fail(ce);
+        w = static_cast<const float *>(buf);
+        w_pitch = pitch;
+    }
+    if (((cog + BM - 1) / BM) * ((ncols + 127) / 128) > INT32_MAX) return KX_DECLINED;
+    CUtensorMap mw;
+    if (!make_map(&mw, w, (uint64_t)kk, (uint64_t)cog, (uint64_t)groups, (uint64_t)w_pitch * 4,
+                  (uint64_t)(w_pitch * cog) * 4, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B))
+        return KX_DECLINED;
+    fill(w, w_pitch);
     const int table_pair = (int)((kk + BK - 1) / BK * BK) * (int)sizeof(Tap);
     // CTA pairs (256 channels x 256 pixels) when the group has 256+ output
     // channels and the pairs fill the SMs (a 256-wide one-SM conv tile

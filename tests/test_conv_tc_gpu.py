@@ -173,3 +173,40 @@ def test_conv_auto_uses_tensor_cores_for_large_convs(kx, torch_cuda):
     assert h.last_kernel == "conv_tc_3xtf32_128x128", h.last_kernel
     d2, ab = oracle.conv2d_dot2(oracle.View.of(x[:1]), oracle.View.of(w), padding=(1, 1))
     assert (np.abs(y[:1].cpu().numpy().astype(np.float64) - d2) <= 2e-6 * ab + 1e-30).all()
+
+
+def test_conv_patch_nonfinite_weights_fall_back(kx, torch_cuda, tc):
+    """An inf weight on the patch-staged path: its split raises the flag and
+    every tile is recomputed with FMA, so inf/NaN follow IEEE as on the SIMT
+    path, and finite outputs keep the bound."""
+    torch = torch_cuda
+    rng = np.random.default_rng(8)
+    x = rng.uniform(-1, 1, (2, 16, 12, 12)).astype(np.float32)
+    wt = rng.normal(0, 0.1, (256, 16, 3, 3)).astype(np.float32)
+    wt[7, 3, 1, 1] = np.inf
+    opts = kx.Conv2dOptions(padding=(1, 1))
+    got = kx.conv2d(to_dev(x, torch), to_dev(wt, torch), opts).cpu().numpy()
+    assert tc.last_kernel == "conv_tc_3xtf32_patch_256x224", tc.last_kernel
+    tc.set_f32_variant(1)
+    ref = kx.conv2d(to_dev(x, torch), to_dev(wt, torch), opts).cpu().numpy()
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    assert np.array_equal(np.isinf(got), np.isinf(ref))
+    assert np.isinf(got[:, 7]).any()
+    fin = np.isfinite(ref)
+    assert (np.abs(got[fin] - ref[fin]) <= 1e-5 * (1 + np.abs(ref[fin]))).all()
+
+
+def test_conv_patch_repacked_weights(kx, torch_cuda, tc):
+    """Weights through a view whose taps are not dense rows (every row padded
+    to 4 columns) are repacked beside their lo parts."""
+    torch = torch_cuda
+    rng = np.random.default_rng(9)
+    x = rng.uniform(-1, 1, (1, 24, 16, 16)).astype(np.float32)
+    wbuf = rng.normal(0, 0.08, (256, 24, 3, 4)).astype(np.float32)
+    wt = np.ascontiguousarray(wbuf[..., :3])
+    dev = to_dev(wbuf, torch).reshape(-1)
+    wv = kx.TensorView(dev, (256, 24, 3, 3), (24 * 12, 12, 4, 1), 0)
+    got = kx.conv2d(to_dev(x, torch), wv, kx.Conv2dOptions(padding=(1, 1))).cpu().numpy().astype(np.float64)
+    assert tc.last_kernel == "conv_tc_3xtf32_patch_256x224", tc.last_kernel
+    d2, ab = oracle.conv2d_dot2(oracle.View.of(x), oracle.View.of(wt), padding=(1, 1))
+    assert (np.abs(got - d2) <= 2e-6 * ab + 1e-30).all()
