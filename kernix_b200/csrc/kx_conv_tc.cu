@@ -961,10 +961,11 @@ conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_c
             const int oy = q / ow, ox = q % ow;
             return (oy - oy_a) * p.sy * g.pitch + (ox * p.sx - p.px - g.x0);
         };
-        const int pix0 = pix_of(r0), pix1 = pix_of(r1);
+        // lanes without a second pixel read their first one again (stores skipped)
+        const int pix0 = pix_of(r0), pix1 = two ? pix_of(r1) : pix0;
         const uint32_t bo0 = (uint32_t)r0 * 64 + ((uint32_t)(kg ^ ((r0 >> 1) & 3)) << 4);
         const uint32_t bo1 = (uint32_t)r1 * 64 + ((uint32_t)(kg ^ ((r1 >> 1) & 3)) << 4);
-        const int4 *tap4 = reinterpret_cast<const int4 *>(tap_off);
+        const uint32_t smem_s = smem_u32(smem), patch_s = smem_u32(patch), tap_s = smem_u32(tap_off);
         float sum[HB];
 #pragma unroll
         for (int j = 0; j < HB; ++j) sum[j] = 0.0f;
@@ -980,17 +981,27 @@ conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_c
                 s_fail = 1;
                 break;
             }
-            const float *pt = reinterpret_cast<const float *>(patch + (j & 1) * g.patch_stride);
-            const int4 t4 = tap4[kin_p * 4 + kg];
-            uint8_t *bt = stage_b(s);
-            auto unit = [&](int pix, uint32_t bo) {
-                const float v0 = pt[t4.x + pix], v1 = pt[t4.y + pix], v2 = pt[t4.z + pix], v3 = pt[t4.w + pix];
-                *reinterpret_cast<float4 *>(bt + bo) = make_float4(v0, v1, v2, v3);
-                *reinterpret_cast<float4 *>(bt + B_TILE + bo) =
-                    make_float4(v0 - tf32_trunc(v0), v1 - tf32_trunc(v1), v2 - tf32_trunc(v2), v3 - tf32_trunc(v3));
-            };
-            unit(pix0, bo0);
-            if (two) unit(pix1, bo1);
+            // shared addresses in bytes; all eight loads go out before any store
+            const uint32_t pt = patch_s + (uint32_t)(j & 1) * g.patch_stride;
+            const int4 t4 = lds_v4_s32(tap_s + (uint32_t)(kin_p * 4 + kg) * 16);
+            const uint32_t bt = smem_s + (uint32_t)(s * STAGE_BYTES + 2 * A_TILE);
+            float v[8];
+            v[0] = lds_f32(pt + 4u * (uint32_t)(t4.x + pix0));
+            v[1] = lds_f32(pt + 4u * (uint32_t)(t4.y + pix0));
+            v[2] = lds_f32(pt + 4u * (uint32_t)(t4.z + pix0));
+            v[3] = lds_f32(pt + 4u * (uint32_t)(t4.w + pix0));
+            v[4] = lds_f32(pt + 4u * (uint32_t)(t4.x + pix1));
+            v[5] = lds_f32(pt + 4u * (uint32_t)(t4.y + pix1));
+            v[6] = lds_f32(pt + 4u * (uint32_t)(t4.z + pix1));
+            v[7] = lds_f32(pt + 4u * (uint32_t)(t4.w + pix1));
+            sts_v4_f32(bt + bo0, v[0], v[1], v[2], v[3]);
+            sts_v4_f32(bt + B_TILE + bo0, v[0] - tf32_trunc(v[0]), v[1] - tf32_trunc(v[1]), v[2] - tf32_trunc(v[2]),
+                       v[3] - tf32_trunc(v[3]));
+            if (two) {
+                sts_v4_f32(bt + bo1, v[4], v[5], v[6], v[7]);
+                sts_v4_f32(bt + B_TILE + bo1, v[4] - tf32_trunc(v[4]), v[5] - tf32_trunc(v[5]),
+                           v[6] - tf32_trunc(v[6]), v[7] - tf32_trunc(v[7]));
+            }
             __syncwarp();
             if (lane == 0 && (kin_p == khw - 1 || kt == ktiles - 1)) mbar_arrive(&pempty[j & 1]);
             if (s_fail || !mbar_wait(&full[s], (kt / NST) & 1)) {
