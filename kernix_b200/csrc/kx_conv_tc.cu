@@ -733,19 +733,24 @@ conv_3xtf32_pair_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_co
 //   warp 0   weight tiles by TMA (as above)
 //   warp 1   TMEM owner; the pair leader's lane 0 issues the MMAs (N = 224)
 //   warp 2   patch boxes by TMA
-//   warp 3   scans each patch for inf/NaN
 //   warps 4..11  build B hi/lo from the patch, fold the hi*hi chunks, store
 //            the output
 // The weights' lo parts are split once per call (split_weights_kernel) and
-// come by TMA beside the hi tile.
+// come by TMA beside the hi tile.  Persistent: one CTA pair per two SMs walks
+// the tiles; the TMEM accumulators of a tile are read into registers before
+// the next tile's MMAs start, so its stores overlap the next tile's loads.
 // ---------------------------------------------------------------------------
-constexpr int PP_HB = 112;                               // pixels per CTA (half the pair's 224)
-constexpr int PP_B_TILE = PP_HB * BK * 4;                // 7 KB
-constexpr int PP_STAGE = 2 * A_TILE + 2 * PP_B_TILE;     // 30 KB
+// HB pixels per CTA (half the pair's width).
+constexpr int PP_HB = 112;
+template <int HB> struct PatchTile {
+    static constexpr int B_TILE = HB * BK * 4;                   // 8 KB at 128
+    static constexpr int STAGE = 2 * A_TILE + 2 * B_TILE;        // 32 KB at 128
+    static_assert(STAGE % 1024 == 0, "stage alignment");
+    static_assert(HB % 16 == 0 && HB >= 96 && HB <= 128 && WORK_WARPS == 8,
+                  "B build: 8 warps = 4 tap groups x 2 halves of HB/2 pixels, 32 < HB/2 <= 64");
+};
 constexpr int PP_NST = 6;                                // most stages; fewer when the patch buffers are large
 constexpr int PP_CH = 16;                                // input channels per patch chunk
-static_assert(PP_HB == 2 * 56 && WORK_WARPS == 8, "B build: 8 warps = 4 tap groups x 2 halves of 56 pixels");
-static_assert(PP_STAGE % 1024 == 0, "stage alignment");
 static_assert(3 * PP_NST + 2 + 4 + 1 <= BAR_BYTES / 8, "barrier area");
 
 struct PatchGeom {
@@ -756,15 +761,14 @@ struct PatchGeom {
     int nimg;                // images
     uint32_t patch_bytes;    // one chunk: PP_CH * prows * pitch * 4
     uint32_t patch_stride;   // patch_bytes rounded up to 1 KB
-    const uint32_t *wflag;   // nonzero: some weight is NaN or infinite (set by split_weights_kernel)
 };
 
-template <int NST>
+template <int NST, int HB>
 __global__ void __launch_bounds__(NTHREADS, 1)
 conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmWlo,
                          const __grid_constant__ CUtensorMap tmX, const __grid_constant__ Params p,
                          const __grid_constant__ PatchGeom g) {
-    constexpr int HB = PP_HB, BNP = 2 * PP_HB, B_TILE = PP_B_TILE, STAGE_BYTES = PP_STAGE;
+    constexpr int BNP = 2 * HB, B_TILE = PatchTile<HB>::B_TILE, STAGE_BYTES = PatchTile<HB>::STAGE;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *patch = smem + NST * STAGE_BYTES;
@@ -778,29 +782,31 @@ conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_c
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pempty + 2);
     int32_t *tap_off = reinterpret_cast<int32_t *>(reinterpret_cast<uint8_t *>(full) + BAR_BYTES);
     __shared__ int s_fail_storage;
-    __shared__ uint32_t s_nonfinite_storage;
     volatile int &s_fail = s_fail_storage;
-    volatile uint32_t &s_nonfinite = s_nonfinite_storage;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
     const uint32_t peer = rank ^ 1u;
     const int tiles_m = (int)(p.cog / 256), tiles_n = g.nimg * g.tpi;
-    int tm, tn;
-    raster((int)(blockIdx.x >> 1), tiles_m, tiles_n, 8, tm, tn);
-    const int m0 = tm * 256 + (int)rank * BM;            // this CTA's output channels
-    const int img = tn / g.tpi;
+    const int ntiles = tiles_m * tiles_n;
+    const int pair0 = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
     const int hw = (int)p.hw, ow = (int)p.ow;
-    const int p0 = (tn % g.tpi) * BNP;                   // the pair's first pixel in the image
-    const int q0 = p0 + (int)rank * HB;                  // this CTA's first pixel
-    const int iy0 = (min(q0, hw - 1) / ow) * p.sy - p.py;   // the patch's first input row
     const int grp = blockIdx.y;
     const int khw = p.kh * p.kw;
     const int ktiles = (p.kk + BK - 1) / BK;
-    const int nchunks = (ktiles + KC - 1) / KC;
     const int npatch = (ktiles + khw - 1) / khw;
     const int ch_floats = g.prows * g.pitch;
+    // tile -> this CTA's output channels m0, image, the pair's first pixel p0
+    // and this CTA's first pixel q0 (112 pixels from it)
+    auto tile_of = [&](int t, int &m0, int &img, int &p0, int &q0) {
+        int tm, tn;
+        raster(t, tiles_m, tiles_n, 8, tm, tn);
+        m0 = tm * 256 + (int)rank * BM;
+        img = tn / g.tpi;
+        p0 = (tn % g.tpi) * BNP;
+        q0 = p0 + (int)rank * HB;
+    };
 
     // patch offset of chunk-local tap kl = (ci, ky, kx)
     for (int kl = threadIdx.x; kl < PP_CH * khw; kl += NTHREADS) {
@@ -817,10 +823,9 @@ conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_c
         mbar_init(chunk_empty, 2 * WORK_WARPS);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&pfull[b], 1);
-            mbar_init(&pempty[b], WORK_WARPS + 1);     // the workers and the scanning warp
+            mbar_init(&pempty[b], WORK_WARPS);
         }
         s_fail = 0;
-        s_nonfinite = *g.wflag != 0u;   // written by the weight split earlier in the stream
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
@@ -835,24 +840,29 @@ conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_c
     const uint32_t tmem = *tmem_slot;
 
     auto stage_a = [&](int s) { return smem + s * STAGE_BYTES; };
-    auto stage_b = [&](int s) { return smem + s * STAGE_BYTES + 2 * A_TILE; };
 
+    // Every role walks the same tiles (pair0, pair0 + npairs, ...) with
+    // stage, patch-buffer and TMEM-chunk counters that run on across tiles.
     if (warp == 0) {
         if (lane == 0) {
-            int issued = 0;
-            for (int kt = 0; kt < ktiles && !s_fail; ++kt) {
-                const int s = kt % NST;
-                if (kt >= NST && !mbar_wait(&empty[s], ((kt / NST) - 1) & 1)) {
-                    s_fail = 1;
-                    break;
+            uint32_t gkt = 0;
+            for (int t = pair0; t < ntiles && !s_fail; t += npairs) {
+                int m0, img, p0, q0;
+                tile_of(t, m0, img, p0, q0);
+                for (int kt = 0; kt < ktiles; ++kt, ++gkt) {
+                    const uint32_t s = gkt % NST;
+                    if (gkt >= NST && !mbar_wait(&empty[s], ((gkt / NST) - 1) & 1)) {
+                        s_fail = 1;
+                        break;
+                    }
+                    mbar_expect_tx(&full[s], 2 * A_TILE);
+                    tma_load_3d(stage_a(s), &tmW, kt * BK, m0, grp, &full[s]);
+                    tma_load_3d(stage_a(s) + A_TILE, &tmWlo, kt * BK, m0, grp, &full[s]);
                 }
-                mbar_expect_tx(&full[s], 2 * A_TILE);
-                tma_load_3d(stage_a(s), &tmW, kt * BK, m0, grp, &full[s]);
-                tma_load_3d(stage_a(s) + A_TILE, &tmWlo, kt * BK, m0, grp, &full[s]);
-                issued = kt + 1;
             }
-            for (int s = 0; s < NST && s < issued; ++s) {
-                const int last = s + NST * ((issued - 1 - s) / NST);
+            // no TMA write may still be in flight when the CTA exits
+            for (uint32_t s = 0; s < NST && s < gkt; ++s) {
+                const uint32_t last = s + NST * ((gkt - 1 - s) / NST);
                 mbar_wait(&full[s], (last / NST) & 1);
             }
         }
@@ -860,34 +870,40 @@ conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_c
         if (leader && lane == 0) {
             constexpr uint32_t idesc = idesc_pair(false, BNP);
             const uint32_t chunk_full_peer = map_to(smem_u32(chunk_full), peer);
-            for (int kt = 0; kt < ktiles; ++kt) {
-                const int s = kt % NST;
-                const int chunk = kt / KC, kin = kt % KC;
-                if (kin == 0 && chunk > 0 && (s_fail || !mbar_wait_cluster(chunk_empty, (chunk - 1) & 1))) {
-                    s_fail = 1;
-                    break;
-                }
-                if (s_fail || !mbar_wait_cluster(&conv[s], (kt / NST) & 1)) {
-                    s_fail = 1;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t a_hi = smem_u32(stage_a(s)), a_lo = a_hi + A_TILE;
-                const uint32_t b_hi = smem_u32(stage_b(s)), b_lo = b_hi + B_TILE;
+            uint32_t gkt = 0, gc = 0;
+            for (int t = pair0; t < ntiles && !s_fail; t += npairs) {
+                for (int kt = 0; kt < ktiles; ++kt, ++gkt) {
+                    const uint32_t s = gkt % NST;
+                    const int kin = kt % KC;
+                    // the workers have folded the previous chunk (and, at a
+                    // tile's first k-tile, read the last tile's accumulators)
+                    if (kin == 0 && gc > 0 && (s_fail || !mbar_wait_cluster(chunk_empty, (gc - 1) & 1))) {
+                        s_fail = 1;
+                        break;
+                    }
+                    if (s_fail || !mbar_wait_cluster(&conv[s], (gkt / NST) & 1)) {
+                        s_fail = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_hi = smem_u32(stage_a(s)), a_lo = a_hi + A_TILE;
+                    const uint32_t b_hi = a_hi + 2 * A_TILE, b_lo = b_hi + B_TILE;
 #pragma unroll
-                for (int ks = 0; ks < BK / 8; ++ks) {
-                    const uint64_t dah = desc_k_sw64(a_hi + ks * 32), dal = desc_k_sw64(a_lo + ks * 32);
-                    const uint64_t dbh = desc_k_sw64(b_hi + ks * 32), dbl = desc_k_sw64(b_lo + ks * 32);
-                    mma_pair(tmem, dah, dbh, idesc, (kin > 0 || ks > 0) ? 1u : 0u);
-                    mma_pair(tmem + XCOL, dah, dbl, idesc, (kt > 0 || ks > 0) ? 1u : 0u);
-                    mma_pair(tmem + XCOL, dal, dbh, idesc, 1u);
-                }
-                const uint32_t e_local = smem_u32(&empty[s]);
-                commit_pair(e_local);
-                commit_pair(map_to(e_local, peer));
-                if (kin == KC - 1 || kt == ktiles - 1) {
-                    commit_pair(smem_u32(chunk_full));
-                    commit_pair(chunk_full_peer);
+                    for (int ks = 0; ks < BK / 8; ++ks) {
+                        const uint64_t dah = desc_k_sw64(a_hi + ks * 32), dal = desc_k_sw64(a_lo + ks * 32);
+                        const uint64_t dbh = desc_k_sw64(b_hi + ks * 32), dbl = desc_k_sw64(b_lo + ks * 32);
+                        mma_pair(tmem, dah, dbh, idesc, (kin > 0 || ks > 0) ? 1u : 0u);
+                        mma_pair(tmem + XCOL, dah, dbl, idesc, (kt > 0 || ks > 0) ? 1u : 0u);
+                        mma_pair(tmem + XCOL, dal, dbh, idesc, 1u);
+                    }
+                    const uint32_t e_local = smem_u32(&empty[s]);
+                    commit_pair(e_local);
+                    commit_pair(map_to(e_local, peer));
+                    if (kin == KC - 1 || kt == ktiles - 1) {
+                        commit_pair(smem_u32(chunk_full));
+                        commit_pair(chunk_full_peer);
+                        ++gc;
+                    }
                 }
             }
             if (s_fail) {
@@ -897,44 +913,26 @@ conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_c
         }
     } else if (warp == 2) {
         if (lane == 0) {
-            int issued = 0;
+            uint32_t gj = 0;
             const int c0 = grp * (int)p.cg;
-            for (int j = 0; j < npatch && !s_fail; ++j) {
-                const int b = j & 1;
-                if (j >= 2 && !mbar_wait(&pempty[b], ((j >> 1) - 1) & 1)) {
-                    s_fail = 1;
-                    break;
+            for (int t = pair0; t < ntiles && !s_fail; t += npairs) {
+                int m0, img, p0, q0;
+                tile_of(t, m0, img, p0, q0);
+                const int iy0 = (min(q0, hw - 1) / ow) * p.sy - p.py;   // the patch's first input row
+                for (int j = 0; j < npatch; ++j, ++gj) {
+                    const uint32_t b = gj & 1;
+                    if (gj >= 2 && !mbar_wait(&pempty[b], ((gj >> 1) - 1) & 1)) {
+                        s_fail = 1;
+                        break;
+                    }
+                    mbar_expect_tx(&pfull[b], g.patch_bytes);
+                    tma_load_4d(patch + b * g.patch_stride, &tmX, g.x0, iy0, c0 + PP_CH * j, img, &pfull[b]);
                 }
-                mbar_expect_tx(&pfull[b], g.patch_bytes);
-                tma_load_4d(patch + b * g.patch_stride, &tmX, g.x0, iy0, c0 + PP_CH * j, img, &pfull[b]);
-                issued = j + 1;
             }
-            for (int b = 0; b < 2 && b < issued; ++b) {
-                const int last = b + 2 * ((issued - 1 - b) / 2);
+            for (uint32_t b = 0; b < 2 && b < gj; ++b) {
+                const uint32_t last = b + 2 * ((gj - 1 - b) / 2);
                 mbar_wait(&pfull[b], (last >> 1) & 1);
             }
-        }
-    } else if (warp == 3) {
-        // Scan each patch chunk for inf/NaN once it has landed, then release
-        // it with the workers (an element no output uses can only send the
-        // tile to the FMA fallback, which is exact).
-        for (int j = 0; j < npatch; ++j) {
-            if (s_fail || !mbar_wait(&pfull[j & 1], (j >> 1) & 1)) {
-                s_fail = 1;
-                break;
-            }
-            const float4 *pv = reinterpret_cast<const float4 *>(patch + (j & 1) * g.patch_stride);
-            float probe = 0.0f;     // becomes NaN iff the chunk holds an inf or NaN
-            for (uint32_t e = lane; e < g.patch_bytes / 16; e += 32) {
-                const float4 v = pv[e];
-                probe = fmaf(v.x, 0.0f, probe);
-                probe = fmaf(v.y, 0.0f, probe);
-                probe = fmaf(v.z, 0.0f, probe);
-                probe = fmaf(v.w, 0.0f, probe);
-            }
-            if (__any_sync(0xffffffffu, probe != probe) && lane == 0) s_nonfinite = 1u;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&pempty[j & 1]);
         }
     } else if (warp >= WORK_WARP0) {
         const int ww = warp - WORK_WARP0;
@@ -945,147 +943,152 @@ conv_3xtf32_patch_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_c
         // B build: lane = pixel, thread = 4 consecutive taps, i.e. one 16-byte
         // row segment of the K-major tile with the 64-byte swizzle (as the TMA
         // writes A): pixel r, taps 4g..4g+3 at byte 64 r + 16 (g ^ ((r/2)%4)).
-        // Warp ww writes tap group g = ww%4 of pixels 56 (ww/4) + [0, 56):
-        // lanes 0..31, then lanes 0..23.  Each quarter-warp store covers 32
+        // Warp ww writes tap group g = ww%4 of pixels HB/2 (ww/4) + [0, HB/2):
+        // lanes 0..31, then lanes 0..HB/2-33.  Each quarter-warp store covers 32
         // distinct banks; the patch reads of a warp are consecutive pixels.
         // Rows of pixels past the image read the last pixel (their outputs are
         // never stored) and taps past the group read whatever the patch holds
-        // there (their weights are zero).  Warp 3 scans every patch chunk for
-        // inf/NaN, so neither reaches a stored result.
+        // there (their weights are zero).  Neither reaches a stored result:
+        // an inf or NaN anywhere in a product makes the accumulated output
+        // nonfinite (the lo part of an inf is NaN, and 0 * inf is NaN), and
+        // an output row segment with a nonfinite value is recomputed with f32
+        // FMA in tap order, as the SIMT implicit GEMM computes it.
         const int kg = ww & 3;
-        const int r0 = 56 * (ww >> 2) + lane, r1 = r0 + 32;
-        const bool two = lane < 24;
-        const int oy_a = min(q0, hw - 1) / ow;
-        auto pix_of = [&](int r) {
-            const int q = min(q0 + r, hw - 1);
-            const int oy = q / ow, ox = q % ow;
-            return (oy - oy_a) * p.sy * g.pitch + (ox * p.sx - p.px - g.x0);
-        };
-        // lanes without a second pixel read their first one again (stores skipped)
-        const int pix0 = pix_of(r0), pix1 = two ? pix_of(r1) : pix0;
+        const int r0 = (HB / 2) * (ww >> 2) + lane, r1 = r0 + 32;
+        const bool two = lane < HB / 2 - 32;
         const uint32_t bo0 = (uint32_t)r0 * 64 + ((uint32_t)(kg ^ ((r0 >> 1) & 3)) << 4);
         const uint32_t bo1 = (uint32_t)r1 * 64 + ((uint32_t)(kg ^ ((r1 >> 1) & 3)) << 4);
         const uint32_t smem_s = smem_u32(smem), patch_s = smem_u32(patch), tap_s = smem_u32(tap_off);
-        float sum[HB];
+        const int ih = (int)p.ih, iw = (int)p.iw;
+        const bool vec_ok = (p.hw % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.y) & 15) == 0);
+        uint32_t gkt = 0, gj = 0, gc = 0;
+        for (int t = pair0; t < ntiles && !s_fail; t += npairs) {
+            int m0, img, p0, q0;
+            tile_of(t, m0, img, p0, q0);
+            const int oy_a = min(q0, hw - 1) / ow;
+            auto pix_of = [&](int r) {
+                const int q = min(q0 + r, hw - 1);
+                const int oy = q / ow, ox = q % ow;
+                return (oy - oy_a) * p.sy * g.pitch + (ox * p.sx - p.px - g.x0);
+            };
+            // lanes without a second pixel read their first one again (stores skipped)
+            const int pix0 = pix_of(r0), pix1 = two ? pix_of(r1) : pix0;
+            float sum[HB];
 #pragma unroll
-        for (int j = 0; j < HB; ++j) sum[j] = 0.0f;
-        int chunk = 0;
-        int j = 0, kin_p = 0;     // patch chunk of k-tile kt and its k-tile within the chunk
-        for (int kt = 0; kt < ktiles; ++kt) {
-            const int s = kt % NST;
-            if (kt >= NST && (s_fail || !mbar_wait(&empty[s], ((kt / NST) - 1) & 1))) {
-                s_fail = 1;
-                break;
-            }
-            if (kin_p == 0 && (s_fail || !mbar_wait(&pfull[j & 1], (j >> 1) & 1))) {
-                s_fail = 1;
-                break;
-            }
-            // shared addresses in bytes; all eight loads go out before any store
-            const uint32_t pt = patch_s + (uint32_t)(j & 1) * g.patch_stride;
-            const int4 t4 = lds_v4_s32(tap_s + (uint32_t)(kin_p * 4 + kg) * 16);
-            const uint32_t bt = smem_s + (uint32_t)(s * STAGE_BYTES + 2 * A_TILE);
-            float v[8];
-            v[0] = lds_f32(pt + 4u * (uint32_t)(t4.x + pix0));
-            v[1] = lds_f32(pt + 4u * (uint32_t)(t4.y + pix0));
-            v[2] = lds_f32(pt + 4u * (uint32_t)(t4.z + pix0));
-            v[3] = lds_f32(pt + 4u * (uint32_t)(t4.w + pix0));
-            v[4] = lds_f32(pt + 4u * (uint32_t)(t4.x + pix1));
-            v[5] = lds_f32(pt + 4u * (uint32_t)(t4.y + pix1));
-            v[6] = lds_f32(pt + 4u * (uint32_t)(t4.z + pix1));
-            v[7] = lds_f32(pt + 4u * (uint32_t)(t4.w + pix1));
-            sts_v4_f32(bt + bo0, v[0], v[1], v[2], v[3]);
-            sts_v4_f32(bt + B_TILE + bo0, v[0] - tf32_trunc(v[0]), v[1] - tf32_trunc(v[1]), v[2] - tf32_trunc(v[2]),
-                       v[3] - tf32_trunc(v[3]));
-            if (two) {
-                sts_v4_f32(bt + bo1, v[4], v[5], v[6], v[7]);
-                sts_v4_f32(bt + B_TILE + bo1, v[4] - tf32_trunc(v[4]), v[5] - tf32_trunc(v[5]),
-                           v[6] - tf32_trunc(v[6]), v[7] - tf32_trunc(v[7]));
-            }
-            __syncwarp();
-            if (lane == 0 && (kin_p == khw - 1 || kt == ktiles - 1)) mbar_arrive(&pempty[j & 1]);
-            if (s_fail || !mbar_wait(&full[s], (kt / NST) & 1)) {
-                s_fail = 1;
-                break;
-            }
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(conv_leader0 + (uint32_t)(s * 8));
-            if (kt % KC == KC - 1 || kt == ktiles - 1) {
-                if (!mbar_wait(chunk_full, chunk & 1)) {
+            for (int j = 0; j < HB; ++j) sum[j] = 0.0f;
+            int kin_p = 0;          // k-tile within the current patch chunk
+            bool done = false;      // the tile's accumulators are in sum[]
+            for (int kt = 0; kt < ktiles; ++kt, ++gkt) {
+                const uint32_t s = gkt % NST;
+                if (gkt >= NST && (s_fail || !mbar_wait(&empty[s], ((gkt / NST) - 1) & 1))) {
                     s_fail = 1;
                     break;
                 }
-                tc_fence_after();
-                if (s_fail) break;
-                tmem_accumulate(tmem, quarter, col0, sum);
-                tc_fence_before();
+                if (kin_p == 0 && (s_fail || !mbar_wait(&pfull[gj & 1], (gj >> 1) & 1))) {
+                    s_fail = 1;
+                    break;
+                }
+                // shared addresses in bytes; all eight loads go out before any store
+                const uint32_t pt = patch_s + (gj & 1) * g.patch_stride;
+                const int4 t4 = lds_v4_s32(tap_s + (uint32_t)(kin_p * 4 + kg) * 16);
+                const uint32_t bt = smem_s + s * STAGE_BYTES + 2 * A_TILE;
+                float v[8];
+                v[0] = lds_f32(pt + 4u * (uint32_t)(t4.x + pix0));
+                v[1] = lds_f32(pt + 4u * (uint32_t)(t4.y + pix0));
+                v[2] = lds_f32(pt + 4u * (uint32_t)(t4.z + pix0));
+                v[3] = lds_f32(pt + 4u * (uint32_t)(t4.w + pix0));
+                v[4] = lds_f32(pt + 4u * (uint32_t)(t4.x + pix1));
+                v[5] = lds_f32(pt + 4u * (uint32_t)(t4.y + pix1));
+                v[6] = lds_f32(pt + 4u * (uint32_t)(t4.z + pix1));
+                v[7] = lds_f32(pt + 4u * (uint32_t)(t4.w + pix1));
+                sts_v4_f32(bt + bo0, v[0], v[1], v[2], v[3]);
+                sts_v4_f32(bt + B_TILE + bo0, v[0] - tf32_trunc(v[0]), v[1] - tf32_trunc(v[1]),
+                           v[2] - tf32_trunc(v[2]), v[3] - tf32_trunc(v[3]));
+                if (two) {
+                    sts_v4_f32(bt + bo1, v[4], v[5], v[6], v[7]);
+                    sts_v4_f32(bt + B_TILE + bo1, v[4] - tf32_trunc(v[4]), v[5] - tf32_trunc(v[5]),
+                               v[6] - tf32_trunc(v[6]), v[7] - tf32_trunc(v[7]));
+                }
                 __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(chunk_empty_leader);
-                ++chunk;
-            }
-            if (++kin_p == khw) {
-                kin_p = 0;
-                ++j;
-            }
-        }
-        tc_fence_before();
-        cluster_sync_any();     // pair-wide: both CTAs' nonfinite flags are final
-        tc_fence_after();
-        const uint32_t nonfinite = s_nonfinite | ld_cluster_u32(map_to(smem_u32((const void *)&s_nonfinite_storage), peer));
-        const int co = m0 + quarter * 32 + lane;
-        const bool row_ok = co < p.cog;
-        const int64_t co_abs = (int64_t)grp * p.cog + co;
-        float *yrow = p.y + ((int64_t)img * p.co_total + co_abs) * p.hw;
-        if (!s_fail && chunk == nchunks) {
-            if (nonfinite) {
-                // the tile again with f32 FMA in tap order, as the SIMT implicit GEMM computes it
-                if (row_ok) {
-                    const float *wrow = p.w + co_abs * p.ws0;
-                    const int ih = (int)p.ih, iw = (int)p.iw;
-                    const float *ximg = p.x + (int64_t)img * p.xs[0] + (int64_t)grp * p.cg * p.xs[1];
-                    for (int jj = 0; jj < HB; ++jj) {
-                        const int q = p0 + col0 + jj;
-                        if (q >= hw) break;
-                        const int y0 = (q / ow) * p.sy - p.py, x0 = (q % ow) * p.sx - p.px;
-                        float acc = 0.0f;
-                        for (int k = 0; k < p.kk; ++k) {
-                            const int ci = k / khw, r = k % khw;
-                            const int iy = y0 + (r / p.kw) * p.dy, ix = x0 + (r % p.kw) * p.dx;
-                            const float xv = (iy >= 0 && iy < ih && ix >= 0 && ix < iw)
-                                                 ? ximg[(int64_t)ci * p.xs[1] + (int64_t)iy * p.xs[2] + (int64_t)ix * p.xs[3]]
-                                                 : 0.0f;
-                            acc = fmaf(wrow[k], xv, acc);
-                        }
-                        yrow[q] = acc;
+                const bool chunk_end = kin_p == khw - 1 || kt == ktiles - 1;
+                if (lane == 0 && chunk_end) mbar_arrive(&pempty[gj & 1]);
+                if (s_fail || !mbar_wait(&full[s], (gkt / NST) & 1)) {
+                    s_fail = 1;
+                    break;
+                }
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(conv_leader0 + s * 8);
+                if (chunk_end) {
+                    kin_p = 0;
+                    ++gj;
+                } else {
+                    ++kin_p;
+                }
+                if (kt % KC == KC - 1 || kt == ktiles - 1) {
+                    if (!mbar_wait(chunk_full, gc & 1)) {
+                        s_fail = 1;
+                        break;
                     }
+                    tc_fence_after();
+                    if (s_fail) break;
+                    tmem_accumulate(tmem, quarter, col0, sum);
+                    if (kt == ktiles - 1) {
+                        // the cross terms too, before the MMAs of the next tile overwrite them
+                        tmem_accumulate(tmem + XCOL, quarter, col0, sum);
+                        done = true;
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(chunk_empty_leader);
+                    ++gc;
+                }
+            }
+            if (!done) break;
+            // store this thread's output row segment (channel co, pixels p0 + col0 + [0, 112))
+            const int co = m0 + quarter * 32 + lane;
+            const int64_t co_abs = (int64_t)grp * p.cog + co;
+            float *yrow = p.y + ((int64_t)img * p.co_total + co_abs) * p.hw;
+            float probe = 0.0f;     // NaN iff some sum is inf or NaN
+#pragma unroll
+            for (int jj = 0; jj < HB; ++jj) probe = fmaf(sum[jj], 0.0f, probe);
+            if (probe != probe) {
+                const float *wrow = p.w + co_abs * p.ws0;
+                const float *ximg = p.x + (int64_t)img * p.xs[0] + (int64_t)grp * p.cg * p.xs[1];
+                for (int jj = 0; jj < HB; ++jj) {
+                    const int q = p0 + col0 + jj;
+                    if (q >= hw) break;
+                    const int y0 = (q / ow) * p.sy - p.py, x0 = (q % ow) * p.sx - p.px;
+                    float acc = 0.0f;
+                    for (int k = 0; k < p.kk; ++k) {
+                        const int ci = k / khw, r = k % khw;
+                        const int iy = y0 + (r / p.kw) * p.dy, ix = x0 + (r % p.kw) * p.dx;
+                        const float xv = (iy >= 0 && iy < ih && ix >= 0 && ix < iw)
+                                             ? ximg[(int64_t)ci * p.xs[1] + (int64_t)iy * p.xs[2] + (int64_t)ix * p.xs[3]]
+                                             : 0.0f;
+                        acc = fmaf(wrow[k], xv, acc);
+                    }
+                    yrow[q] = acc;
                 }
             } else {
-                const bool vec_ok = (p.hw % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.y) & 15) == 0);
 #pragma unroll
                 for (int c = 0; c < HB / 16; ++c) {
-                    uint32_t r[16];
-                    tmem_ld16(tmem + XCOL + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(col0 + c * 16), r);
-                    tmem_wait_ld();
-                    if (!row_ok) continue;
-                    float v[16];
-#pragma unroll
-                    for (int jj = 0; jj < 16; ++jj) v[jj] = sum[c * 16 + jj] + __uint_as_float(r[jj]);
                     const int q = p0 + col0 + c * 16;
                     if (vec_ok && q + 16 <= hw) {
 #pragma unroll
                         for (int jj = 0; jj < 16; jj += 4)
-                            *reinterpret_cast<float4 *>(yrow + q + jj) = make_float4(v[jj], v[jj + 1], v[jj + 2], v[jj + 3]);
+                            *reinterpret_cast<float4 *>(yrow + q + jj) =
+                                make_float4(sum[c * 16 + jj], sum[c * 16 + jj + 1], sum[c * 16 + jj + 2],
+                                            sum[c * 16 + jj + 3]);
                     } else {
 #pragma unroll
                         for (int jj = 0; jj < 16; ++jj)
-                            if (q + jj < hw) yrow[q + jj] = v[jj];
+                            if (q + jj < hw) yrow[q + jj] = sum[c * 16 + jj];
                     }
                 }
             }
         }
     }
-    if (warp < WORK_WARP0) cluster_sync_any();
     tc_fence_before();
     cluster_sync_any();
     if (warp == 1) {
@@ -1116,13 +1119,12 @@ __global__ void pack_weights_kernel(const float *__restrict__ w, int64_t ws0, in
 
 // The patch-staged kernel's weights: dense hi rows (when `hi` is given; the
 // caller's rows are used in place otherwise) and their lo parts w - tf32(w),
-// `pitch` floats per output channel in tap order, zero beyond the taps.  A
-// NaN or infinite weight sets *flag.
+// `pitch` floats per output channel in tap order, zero beyond the taps (the
+// lo part of an infinite weight is NaN, which the kernel's epilogue catches).
 __global__ void split_weights_kernel(const float *__restrict__ w, int64_t ws0, int64_t ws1, int64_t ws2, int64_t ws3,
                                      int64_t co, int kh, int kw, int kk, int pitch, float *__restrict__ hi,
-                                     float *__restrict__ lo, uint32_t *flag) {
+                                     float *__restrict__ lo) {
     const int64_t total = co * pitch;
-    bool bad = false;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t o = e / pitch;
         const int k = (int)(e % pitch);
@@ -1134,9 +1136,7 @@ __global__ void split_weights_kernel(const float *__restrict__ w, int64_t ws0, i
         }
         if (hi) hi[e] = v;
         lo[e] = v - tf32_trunc(v);
-        bad |= !isfinite(v);
     }
-    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(flag, 1u);
 }
 
 }  // namespace conv
@@ -1206,21 +1206,30 @@ int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, co
         const int64_t x0 = -((px + 3) / 4) * 4;
         const int64_t xmax = (ow - 1) * sx - px + (kw - 1) * dx;
         const int64_t pitch = (xmax - x0 + 1 + 3) / 4 * 4;
-        const int64_t tpi = (hw + 2 * PP_HB - 1) / (2 * PP_HB);
-        int64_t span = 0;
-        for (int64_t q0 = 0; q0 < hw; q0 += PP_HB) {
-            const int64_t qb = std::min(q0 + PP_HB, hw) - 1;
-            span = std::max(span, qb / ow - q0 / ow);
-        }
-        const int64_t prows = span * sy + (kh - 1) * dy + 1;
-        const int64_t patch_bytes = (int64_t)PP_CH * prows * pitch * 4;
-        const int64_t patch_stride = (patch_bytes + 1023) / 1024 * 1024;
-        const int64_t smem_fixed = 2 * patch_stride + BAR_BYTES + PP_CH * kh * kw * 4 + 1024;
-        // as many stages as fit: the weight tile of k-tile kt is fetched when
-        // the MMAs of kt - nst have freed its stage
+        // patch geometry for halves of hb pixels: rows under the widest half
+        auto patch_for = [&](int64_t hb, int64_t &prows, int64_t &patch_bytes, int64_t &patch_stride) {
+            int64_t span = 0;
+            for (int64_t q0 = 0; q0 < hw; q0 += hb) {
+                const int64_t qb = std::min(q0 + hb, hw) - 1;
+                span = std::max(span, qb / ow - q0 / ow);
+            }
+            prows = span * sy + (kh - 1) * dy + 1;
+            patch_bytes = (int64_t)PP_CH * prows * pitch * 4;
+            patch_stride = (patch_bytes + 1023) / 1024 * 1024;
+            return 2 * patch_stride + BAR_BYTES + PP_CH * kh * kw * 4 + 1024;
+        };
+        // 112-pixel halves: 128 (N = 256 per pair) measured slower on c4
+        // (149.0 vs 145.3 TFLOP/s: register spills and taller patches)
+        constexpr int hb = PP_HB;
+        int64_t prows, patch_bytes, patch_stride;
+        const int64_t smem_fixed = patch_for(hb, prows, patch_bytes, patch_stride);
+        const int64_t stage_bytes = PatchTile<hb>::STAGE;
+        const int64_t tpi = (hw + 2 * hb - 1) / (2 * hb);
+        // as many stages as fit (up to PP_NST): the weight tile of k-tile kt is
+        // fetched when the MMAs of kt - nst have freed its stage
         int nst = PP_NST;
-        while (nst > 3 && smem_fixed + (int64_t)nst * PP_STAGE > SMEM_LIMIT) --nst;
-        const int64_t smem = smem_fixed + (int64_t)nst * PP_STAGE;
+        while (nst > 3 && smem_fixed + (int64_t)nst * stage_bytes > SMEM_LIMIT) --nst;
+        const int64_t smem = smem_fixed + (int64_t)nst * stage_bytes;
         const int64_t pairs = (cog / 256) * n * tpi * groups;
         CUtensorMap mx;
         const uint64_t dims[4] = {(uint64_t)iw, (uint64_t)ih, (uint64_t)c, (uint64_t)n};
@@ -1230,8 +1239,7 @@ int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, co
             (2 * pairs >= h->sm_count || h->f32_variant == KX_F32_3XTF32) && make_map4(&mx, x, dims, strides, box)) {
             // The weights' lo parts (and the dense hi rows when the caller's
             // layout is not) go to the workspace once per call; the kernel
-            // loads both by TMA.  A nonfinite weight raises the flag word,
-            // which sends every tile to the FMA fallback.
+            // loads both by TMA.
             const int64_t wp = repack ? (kk + 3) / 4 * 4 : ws[0];
             const uint64_t part = (uint64_t)co * wp * sizeof(float);
             void *buf = nullptr;
@@ -1240,15 +1248,12 @@ int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, co
             float *hi = repack ? static_cast<float *>(buf) : nullptr;
             float *lo = static_cast<float *>(buf) + (repack ? co * wp : 0);
             const float *whi = repack ? hi : w;
-            cudaError_t ce = cudaMemsetAsync(h->flags + kConvLoWord, 0, sizeof(uint32_t), h->stream);
-            if (ce == cudaSuccess) {
-                int64_t blocks = (co * wp + 255) / 256;
-                if (blocks > 4LL * h->sm_count) blocks = 4LL * h->sm_count;
-                split_weights_kernel<<<(unsigned)blocks, 256, 0, h->stream>>>(
-                    w, ws[0], ws[1], ws[2], ws[3], co, (int)kh, (int)kw, (int)kk, (int)wp, hi, lo, h->flags + kConvLoWord);
-                ++h->launches;
-                ce = cudaGetLastError();
-            }
+            int64_t blocks = (co * wp + 255) / 256;
+            if (blocks > 4LL * h->sm_count) blocks = 4LL * h->sm_count;
+            split_weights_kernel<<<(unsigned)blocks, 256, 0, h->stream>>>(w, ws[0], ws[1], ws[2], ws[3], co, (int)kh,
+                                                                           (int)kw, (int)kk, (int)wp, hi, lo);
+            ++h->launches;
+            cudaError_t ce = cudaGetLastError();
             if (ce != cudaSuccess) return h->cuda_fail(ce);
             CUtensorMap mw, mwlo;
             if (!make_map(&mw, whi, (uint64_t)kk, (uint64_t)cog, (uint64_t)groups, (uint64_t)wp * 4,
@@ -1265,15 +1270,17 @@ int run_conv_tc(Handle *h, const float *x, const int64_t *xs, const float *w, co
             g.nimg = (int)n;
             g.patch_bytes = (uint32_t)patch_bytes;
             g.patch_stride = (uint32_t)patch_stride;
-            g.wflag = h->flags + kConvLoWord;
-            auto k = nst == 6 ? conv_3xtf32_patch_kernel<6>
-                     : nst == 5 ? conv_3xtf32_patch_kernel<5>
-                     : nst == 4 ? conv_3xtf32_patch_kernel<4>
-                                : conv_3xtf32_patch_kernel<3>;
+            auto k = nst == 6 ? conv_3xtf32_patch_kernel<6, hb>
+                     : nst == 5 ? conv_3xtf32_patch_kernel<5, hb>
+                     : nst == 4 ? conv_3xtf32_patch_kernel<4, hb>
+                                : conv_3xtf32_patch_kernel<3, hb>;
             ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             if (ce == cudaSuccess) {
                 cudaLaunchConfig_t cfg = {};
-                cfg.gridDim = dim3((unsigned)(2 * pairs / groups), (unsigned)groups, 1);
+                // persistent: one pair per two SMs in all, each group's pairs walking its tiles
+                const int64_t per_group = pairs / groups;
+                const int64_t launch = std::min(per_group, std::max<int64_t>(1, h->sm_count / 2 / groups));
+                cfg.gridDim = dim3((unsigned)(2 * launch), (unsigned)groups, 1);
                 cfg.blockDim = dim3(NTHREADS, 1, 1);
                 cfg.dynamicSmemBytes = (size_t)smem;
                 cfg.stream = h->stream;

@@ -116,11 +116,9 @@ int mc_copy(Handle *h, const void *src, void *mc_dst, uint64_t bytes);
 //   [1]     status written by device code: bit 0 = a bounded wait expired
 //   [2..3]  softmax: 64-bit key of the first nonfinite element (8-byte aligned)
 //   [4]     conv2d: some weight is NaN or infinite
-//   [5]     conv2d, patch-staged kernel: a weight it split is NaN or infinite
 constexpr int kStatusWord = 1;
 constexpr int kSoftmaxWord = 2;
 constexpr int kConvFlagWord = 4;
-constexpr int kConvLoWord = 5;
 
 }  // namespace kx
 

@@ -65,7 +65,7 @@ PATCH_GEOMETRIES = [
 def expected_kernel(xs, ws, opts):
     if (ws[0] // opts["groups"]) % 256:
         return "conv_tc_3xtf32_128x128"
-    return "conv_tc_3xtf32_patch_256x224" if xs[3] % 4 == 0 else "conv_tc_3xtf32_pair_256x256"
+    return "conv_tc_3xtf32_patch_256x" if xs[3] % 4 == 0 else "conv_tc_3xtf32_pair_256x256"
 
 
 @pytest.mark.parametrize("xs,ws,opts", GEOMETRIES + PATCH_GEOMETRIES)
@@ -76,7 +76,7 @@ def test_conv_tc_geometries(kx, torch_cuda, tc, xs, ws, opts):
     x = rng.uniform(-1, 1, xs).astype(np.float32)
     wt = rng.normal(0, math.sqrt(2 / (c // opts["groups"] * kh * kw)), (co, c // opts["groups"], kh, kw)).astype(np.float32)
     _check(kx, torch_cuda, x, wt, opts)
-    assert tc.last_kernel == expected_kernel(xs, ws, opts), tc.last_kernel
+    assert tc.last_kernel.startswith(expected_kernel(xs, ws, opts)), tc.last_kernel
 
 
 def test_conv_patch_channel_and_image_strides(kx, torch_cuda, tc):
@@ -91,7 +91,7 @@ def test_conv_patch_channel_and_image_strides(kx, torch_cuda, tc):
     xv = kx.TensorView(dev, (2, 20, 14, 16), (2 * 40 * 14 * 16, 2 * 14 * 16, 16, 1), 0)
     _check(kx, torch, np.ascontiguousarray(x), wt, dict(stride=(1, 1), padding=(1, 1), dilation=(1, 1), groups=1),
            x_dev=xv)
-    assert tc.last_kernel == "conv_tc_3xtf32_patch_256x224"
+    assert tc.last_kernel.startswith("conv_tc_3xtf32_patch_256x"), tc.last_kernel
 
 
 def test_conv_tc_reversed_and_strided_input(kx, torch_cuda, tc):
@@ -124,7 +124,7 @@ def test_conv_tc_nonfinite_input_tiles(kx, torch_cuda, tc, co, width):
     wt = np.abs(rng.normal(0, 0.1, (co, 32, 3, 3))).astype(np.float32)
     opts = kx.Conv2dOptions(padding=(1, 1))
     got = kx.conv2d(to_dev(x, torch), to_dev(wt, torch), opts).cpu().numpy()
-    assert tc.last_kernel == expected_kernel(x.shape, wt.shape, dict(groups=1)), tc.last_kernel
+    assert tc.last_kernel.startswith(expected_kernel(x.shape, wt.shape, dict(groups=1))), tc.last_kernel
     tc.set_f32_variant(1)
     ref = kx.conv2d(to_dev(x, torch), to_dev(wt, torch), opts).cpu().numpy()
     assert np.array_equal(np.isnan(got), np.isnan(ref))
@@ -186,7 +186,7 @@ def test_conv_patch_nonfinite_weights_fall_back(kx, torch_cuda, tc):
     wt[7, 3, 1, 1] = np.inf
     opts = kx.Conv2dOptions(padding=(1, 1))
     got = kx.conv2d(to_dev(x, torch), to_dev(wt, torch), opts).cpu().numpy()
-    assert tc.last_kernel == "conv_tc_3xtf32_patch_256x224", tc.last_kernel
+    assert tc.last_kernel.startswith("conv_tc_3xtf32_patch_256x"), tc.last_kernel
     tc.set_f32_variant(1)
     ref = kx.conv2d(to_dev(x, torch), to_dev(wt, torch), opts).cpu().numpy()
     assert np.array_equal(np.isnan(got), np.isnan(ref))
@@ -207,6 +207,6 @@ def test_conv_patch_repacked_weights(kx, torch_cuda, tc):
     dev = to_dev(wbuf, torch).reshape(-1)
     wv = kx.TensorView(dev, (256, 24, 3, 3), (24 * 12, 12, 4, 1), 0)
     got = kx.conv2d(to_dev(x, torch), wv, kx.Conv2dOptions(padding=(1, 1))).cpu().numpy().astype(np.float64)
-    assert tc.last_kernel == "conv_tc_3xtf32_patch_256x224", tc.last_kernel
+    assert tc.last_kernel.startswith("conv_tc_3xtf32_patch_256x"), tc.last_kernel
     d2, ab = oracle.conv2d_dot2(oracle.View.of(x), oracle.View.of(wt), padding=(1, 1))
     assert (np.abs(got - d2) <= 2e-6 * ab + 1e-30).all()
