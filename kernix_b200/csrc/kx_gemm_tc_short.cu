@@ -30,7 +30,11 @@ namespace shortk {
 constexpr int BN = 128, NST = 6;
 constexpr int B_TILE = BN * BK * 4;                   // 8 KB
 constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 32 KB
-constexpr int SMEM_BYTES = NST * STAGE_BYTES + BAR_BYTES + 1024;
+// Output staging: per epilogue warp two 32 x 32 f32 boxes (128-byte swizzle)
+// that the TMA stores to C.
+constexpr int OUT_BOX = 32 * 32 * 4;                  // 4 KB
+constexpr int OUT_BYTES = 4 * 2 * OUT_BOX;            // 32 KB
+constexpr int SMEM_BYTES = NST * STAGE_BYTES + OUT_BYTES + BAR_BYTES + 1024;
 constexpr int NT = 448;
 constexpr int EPI_WARP0 = 2, EPI_WARPS = 4;
 constexpr int SPLIT_WARP0 = 6, SPLIT_WARPS = 8, SPLIT_THREADS = SPLIT_WARPS * 32;
@@ -51,6 +55,7 @@ struct Params {
     int a_batched, b_batched;
     int tiles_m, tiles_n;
     int64_t ntiles;       // tiles_m * tiles_n * nbatch
+    int c_tma;            // C is stored through the tensor map (else plain stores)
     uint32_t *status;
 };
 
@@ -66,10 +71,11 @@ __device__ __forceinline__ void tile_coords(const Params &p, int64_t t, int &m0,
 template <bool B_MN>
 __global__ void __launch_bounds__(NT, 1)
 gemm_3xtf32_short_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                         const __grid_constant__ Params p) {
+                         const __grid_constant__ CUtensorMap tmC, const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + NST * STAGE_BYTES);
+    uint8_t *out_stage = smem + NST * STAGE_BYTES;   // [epilogue warp][2] boxes of OUT_BOX bytes
+    uint64_t *full = reinterpret_cast<uint64_t *>(out_stage + OUT_BYTES);
     uint64_t *conv = full + NST;
     uint64_t *empty = conv + NST;
     uint64_t *tmem_full = empty + NST;      // [2]
@@ -242,6 +248,7 @@ gemm_3xtf32_short_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
     } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + EPI_WARPS) {
         // ---- epilogue warps ----------------------------------------------
         const int quarter = warp & 3;
+        uint32_t sc = 0;    // staging boxes filled by this warp (buffer sc % 2)
         for (int64_t i = 0; i < my_tiles && !s_fail; ++i) {
             const int b = (int)(i & 1);
             if (!mbar_wait(&tmem_full[b], (uint32_t)((i >> 1) & 1)) ||
@@ -259,7 +266,48 @@ gemm_3xtf32_short_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
             const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 256);
             float *crow = p.C + (int64_t)batch * p.c_bs + (int64_t)(in_rows ? row : 0) * p.c_rs + n0;
             const bool vec = (p.c_rs % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) && (p.c_bs % 4 == 0);
-            if (!nonfinite) {
+            if (!nonfinite && p.c_tma) {
+                // 32-column boxes: this lane's row into the swizzled staging
+                // box (16-byte chunk j of row r at chunk j ^ (r % 8): each
+                // quarter-warp store covers 32 distinct banks), then one TMA
+                // store per box, clipped at the matrix edges.
+                const uint32_t sbase = smem_u32(out_stage) + (uint32_t)((warp - EPI_WARP0) * 2 * OUT_BOX);
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t r0[16], r1[16], x0[16], x1[16];
+                    tmem_ld16(lane_base + (uint32_t)(c * 32), r0);
+                    tmem_ld16(lane_base + (uint32_t)(c * 32 + 16), r1);
+                    tmem_ld16(lane_base + 128u + (uint32_t)(c * 32), x0);
+                    tmem_ld16(lane_base + 128u + (uint32_t)(c * 32 + 16), x1);
+                    tmem_wait_ld();
+                    const uint32_t box = sbase + (uint32_t)((sc & 1) * OUT_BOX);
+                    if (lane == 0) bulk_wait_read<1>();     // the store that last read this box is done
+                    __syncwarp();
+                    const uint32_t row = box + (uint32_t)lane * 128;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        sts_v4_f32(row + (uint32_t)((j ^ (lane & 7)) << 4),
+                                   __uint_as_float(r0[4 * j]) + __uint_as_float(x0[4 * j]),
+                                   __uint_as_float(r0[4 * j + 1]) + __uint_as_float(x0[4 * j + 1]),
+                                   __uint_as_float(r0[4 * j + 2]) + __uint_as_float(x0[4 * j + 2]),
+                                   __uint_as_float(r0[4 * j + 3]) + __uint_as_float(x0[4 * j + 3]));
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        sts_v4_f32(row + (uint32_t)(((j + 4) ^ (lane & 7)) << 4),
+                                   __uint_as_float(r1[4 * j]) + __uint_as_float(x1[4 * j]),
+                                   __uint_as_float(r1[4 * j + 1]) + __uint_as_float(x1[4 * j + 1]),
+                                   __uint_as_float(r1[4 * j + 2]) + __uint_as_float(x1[4 * j + 2]),
+                                   __uint_as_float(r1[4 * j + 3]) + __uint_as_float(x1[4 * j + 3]));
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_3d(&tmC, out_stage + (box - smem_u32(out_stage)), n0 + c * 32, m0 + quarter * 32,
+                                     batch);
+                        bulk_commit();
+                    }
+                    ++sc;
+                }
+            } else if (!nonfinite) {
 #pragma unroll 1
                 for (int c = 0; c < BN / 16; ++c) {
                     uint32_t r0[16], r1[16];
@@ -299,6 +347,7 @@ gemm_3xtf32_short_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
                 }
             }
         }
+        if (lane == 0) bulk_wait_all();   // every TMA store of C has completed
     }
     tc_fence_before();
     __syncthreads();
@@ -365,13 +414,22 @@ int run_gemm_tc_short(Handle *h, const GemmParams<float> &p, const char **kernel
     pp.tiles_n = (p.N + BN - 1) / BN;
     pp.ntiles = (int64_t)pp.tiles_m * pp.tiles_n * nb;
     pp.status = h->flags + kStatusWord;
+    // C through a tensor map (dims N, M, batch): 16-byte aligned base and strides
+    CUtensorMap mc;
+    std::memset(&mc, 0, sizeof(mc));
+    const bool c_batched = nb > 1;
+    pp.c_tma = p.M > 1 && p.c_rs > 0 && (p.c_rs * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0 &&
+               (!c_batched || (c_bs > 0 && (c_bs * 4) % 16 == 0)) &&
+               make_map(&mc, p.C, (uint64_t)p.N, (uint64_t)p.M, (uint64_t)nb, (uint64_t)p.c_rs * 4,
+                        c_batched ? (uint64_t)c_bs * 4 : (uint64_t)((p.c_rs * 4 * (int64_t)p.M + 15) / 16 * 16), 32, 32,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
     const int64_t grid = pp.ntiles < h->sm_count ? pp.ntiles : h->sm_count;
     cudaError_t ce;
     if (b_mn) {
         auto k = gemm_3xtf32_short_kernel<true>;
         ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (ce == cudaSuccess) {
-            k<<<(unsigned)grid, NT, SMEM_BYTES, h->stream>>>(ma, mb, pp);
+            k<<<(unsigned)grid, NT, SMEM_BYTES, h->stream>>>(ma, mb, mc, pp);
             ce = cudaGetLastError();
         }
         *kernel_name = "tc_3xtf32_short_128x128_bmn";
@@ -379,7 +437,7 @@ int run_gemm_tc_short(Handle *h, const GemmParams<float> &p, const char **kernel
         auto k = gemm_3xtf32_short_kernel<false>;
         ce = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (ce == cudaSuccess) {
-            k<<<(unsigned)grid, NT, SMEM_BYTES, h->stream>>>(ma, mb, pp);
+            k<<<(unsigned)grid, NT, SMEM_BYTES, h->stream>>>(ma, mb, mc, pp);
             ce = cudaGetLastError();
         }
         *kernel_name = "tc_3xtf32_short_128x128_bk";

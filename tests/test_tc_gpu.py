@@ -187,6 +187,44 @@ def test_tc_pair_batched_and_nonfinite(kx, torch_cuda, pair_handle):
     pair_handle.synchronize()
 
 
+def test_tc_short_k_output_paths(kx, torch_cuda):
+    """The short-K kernel stores C through a tensor map in 32 x 32 boxes
+    (clipped at ragged edges, batched scores) and with plain stores for
+    single-row products; every output element is checked against f64 with
+    the f32 bound."""
+    torch = torch_cuda
+    h = kx.handle(0)
+    h.set_f32_variant(0)
+    rng = np.random.default_rng(23)
+    a = rng.uniform(-1, 1, (4100, 300)).astype(np.float32)
+    b = rng.uniform(-1, 1, (300, 2052)).astype(np.float32)
+    da, db = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    c = torch.empty(4100, 2052, device="cuda")
+    kx.matmul_into(da, db, c)
+    assert h.last_kernel == "tc_3xtf32_short_128x128_bmn", h.last_kernel
+    got = c.cpu().numpy().astype(np.float64)
+    exact = a.astype(np.float64) @ b.astype(np.float64)
+    bound = 2e-6 * (np.abs(a).astype(np.float64) @ np.abs(b).astype(np.float64)) + 1e-30
+    assert (np.abs(got - exact) <= bound).all()
+    # single-row products (600 batches of 1 x 128 x 128): no row stride for a
+    # tensor map -> plain stores
+    a1 = rng.uniform(-1, 1, (600, 1, 128)).astype(np.float32)
+    b1 = rng.uniform(-1, 1, (600, 128, 128)).astype(np.float32)
+    c1 = kx.matmul(torch.from_numpy(a1).cuda(), torch.from_numpy(b1).cuda()).cpu().numpy().astype(np.float64)
+    assert h.last_kernel == "tc_3xtf32_short_128x128_bmn", h.last_kernel
+    a64, b64 = a1.astype(np.float64), b1.astype(np.float64)
+    assert (np.abs(c1 - a64 @ b64) <= 2e-6 * (np.abs(a64) @ np.abs(b64)) + 1e-30).all()
+    q = rng.standard_normal((4, 8, 512, 128)).astype(np.float32)     # 512 tiles
+    k = rng.standard_normal((4, 8, 512, 128)).astype(np.float32)
+    s = kx.matmul(torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda().transpose(2, 3)).cpu().numpy()
+    assert h.last_kernel == "tc_3xtf32_short_128x128_bk", h.last_kernel
+    q64, k64 = q.astype(np.float64), k.astype(np.float64)
+    exact = np.einsum("bhik,bhjk->bhij", q64, k64)
+    bound = 2e-6 * np.einsum("bhik,bhjk->bhij", np.abs(q64), np.abs(k64)) + 1e-30
+    assert (np.abs(s - exact) <= bound).all()
+    h.synchronize()
+
+
 def test_tc_short_k_persistent(kx, torch_cuda):
     """K <= 1024 over many tiles: the persistent kernel (TMEM double-buffered,
     epilogue overlapping the next tile) -- attention scores Q K^T with a
