@@ -194,23 +194,8 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             // (A hi: 512 at offset 0, B hi: BN * 4 at 16 KB); the 256 worker
             // threads split them, lo going to the buffer beside its hi.
             uint32_t bad = 0;
-            uint8_t *base = stage_a(s);
-#pragma unroll
-            for (int j = 0; j < TN::CONV_ITERS; ++j) {
-                const int c = wt + j * WORK_THREADS;
-                if (TN::CONV_CHUNKS % WORK_THREADS != 0 && c >= TN::CONV_CHUNKS) break;
-                const bool in_a = c < A_TILE / 16;
-                float4 *hp = reinterpret_cast<float4 *>(base + (in_a ? c * 16 : 2 * A_TILE + (c - A_TILE / 16) * 16));
-                float4 *lp = reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(hp) + (in_a ? A_TILE : B_TILE));
-                const float4 v = *hp;   // stays in place: the MMA reads it as hi
-                float4 l;
-                l.x = v.x - tf32_trunc(v.x);
-                l.y = v.y - tf32_trunc(v.y);
-                l.z = v.z - tf32_trunc(v.z);
-                l.w = v.w - tf32_trunc(v.w);
-                bad |= nonfinite_bits(v.x) | nonfinite_bits(v.y) | nonfinite_bits(v.z) | nonfinite_bits(v.w);
-                *lp = l;
-            }
+            bad |= split_stage<TN::CONV_ITERS, WORK_THREADS>(smem_u32(stage_a(s)), wt, TN::CONV_CHUNKS, A_TILE / 16,
+                                                            2 * A_TILE, A_TILE, TN::B_TILE);
             if (bad) s_nonfinite = 1;   // inf/NaN input: FMA fallback for this tile
             fence_proxy_async();        // generic-proxy writes -> visible to the tensor core
             __syncwarp();

@@ -223,22 +223,8 @@ gemm_3xtf32_short_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
                     s_fail = 1;
                     break;
                 }
-                uint8_t *base = stage_a(s);
-#pragma unroll
-                for (int j = 0; j < CHUNKS / SPLIT_THREADS; ++j) {
-                    const int c = wt + j * SPLIT_THREADS;
-                    const bool in_a = c < A_TILE / 16;
-                    float4 *hp = reinterpret_cast<float4 *>(base + (in_a ? c * 16 : 2 * A_TILE + (c - A_TILE / 16) * 16));
-                    float4 *lp = reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(hp) + (in_a ? A_TILE : B_TILE));
-                    const float4 v = *hp;
-                    float4 l;
-                    l.x = v.x - tf32_trunc(v.x);
-                    l.y = v.y - tf32_trunc(v.y);
-                    l.z = v.z - tf32_trunc(v.z);
-                    l.w = v.w - tf32_trunc(v.w);
-                    bad |= nonfinite_bits(v.x) | nonfinite_bits(v.y) | nonfinite_bits(v.z) | nonfinite_bits(v.w);
-                    *lp = l;
-                }
+                bad |= split_stage<CHUNKS / SPLIT_THREADS, SPLIT_THREADS>(smem_u32(stage_a(s)), wt, CHUNKS, A_TILE / 16,
+                                                                     2 * A_TILE, A_TILE, B_TILE);
                 if (bad) atomicMax(&s_nonfinite[i & 15], (uint32_t)(i + 1));   // before this k-tile's arrive
                 fence_proxy_async();
                 __syncwarp();

@@ -105,6 +105,12 @@ __device__ __forceinline__ int4 lds_v4_s32(uint32_t a) {
 __device__ __forceinline__ void sts_v4_f32(uint32_t a, float x, float y, float z, float w) {
     asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(x), "f"(y), "f"(z), "f"(w) : "memory");
 }
+__device__ __forceinline__ float4 lds_v4_f32(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a)
+                 : "memory");
+    return v;
+}
 // TMA tensor store of a shared-memory box (bulk-group completion).
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *src, int c0, int c1, int c2) {
     asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
@@ -189,6 +195,36 @@ __device__ __forceinline__ void mc_st1(float *addr, float v) {
 // Exponent of all ones: an inf or NaN input.
 __device__ __forceinline__ uint32_t nonfinite_bits(float x) {
     return (__float_as_uint(x) & 0x7F800000u) == 0x7F800000u ? 1u : 0u;
+}
+
+// Split one stage's raw TMA tiles in place: each of this thread's 16-byte
+// chunks c = wt, wt + NT, ... below `chunks` (A's first `a_chunks`, B's from
+// byte `b_off`) gets its lo part x - tf32(x) `a_lo` (A) or `b_lo` (B) bytes
+// further; the raw chunk stays as hi.  All loads are issued before the
+// stores, with explicit shared-memory instructions.  Returns the nonfinite
+// bits of the chunks read.
+template <int ITERS, int NT>
+__device__ __forceinline__ uint32_t split_stage(uint32_t base, int wt, int chunks, int a_chunks, uint32_t b_off,
+                                                uint32_t a_lo, uint32_t b_lo) {
+    float4 v[ITERS];
+    uint32_t at[ITERS];
+#pragma unroll
+    for (int j = 0; j < ITERS; ++j) {
+        const int c = wt + j * NT;
+        at[j] = c < a_chunks ? base + (uint32_t)c * 16 : base + b_off + (uint32_t)(c - a_chunks) * 16;
+        if (c < chunks) v[j] = lds_v4_f32(at[j]);
+    }
+    uint32_t bad = 0;
+#pragma unroll
+    for (int j = 0; j < ITERS; ++j) {
+        const int c = wt + j * NT;
+        if (c < chunks) {
+            bad |= nonfinite_bits(v[j].x) | nonfinite_bits(v[j].y) | nonfinite_bits(v[j].z) | nonfinite_bits(v[j].w);
+            sts_v4_f32(at[j] + (c < a_chunks ? a_lo : b_lo), v[j].x - tf32_trunc(v[j].x), v[j].y - tf32_trunc(v[j].y),
+                       v[j].z - tf32_trunc(v[j].z), v[j].w - tf32_trunc(v[j].w));
+        }
+    }
+    return bad;
 }
 
 // 16 consecutive f32 columns of this thread's TMEM lane.
