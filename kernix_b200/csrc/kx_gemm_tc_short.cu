@@ -13,7 +13,8 @@
 // Roles (448 threads):
 //   warp 0      TMA producer: A and B tiles of every k-tile of every tile
 //   warp 1      TMEM owner (512 columns) and MMA issuer
-//   warps 2..5  epilogue: one TMEM lane quarter each (warp % 4), 128 columns
+//   warps 2..5  epilogue: one TMEM lane quarter each (warp % 4), 128 columns,
+//               written as 32 x 32 boxes through shared memory and TMA stores
 //   warps 6..13 split: lo beside each raw tile (the raw tile is hi)
 // TMEM: buffer b in {0, 1} holds hi*hi at columns [256 b, 256 b + 128) and the
 // cross terms at [256 b + 128, 256 b + 256).  Same arithmetic, nonfinite
