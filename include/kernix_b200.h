@@ -15,6 +15,7 @@
  *   - Device<T> upload/download/sync    crates/kernix-core/src/device.rs:22-35
  *   - neural::conv2d / ConvGeometry     crates/kernix-ops/src/neural.rs:22-133,177-183
  *   - softmax_temperature               crates/kernix-ops/src/ops/math_extra.rs:394-401,425-500,544-557
+ *   - softmax                           crates/kernix-ops/src/ops/math.rs:398-465,531-536
  *   - CpuExecutor::matmul_into          crates/kernix-ops/src/execution.rs:149-240
  *   - the C bridge convention           crates/kernix-ops/src/accelerate.c:15-30
  *     (int status, caller-owned buffers, row-major output)
@@ -202,6 +203,12 @@ int kx_softmax_temperature_f32(kx_handle *h, const kx_tensor *src, int64_t axis,
                                const kx_tensor *out, kx_error *err);
 int kx_softmax_temperature_f64(kx_handle *h, const kx_tensor *src, int64_t axis, double temperature,
                                const kx_tensor *out, kx_error *err);
+/* softmax(src, axis) (ops/math.rs:398-465,531-536): exp(x - max) / sum along
+ * `axis` into a C-contiguous `out` of the same dims.  Axis errors come first;
+ * nonfinite input returns KX_E_NONFINITE (operation "softmax") with the
+ * C-order indices of the first nonfinite element in the reference scan order. */
+int kx_softmax_f32(kx_handle *h, const kx_tensor *src, int64_t axis, const kx_tensor *out, kx_error *err);
+int kx_softmax_f64(kx_handle *h, const kx_tensor *src, int64_t axis, const kx_tensor *out, kx_error *err);
 
 /* ---- host-buffer hooks (MatmulElement) ---------------------------------- */
 /* try_dense_matmul: C-order a[m*k], b[k*n] -> out[m*n] in HOST memory.

@@ -5,6 +5,7 @@ The public names follow the reference crate (kernix-ops):
 * ``matmul(a, b)``                 ops/linalg.rs:31-44  (NumPy matmul semantics)
 * ``conv2d(x, w, Conv2dOptions())`` neural.rs:177-183
 * ``softmax_temperature(s, axis, t)`` ops/math_extra.rs:544-557
+* ``softmax(s, axis)``             ops/math.rs:531-536
 * ``MatrixInput`` / ``try_dense_matmul`` / ``try_strided_matmul``
                                    ops/matmul_element.rs:14-44, 262-300
 * ``CudaExecutor``                 the ``MatmulDevice`` / ``Device`` plug point
@@ -35,7 +36,7 @@ MAX_RANK = _abi.MAX_RANK
 
 __all__ = [
     "matmul", "matmul_reference", "matmul_shape", "matmul_into", "conv2d", "conv2d_reference", "conv2d_shape",
-    "Conv2dOptions", "softmax_temperature", "matmul_into_replicated", "conv2d_into", "softmax_temperature_into",
+    "Conv2dOptions", "softmax", "softmax_into", "softmax_temperature", "matmul_into_replicated", "conv2d_into", "softmax_temperature_into",
     "MatrixInput", "try_dense_matmul", "try_strided_matmul", "TensorView", "CudaExecutor", "Handle",
     "handle", "OpsError", "InvalidRank", "ContractDimensionMismatch", "BroadcastIncompatible",
     "ElementCountOverflow", "DimensionOverflow", "LayoutError", "InvalidParameter", "ExactRank",
@@ -358,6 +359,23 @@ def softmax_temperature_into(src, axis: int, temperature: float, out) -> None:
     err = KxError()
     ds, do = _descriptor(src), _descriptor(out)
     raise_for(fn(h.ptr, C.byref(ds), int(axis), float(temperature), C.byref(do), C.byref(err)), err)
+
+
+def softmax(src, axis: int):
+    """Softmax of ``x - max`` along ``axis`` (ops/math.rs:531-536); nonfinite
+    input raises NonFiniteInput with operation ``"softmax"``."""
+    out = _empty(tuple(src.shape), src.dtype, src.device)
+    softmax_into(src, axis, out)
+    return out
+
+
+def softmax_into(src, axis: int, out) -> None:
+    """``softmax`` written into an existing C-contiguous tensor."""
+    fn = _fn("kx_softmax", src.dtype)
+    h = _bind(src)
+    err = KxError()
+    ds, do = _descriptor(src), _descriptor(out)
+    raise_for(fn(h.ptr, C.byref(ds), int(axis), C.byref(do), C.byref(err)), err)
 
 
 # ---------------------------------------------------------------------------

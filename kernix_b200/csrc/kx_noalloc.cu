@@ -20,7 +20,8 @@
 //     contents; calls whose kernels overlap on the GPU (different streams, or
 //     different host threads) race on it -- serialise them on one stream;
 //   * nothing in the array has to start at zero: each split writes its full
-//     M x N partial before the reduction reads it.
+//     M x N partial before the reduction reads it, and a product with one
+//     split (K under 128) stores C directly without reading the array.
 // Set-up: the first call on a device, with that device current, resolves the
 // array's device address once (cudaGetSymbolAddress, which also loads the
 // module on that device); make that first call before any stream capture.
@@ -157,17 +158,19 @@ extern "C" int kx_matmul_splitk_f32_static(const kx_tensor *a, const kx_tensor *
     p.K = (int)k;
     p.nbatch = 1;
     // Splits: enough CTAs for a full machine (~2 per SM on 148 SMs), at least
-    // four k-tiles per split, and splits * M * N within the array.
+    // four k-tiles per split, and splits * M * N within the array.  A short K
+    // (under 128) ends with one split: the GEMM kernel then stores C itself
+    // and neither the array nor the reduction is used.
     const int64_t tiles = (int64_t)((m + 63) / 64) * ((n + 63) / 64);
     int64_t splits = (296 + tiles - 1) / tiles;
     const int64_t by_k = (int64_t)k / (4 * StaticCfg::BK);
     if (splits > by_k) splits = by_k;
     const int64_t by_cap = (int64_t)(cap / (m * n));
     if (splits > by_cap) splits = by_cap;
-    if (splits < 2) splits = 2;     // the partials always go through the array
+    if (splits < 1) splits = 1;
     int64_t kps = ((int64_t)k + splits - 1) / splits;
     kps = (kps + StaticCfg::BK - 1) / StaticCfg::BK * StaticCfg::BK;
-    splits = ((int64_t)k + kps - 1) / kps;
+    splits = ((int64_t)k + kps - 1) / kps;   // rounding kps up can only lower it
     if (splits < 1) splits = 1;
     p.splits = (int)splits;
     p.k_per_split = (int)kps;
@@ -181,7 +184,7 @@ extern "C" int kx_matmul_splitk_f32_static(const kx_tensor *a, const kx_tensor *
         case kx::kGatherMN: ce = launch_b<kx::kGatherMN>(p, bm, s); break;
         default: ce = launch_b<kx::kGatherK>(p, bm, s); break;
     }
-    if (ce == cudaSuccess) {
+    if (ce == cudaSuccess && p.splits > 1) {
         const int64_t total = (int64_t)m * n;
         int64_t blocks = (total + 255) / 256;
         if (blocks > 1184) blocks = 1184;

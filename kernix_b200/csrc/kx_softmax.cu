@@ -428,14 +428,19 @@ bool collapse_rows(const int64_t *dims, const int64_t *str, int n, int64_t *rs) 
     return true;
 }
 
+// `plain` selects softmax (math.rs:398-465,531-536): exp(x - max) / sum with
+// no temperature and "softmax" as the operation of its errors.  Running it as
+// temperature 1 gives the same values: (x - max) / 1 and the reciprocal path's
+// x * 1 are exact, and the divide-first fallback x/1 - max/1 is x - max again.
 template <typename T>
 int softmax_impl(kx_handle *hh, const kx_tensor *src, int64_t axis, T temperature, const kx_tensor *out,
-                 kx_error *err) {
-    static const char *kOp = "softmax_temperature";
+                 kx_error *err, bool plain = false) {
+    const char *kOp = plain ? "softmax" : "softmax_temperature";
     if (!hh) return set_err(err, KX_E_PARAM, kOp, "null handle");
     Handle *h = &hh->impl;
-    // normalized_exp_advanced: temperature first, then axis, then shape.
-    if (!std::isfinite((double)temperature) || !(temperature > T(0)))
+    // normalized_exp_advanced: temperature first, then axis, then shape;
+    // normalized_exp (plain): axis, then shape.
+    if (!plain && (!std::isfinite((double)temperature) || !(temperature > T(0))))
         return set_err(err, KX_E_PARAM, kOp, "temperature (must be finite and > 0)");
     Span ss, so;
     int rc = validate_tensor(src, sizeof(T), &ss, err);
@@ -580,5 +585,11 @@ int kx_softmax_temperature_f32(kx_handle *h, const kx_tensor *src, int64_t axis,
 int kx_softmax_temperature_f64(kx_handle *h, const kx_tensor *src, int64_t axis, double temperature,
                                const kx_tensor *out, kx_error *err) {
     return softmax_impl<double>(h, src, axis, temperature, out, err);
+}
+int kx_softmax_f32(kx_handle *h, const kx_tensor *src, int64_t axis, const kx_tensor *out, kx_error *err) {
+    return softmax_impl<float>(h, src, axis, 1.0f, out, err, true);
+}
+int kx_softmax_f64(kx_handle *h, const kx_tensor *src, int64_t axis, const kx_tensor *out, kx_error *err) {
+    return softmax_impl<double>(h, src, axis, 1.0, out, err, true);
 }
 }

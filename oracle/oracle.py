@@ -294,10 +294,22 @@ def conv2d_dot2(x: View, w: View, stride=(1, 1), padding=(0, 0), dilation=(1, 1)
 # ---------------------------------------------------------------------------
 # softmax_temperature
 # ---------------------------------------------------------------------------
+def softmax(x: np.ndarray, axis: int) -> np.ndarray:
+    """normalized_exp, not logarithmic (math.rs:398-465): axis check, finite
+    scan, max, sequential sum of exp(x - max), exp(x - max) / sum.  The values
+    are those of temperature 1 ((x - max) / 1 is exact, and the divide-first
+    branch gives x - max again), so the same row routine computes them."""
+    return _softmax_rows(x, axis, 1.0, "softmax")
+
+
 def softmax_temperature(x: np.ndarray, axis: int, temperature: float) -> np.ndarray:
     """normalized_exp_advanced without mask (math_extra.rs:425-500)."""
     if not np.isfinite(temperature) or not temperature > 0:
         raise OracleError("InvalidParameter", parameter="temperature (must be finite and > 0)")
+    return _softmax_rows(x, axis, temperature, "softmax_temperature")
+
+
+def _softmax_rows(x: np.ndarray, axis: int, temperature: float, operation: str) -> np.ndarray:
     rank = x.ndim
     ax = axis + rank if axis < 0 else axis
     if not 0 <= ax < rank:
@@ -314,5 +326,5 @@ def softmax_temperature(x: np.ndarray, axis: int, temperature: float) -> np.ndar
         r, pos = divmod(int(bad), length)
         outer = list(np.unravel_index(r, moved.shape[:-1])) if moved.ndim > 1 else []
         idx = outer[:ax] + [pos] + outer[ax:]
-        raise OracleError("NonFiniteInput", indices=[int(i) for i in idx])
+        raise OracleError("NonFiniteInput", operation=operation, indices=[int(i) for i in idx])
     return np.moveaxis(out, -1, ax)

@@ -242,3 +242,55 @@ def test_status_words_do_not_alias(kx, torch_cuda):
     w[0, 0, 0, 0] = float("nan")
     kx.conv2d(torch_cuda.ones(1, 1, 5, 5, device="cuda"), w, kx.Conv2dOptions(padding=(1, 1)))
     h.synchronize()
+
+
+# ---------------------------------------------------------------------------
+# plain softmax (ops/math.rs:398-465, 531-536)
+# ---------------------------------------------------------------------------
+def test_plain_softmax_known_answers(kx, torch_cuda):
+    """ops_expansion_tests.rs:373-418: large logits along both axes, F-order
+    views, the nonfinite error with operation "softmax", empty and scalar."""
+    x = to_dev(np.array([[1000.0, 1001.0, 1002.0], [-1000.0, -1000.0, -1000.0]]), torch_cuda)
+    y = kx.softmax(x, -1).cpu().numpy().reshape(-1)
+    for got, want, tol in zip(y, [0.09003057317, 0.24472847105, 0.66524095577, 1 / 3, 1 / 3, 1 / 3],
+                              [1e-9, 1e-9, 1e-9, 1e-12, 1e-12, 1e-12]):
+        assert abs(got - want) < tol
+    f = to_dev(np.array([[0.0, 1.0, 2.0], [3.0, 4.0, 5.0]], dtype=np.float32), torch_cuda)
+    fview = kx.TensorView(f.reshape(-1), (2, 3), (1, 2))       # Order::F storage [0,3,1,4,2,5]
+    y = kx.softmax(fview, 0).cpu().numpy()
+    assert (np.abs(y.sum(axis=0) - 1) < 1e-6).all() and (y[0] < y[1]).all()
+    with pytest.raises(kx.NonFiniteInput) as ge:
+        kx.softmax(to_dev(np.array([1.0, np.nan]), torch_cuda), 0)
+    assert ge.value.indices == [1] and ge.value.operation == "softmax"
+    assert tuple(kx.softmax(torch_cuda.zeros(0, 4, device="cuda", dtype=torch_cuda.float64), 1).shape) == (0, 4)
+    with pytest.raises(kx.AxisOutOfBounds):
+        kx.softmax(torch_cuda.zeros((), device="cuda", dtype=torch_cuda.float64), 0)
+
+
+@pytest.mark.parametrize("shape,axis", [((7, 11), -1), ((4, 2048), -1), ((3, 5000), 1), ((6, 33), 0)])
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_plain_softmax_matches_oracle(kx, torch_cuda, shape, axis, dtype):
+    from kernix_b200 import rng
+    x = rng.normal(23, int(np.prod(shape)), 3.0, dtype).reshape(shape)
+    exp = oracle.softmax(x, axis)
+    got = kx.softmax(to_dev(x, torch_cuda), axis).cpu().numpy()
+    truth = softmax_truth(x, axis, 1.0)
+    assert (np.abs(got - truth) <= softmax_tol_cond(x, axis, 1.0) * np.abs(truth) + np.finfo(dtype).tiny).all()
+    seq = (8 + shape[axis]) * np.finfo(dtype).eps
+    assert (np.abs(exp - truth) <= seq * np.abs(truth) + np.finfo(dtype).tiny).all()
+    # the same values as softmax_temperature at temperature 1 (execution_tests.rs:33-49 pins
+    # the fast and indexed paths to each other; here the plain and tempered entries)
+    same = kx.softmax_temperature(to_dev(x, torch_cuda), axis, 1.0).cpu().numpy()
+    assert np.array_equal(got, same)
+
+
+def test_plain_softmax_first_nonfinite_matches_oracle(kx, torch_cuda):
+    x = np.zeros((7, 11), dtype=np.float64)
+    x[3, 7] = np.nan
+    x[5, 1] = np.inf
+    with pytest.raises(oracle.OracleError) as oe:
+        oracle.softmax(x, -1)
+    with pytest.raises(kx.NonFiniteInput) as ge:
+        kx.softmax(to_dev(x, torch_cuda), -1)
+    assert ge.value.indices == oe.value.fields["indices"] == [3, 7]
+    assert ge.value.operation == oe.value.fields["operation"] == "softmax"

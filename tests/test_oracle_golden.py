@@ -156,6 +156,23 @@ def test_softmax_known_answers():
             oracle.softmax_temperature(x, 1, t)
 
 
+def test_plain_softmax_known_answers():
+    """ops_expansion_tests.rs:373-386 and :405-418 (values quoted there)."""
+    x = np.array([[1000.0, 1001.0, 1002.0], [-1000.0, -1000.0, -1000.0]])
+    y = oracle.softmax(x, -1).reshape(-1)
+    for got, want, tol in zip(y, [0.09003057317, 0.24472847105, 0.66524095577, 1 / 3],
+                              [1e-9, 1e-9, 1e-9, 1e-12]):
+        assert abs(got - want) < tol
+    with pytest.raises(oracle.OracleError) as e:
+        oracle.softmax(np.array([1.0, np.nan]), 0)
+    assert e.value.kind == "NonFiniteInput"
+    assert e.value.fields == {"operation": "softmax", "indices": [1]}
+    assert oracle.softmax(np.zeros((0, 4)), 1).shape == (0, 4)
+    with pytest.raises(oracle.OracleError) as e:
+        oracle.softmax(np.zeros(()), 0)
+    assert e.value.kind == "AxisOutOfBounds"
+
+
 def test_softmax_first_nonfinite_in_scan_order():
     x = np.zeros((3, 4, 5))
     x[2, 1, 3] = np.inf
