@@ -28,8 +28,8 @@ LIB = HERE / "libkx_oracle.so"
 
 
 def build() -> Path:
-    src = HERE / "kx_oracle.c"
-    if not LIB.exists() or LIB.stat().st_mtime < src.stat().st_mtime:
+    srcs = [HERE / "kx_oracle.c", HERE / "kx_engine.c", HERE / "Makefile"]
+    if not LIB.exists() or any(LIB.stat().st_mtime < s.stat().st_mtime for s in srcs):
         subprocess.run(["make", "-C", str(HERE), "-s"], check=True)
     return LIB
 
@@ -52,6 +52,8 @@ def _load() -> C.CDLL:
         getattr(lib, f"kxo_conv2d_dot2_{t}").argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, C.c_int]
         getattr(lib, f"kxo_softmax_rows_{t}").argtypes = [vp, vp, i64, i64, C.c_float if t == "f32" else dbl]
         getattr(lib, f"kxo_softmax_rows_{t}").restype = i64
+        getattr(lib, f"kxo_engine_gemm_{t}").argtypes = [vp, i64, i64, vp, i64, i64, vp, i64, i64, i64, C.c_int]
+        getattr(lib, f"kxo_engine_gemm_{t}").restype = C.c_int
     lib.kxo_openmp_threads.restype = C.c_int
     return lib
 
@@ -218,6 +220,23 @@ def gemm_dot2(a: View, b: View, threads: int | None = None):
     getattr(lib, f"kxo_gemm_dot2_{_t(a.dtype)}")(a.ptr(), a.strides[0], a.strides[1], b.ptr(), b.strides[0],
                                                  b.strides[1], _p(out), _p(absm), m, n, k, threads or THREADS)
     return out, absm
+
+
+def engine_gemm(a: View, b: View, threads: int = 1) -> np.ndarray:
+    """The blocked fp32/f64 engine restatement (kx_engine.c): the BLIS loop
+    nest gemm-f32/f64 0.19.0 and matrixmultiply 0.3.11 implement, serial for
+    threads=1, else row chunks over threads as CpuExecutor::matmul_into
+    (execution.rs:188-233).  Rounding: fp32 (f64) FMA accumulation per k
+    block, blocks added into C -- a CPU result of the kind Kernix returns."""
+    m, k = a.dims
+    k2, n = b.dims
+    assert k == k2
+    out = np.empty((m, n), dtype=a.dtype)
+    rc = getattr(lib, f"kxo_engine_gemm_{_t(a.dtype)}")(a.ptr(), a.strides[0], a.strides[1], b.ptr(), b.strides[0],
+                                                        b.strides[1], _p(out), m, n, k, int(threads))
+    if rc:
+        raise MemoryError("engine packing buffers")
+    return out
 
 
 def gemm_ordered_par(a: View, b: View, threads: int | None = None) -> np.ndarray:
