@@ -210,6 +210,23 @@ int kx_softmax_temperature_f64(kx_handle *h, const kx_tensor *src, int64_t axis,
 int kx_softmax_f32(kx_handle *h, const kx_tensor *src, int64_t axis, const kx_tensor *out, kx_error *err);
 int kx_softmax_f64(kx_handle *h, const kx_tensor *src, int64_t axis, const kx_tensor *out, kx_error *err);
 
+/* Attention products in one call: out = matmul(softmax_temperature(matmul(q,
+ * kt), -1, temperature), v) -- the composition Kernix users write from
+ * matmul (linalg.rs:68-214) and softmax_temperature (math_extra.rs:394-401,
+ * 425-500,544-557), with the same errors in the same order: matmul(q, kt)'s
+ * shape errors, the temperature, matmul(P, v)'s shape errors, then
+ * NonFiniteInput (operation "softmax_temperature") with the indices into the
+ * scores of their first inf/NaN in the reference scan order.  `out` is
+ * C-contiguous with matmul(P, v)'s dims.  When q is [B.., sq, 128], kt the
+ * transposed view [B.., 128, sk] of a row-major k, v [B.., sk, 128] with equal
+ * batch dims (each nesting into one stride) and unit strides along the head
+ * dimension, one fused tcgen05 kernel computes it without materialising the
+ * scores; other layouts, ordered mode, and inputs whose scores hold an inf or
+ * NaN (or whose v does) run the three calls on a scores buffer the handle
+ * allocates.  Synchronises the handle's stream (the nonfinite flag is read). */
+int kx_attention_f32(kx_handle *h, const kx_tensor *q, const kx_tensor *kt, const kx_tensor *v, float temperature,
+                     const kx_tensor *out, kx_error *err);
+
 /* ---- host-buffer hooks (MatmulElement) ---------------------------------- */
 /* try_dense_matmul: C-order a[m*k], b[k*n] -> out[m*n] in HOST memory.
  * Returns KX_DECLINED (nothing written) on any length mismatch, exactly like

@@ -6,6 +6,7 @@ The public names follow the reference crate (kernix-ops):
 * ``conv2d(x, w, Conv2dOptions())`` neural.rs:177-183
 * ``softmax_temperature(s, axis, t)`` ops/math_extra.rs:544-557
 * ``softmax(s, axis)``             ops/math.rs:531-536
+* ``attention(q, kt, v, t)``       matmul + softmax_temperature + matmul in one call
 * ``MatrixInput`` / ``try_dense_matmul`` / ``try_strided_matmul``
                                    ops/matmul_element.rs:14-44, 262-300
 * ``CudaExecutor``                 the ``MatmulDevice`` / ``Device`` plug point
@@ -36,7 +37,7 @@ MAX_RANK = _abi.MAX_RANK
 
 __all__ = [
     "matmul", "matmul_reference", "matmul_shape", "matmul_into", "conv2d", "conv2d_reference", "conv2d_shape",
-    "Conv2dOptions", "softmax", "softmax_into", "softmax_temperature", "matmul_into_replicated", "conv2d_into", "softmax_temperature_into",
+    "Conv2dOptions", "attention", "attention_into", "softmax", "softmax_into", "softmax_temperature", "matmul_into_replicated", "conv2d_into", "softmax_temperature_into",
     "MatrixInput", "try_dense_matmul", "try_strided_matmul", "TensorView", "CudaExecutor", "Handle",
     "handle", "OpsError", "InvalidRank", "ContractDimensionMismatch", "BroadcastIncompatible",
     "ElementCountOverflow", "DimensionOverflow", "LayoutError", "InvalidParameter", "ExactRank",
@@ -359,6 +360,36 @@ def softmax_temperature_into(src, axis: int, temperature: float, out) -> None:
     err = KxError()
     ds, do = _descriptor(src), _descriptor(out)
     raise_for(fn(h.ptr, C.byref(ds), int(axis), float(temperature), C.byref(do), C.byref(err)), err)
+
+
+def attention(q, kt, v, temperature: float):
+    """``matmul(softmax_temperature(matmul(q, kt), -1, temperature), v)`` in one
+    call, with the composition's errors.  ``kt`` is the transposed view of k
+    ([.., d, sk]); with head dim 128, equal batch dims and unit strides along
+    the head dimension one fused tensor-core kernel runs without writing the
+    scores."""
+    import math
+    s_dims = matmul_shape(q.shape, kt.shape)
+    t = float(temperature)
+    if not s_dims or not (math.isfinite(t) and t > 0):
+        # softmax_temperature's own errors come before matmul(P, v)'s: the
+        # library reports them without looking at the output
+        attention_into(q, kt, v, t, _empty((), q.dtype, q.device))
+    out = _empty(matmul_shape(s_dims, v.shape), q.dtype, q.device)
+    attention_into(q, kt, v, t, out)
+    return out
+
+
+def attention_into(q, kt, v, temperature: float, out) -> None:
+    """``attention`` written into an existing C-contiguous f32 tensor."""
+    import torch
+    if q.dtype != torch.float32:
+        raise Unsupported(f"dtype {q.dtype}: attention runs in f32")
+    h = _bind(q)
+    err = KxError()
+    dq, dk, dv, do = _descriptor(q), _descriptor(kt), _descriptor(v), _descriptor(out)
+    raise_for(lib.kx_attention_f32(h.ptr, C.byref(dq), C.byref(dk), C.byref(dv), float(temperature), C.byref(do),
+                                   C.byref(err)), err)
 
 
 def softmax(src, axis: int):

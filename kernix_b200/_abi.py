@@ -117,6 +117,8 @@ _SIGNATURES = {
     "kx_conv2d_f64": (C.c_int, [_vp, _P(KxTensor), _P(KxTensor), _P(KxConv2dOptions), _P(KxTensor), _P(KxError)]),
     "kx_softmax_temperature_f32": (C.c_int, [_vp, _P(KxTensor), C.c_int64, C.c_float, _P(KxTensor), _P(KxError)]),
     "kx_softmax_temperature_f64": (C.c_int, [_vp, _P(KxTensor), C.c_int64, C.c_double, _P(KxTensor), _P(KxError)]),
+    "kx_attention_f32": (C.c_int, [_vp, _P(KxTensor), _P(KxTensor), _P(KxTensor), C.c_float, _P(KxTensor),
+                                   _P(KxError)]),
     "kx_softmax_f32": (C.c_int, [_vp, _P(KxTensor), C.c_int64, _P(KxTensor), _P(KxError)]),
     "kx_softmax_f64": (C.c_int, [_vp, _P(KxTensor), C.c_int64, _P(KxTensor), _P(KxError)]),
     "kx_try_dense_matmul_f32": (C.c_int, [_vp, _vp, _u64, _vp, _u64, _vp, _u64, _u64, _u64, _u64]),

@@ -410,6 +410,7 @@ int kx_destroy(kx_handle *hh) {
         if (h.d2h) cudaStreamSynchronize(h.d2h);
         cudaFree(h.ws);
         for (auto &s : h.stage) cudaFree(s);
+        cudaFree(h.attn);
         cudaFree(h.flags);
         for (auto &e : h.ev)
             if (e) cudaEventDestroy(e);

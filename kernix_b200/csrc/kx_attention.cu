@@ -1,0 +1,755 @@
+// Fused attention products: out = softmax_temperature(q . kt, -1, T) . v in one
+// persistent tcgen05 kernel, without writing the scores or the probabilities.
+//
+// Kernix composes attention from three calls -- matmul (ops/linalg.rs:68-214),
+// softmax_temperature (ops/math_extra.rs:394-401,425-500,544-557) and matmul
+// again -- and materialises S = q kt and P = softmax(S) in full.  On the GPU
+// that costs two round trips of the [.., sq, sk] scores through HBM (8.6 GB
+// each for 16 x 32 heads of 2048 x 2048).  Here each CTA keeps a 128-row block
+// of q on chip and walks the keys in blocks of 64:
+//
+//   S_j  = q . kt_j                 split-TF32 on the tensor cores (TMEM)
+//   m    = max(m, rowmax S_j)       online maximum (Milakov & Gimelshein 2018)
+//   P_j  = exp((S_j - m) / T)       written back into TMEM as the A operand
+//   O_j  = P_j . v_j                split-TF32, A from TMEM, fresh accumulator
+//   O    = O * exp((m_old - m)/T) + O_j    in registers (round-to-nearest)
+//   l    = l * exp((m_old - m)/T) + sum P_j
+// and stores out = O / l once per row block.  The result equals the composed
+// path's up to rounding: exp((x - max)/T) / sum with the final maximum, summed
+// against v (the tests bound the difference against the compensated oracle).
+// Anything the composition would treat specially -- an inf/NaN score (the
+// reference's NonFiniteInput with its first index), an overflowing x - max
+// (its divide-first branch), an inf/NaN in v (IEEE propagation through the
+// product) -- sets a flag; the host then runs the composed path, which
+// reproduces the reference's result or error exactly.
+//
+// Split-TF32: x = hi + lo with hi = tf32(x) (the raw f32 tile, which the tensor
+// core reads truncated) and lo = x - hi; a.b = hi.hi + hi.lo + lo.hi.  The
+// score accumulators keep hi.hi and the cross terms apart (K = head dim <= 128
+// per block); each key block's O_j holds all three products over 64 keys and
+// is folded into f32 registers right away, so the tensor core's truncating
+// accumulation never runs over more than 64 keys.
+//
+// Roles (512 threads, one CTA per SM, persistent over (batch, row block) units):
+//   warp 0       TMA producer: q block, then per key block 4 kt slots and
+//                4 v slots through a ring of 16 KB slots
+//   warp 1       TMEM owner (512 columns) and MMA issuer
+//   warps 2..5   softmax: one row each (TMEM lane), S_j -> P_j, m, l
+//   warps 6..13  fold: rows x 64 columns of O in registers; epilogue stores
+//   warps 14,15  split: lo parts of q, kt and v (v checked for inf/NaN)
+// TMEM: S buffer b (b = key block % 2) at columns [128 b, 128 b + 128): hi.hi
+// scores in the first 64, cross terms in the next 64, overwritten in place by
+// P_hi and P_lo; O buffer b at [256 + 128 b, 256 + 128 b + 128).
+// Every mbarrier wait is bounded (2 s); on expiry the kernel stops its loops,
+// waits for its own TMA copies, frees TMEM and sets the handle's status bit.
+#include <cmath>
+#include <cstring>
+
+#include "tc_common.cuh"
+
+extern "C" int kx_matmul_f32(kx_handle *h, const kx_tensor *a, const kx_tensor *b, const kx_tensor *out,
+                             kx_error *err);
+extern "C" int kx_softmax_temperature_f32(kx_handle *h, const kx_tensor *src, int64_t axis, float temperature,
+                                          const kx_tensor *out, kx_error *err);
+
+namespace kx {
+
+namespace tc {
+namespace attn {
+
+constexpr int BQ = 128;            // query rows per unit
+constexpr int BKEY = 64;           // keys per block
+constexpr int DH = 128;            // head dimension (q, kt rows, v columns)
+constexpr int NSLOT = 5;           // ring slots
+constexpr int SLOT = 16384;        // hi (8 KB) + lo (8 KB)
+constexpr int Q_BYTES = BQ * DH * 4;          // 64 KB (hi); lo follows
+constexpr int RING_OFF = 2 * Q_BYTES;         // 128 KB
+constexpr int MISC_OFF = RING_OFF + NSLOT * SLOT;   // 208 KB
+// misc: mbarriers (256 B), alpha ring [4][128] and l ring [4][128] f32 (4 KB)
+constexpr int MISC_BYTES = 256 + 2 * 4 * BQ * 4;
+constexpr int SMEM_BYTES = MISC_OFF + MISC_BYTES + 1024;
+constexpr int NT = 512;
+constexpr int SOFT_WARP0 = 2, FOLD_WARP0 = 6, SPLIT_WARP0 = 14, SPLIT_WARPS = 2;
+constexpr int SPLIT_THREADS = SPLIT_WARPS * 32;
+static_assert(SMEM_BYTES <= 232448, "shared memory");
+
+struct Params {
+    float *out;
+    int64_t o_rs, o_bs;          // out row and batch strides (elements)
+    int sq, sk, nbatch;
+    int nq;                      // row blocks per batch entry
+    int64_t units;               // nbatch * nq
+    int nkb;                     // key blocks
+    float temperature, recip;    // T and 1/T (recip used when use_recip)
+    int use_recip;
+    uint32_t *status;            // bit 0: a bounded wait expired
+    uint32_t *flag;              // nonzero: run the composed path
+};
+
+// (x - m) / T as the softmax kernel computes it: the reciprocal with one
+// Markstein residual correction ("IA-64 and Elementary Functions", 2000),
+// within an ulp of the IEEE quotient; the IEEE division when 1/T is not a
+// normal number.
+__device__ __forceinline__ float scaled(float diff, const Params &p) {
+    if (p.use_recip) {
+        const float q = diff * p.recip;
+        const float r = fmaf(-p.temperature, q, diff);
+        return fmaf(r, p.recip, q);
+    }
+    return diff / p.temperature;
+}
+
+// 16 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D (TMEM) += A (TMEM, 128 lanes x 8 tf32 columns) x B (shared memory).
+__device__ __forceinline__ void mma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Split one buffer of `chunks` 16-byte chunks in place: lo (x - tf32(x)) at
+// `lo_off` bytes past each raw chunk.  Returns the nonfinite bits seen.
+__device__ __forceinline__ uint32_t split_buf(uint32_t base, int chunks, uint32_t lo_off, int wt) {
+    uint32_t bad = 0;
+#pragma unroll 4
+    for (int c = wt; c < chunks; c += SPLIT_THREADS * 4) {
+        float4 v[4];
+        uint32_t at[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int cc = c + u * SPLIT_THREADS;
+            at[u] = base + (uint32_t)cc * 16;
+            if (cc < chunks) v[u] = lds_v4_f32(at[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int cc = c + u * SPLIT_THREADS;
+            if (cc < chunks) {
+                bad |= nonfinite_bits(v[u].x) | nonfinite_bits(v[u].y) | nonfinite_bits(v[u].z) |
+                       nonfinite_bits(v[u].w);
+                sts_v4_f32(at[u] + lo_off, v[u].x - tf32_trunc(v[u].x), v[u].y - tf32_trunc(v[u].y),
+                           v[u].z - tf32_trunc(v[u].z), v[u].w - tf32_trunc(v[u].w));
+            }
+        }
+    }
+    return bad;
+}
+
+// Slot stream of one unit, in the order the MMA thread consumes it:
+// kt_0, kt_1, v_0, kt_2, v_1, ..., kt_{n-1}, v_{n-2}, v_{n-1}; each kt_j and
+// v_j is 4 slots.  Slot item e (0-based) of a unit -> (is_v, block, part).
+__device__ __forceinline__ void slot_item(int e, int nkb, bool &is_v, int &blk, int &part) {
+    part = e & 3;
+    const int grp = e >> 2;   // 0: kt_0; then pairs (kt_j, v_{j-1}); last: v_{n-1}
+    if (grp == 0) {
+        is_v = false;
+        blk = 0;
+    } else if (grp >= 2 * nkb - 1) {
+        is_v = true;
+        blk = nkb - 1;
+    } else {
+        const int j = (grp + 1) >> 1;
+        is_v = (grp & 1) == 0;
+        blk = is_v ? j - 1 : j;
+    }
+}
+
+__global__ void __launch_bounds__(NT, 1)
+attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *ring = smem + RING_OFF;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + MISC_OFF);
+    uint64_t *slot_full = bars;                 // [NSLOT]
+    uint64_t *slot_conv = slot_full + NSLOT;    // [NSLOT]
+    uint64_t *slot_empty = slot_conv + NSLOT;   // [NSLOT]
+    uint64_t *q_full = slot_empty + NSLOT;
+    uint64_t *q_conv = q_full + 1;
+    uint64_t *q_empty = q_conv + 1;
+    uint64_t *s_full = q_empty + 1;             // [2]
+    uint64_t *p_ready = s_full + 2;             // [2]
+    uint64_t *o_full = p_ready + 2;             // [2]
+    uint64_t *o_empty = o_full + 2;             // [2]
+    uint64_t *a_ready = o_empty + 2;            // [4]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(a_ready + 4);
+    float *alpha_ring = reinterpret_cast<float *>(smem + MISC_OFF + 256);   // [4][BQ]
+    float *l_ring = alpha_ring + 4 * BQ;                                    // [4][BQ]
+    __shared__ int s_fail_storage;
+    volatile int &s_fail = s_fail_storage;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t my_units = p.units > blockIdx.x ? (p.units - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    const int nkb = p.nkb;
+    const int items = 8 * nkb;        // slot items per unit
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NSLOT; ++s) {
+            mbar_init(&slot_full[s], 1);
+            mbar_init(&slot_conv[s], SPLIT_WARPS);
+            mbar_init(&slot_empty[s], 1);
+        }
+        mbar_init(q_full, 1);
+        mbar_init(q_conv, SPLIT_WARPS);
+        mbar_init(q_empty, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&s_full[b], 1);
+            mbar_init(&p_ready[b], 4);
+            mbar_init(&o_full[b], 1);
+            mbar_init(&o_empty[b], 8);
+        }
+        for (int r = 0; r < 4; ++r) mbar_init(&a_ready[r], 4);
+        s_fail = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---- TMA producer ------------------------------------------------
+        if (lane == 0) {
+            int64_t g = 0;        // slot loads issued so far
+            int64_t i = 0;
+            for (; i < my_units && !s_fail; ++i) {
+                const int64_t u = blockIdx.x + i * gridDim.x;
+                const int bh = (int)(u / p.nq), q0 = (int)(u % p.nq) * BQ;
+                if (i > 0 && !mbar_wait(q_empty, (uint32_t)((i - 1) & 1))) {
+                    s_fail = 1;
+                    break;
+                }
+                mbar_expect_tx(q_full, Q_BYTES);
+#pragma unroll 1
+                for (int t = 0; t < DH / 16; ++t) tma_load_3d(smem + t * 8192, &tmQ, t * 16, q0, bh, q_full);
+                for (int e = 0; e < items; ++e, ++g) {
+                    const int s = (int)(g % NSLOT);
+                    if (g >= NSLOT && !mbar_wait(&slot_empty[s], (uint32_t)(((g / NSLOT) - 1) & 1))) {
+                        s_fail = 1;
+                        break;
+                    }
+                    bool is_v;
+                    int blk, part;
+                    slot_item(e, nkb, is_v, blk, part);
+                    uint8_t *dst = ring + s * SLOT;
+                    mbar_expect_tx(&slot_full[s], SLOT / 2);
+                    if (!is_v) {
+                        // kt_j: 64 keys x 32 head columns as two 16-column boxes
+                        tma_load_3d(dst, &tmK, part * 32, blk * BKEY, bh, &slot_full[s]);
+                        tma_load_3d(dst + 4096, &tmK, part * 32 + 16, blk * BKEY, bh, &slot_full[s]);
+                    } else {
+                        // v_j: 16 keys x 128 columns as four 32-column boxes
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
+                            tma_load_3d(dst + c * 2048, &tmV, c * 32, blk * BKEY + part * 16, bh, &slot_full[s]);
+                    }
+                }
+            }
+            // drain: the last copy issued into each slot, and the last q block, have landed
+            for (int s = 0; s < NSLOT && s < g; ++s) {
+                const int64_t last = s + NSLOT * ((g - 1 - s) / NSLOT);
+                mbar_wait(&slot_full[s], (uint32_t)((last / NSLOT) & 1));
+            }
+            if (i > 0) mbar_wait(q_full, (uint32_t)((i - 1) & 1));
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer --------------------------------------------------
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = idesc_tf32<BKEY>(false);
+            constexpr uint32_t idesc_o = idesc_tf32<DH>(true);
+            const uint32_t q_hi = smem_u32(smem), q_lo = q_hi + Q_BYTES;
+            int64_t g = 0;        // slot items consumed
+            int64_t kb = 0;       // key blocks started (global, for the TMEM buffers)
+            for (int64_t i = 0; i < my_units && !s_fail; ++i) {
+                if (!mbar_wait(q_conv, (uint32_t)(i & 1))) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                const int64_t kb0 = kb;
+                // S_j for j = 0..nkb-1, PV_{j-1} after S_j, PV_{nkb-1} last
+                for (int j = 0; j <= nkb && !s_fail; ++j) {
+                    if (j < nkb) {
+                        const int64_t gb = kb0 + j;
+                        const uint32_t sm = tmem + (uint32_t)((gb & 1) * 128), sx = sm + 64;
+                        for (int t = 0; t < 4; ++t, ++g) {
+                            const int s = (int)(g % NSLOT);
+                            if (!mbar_wait(&slot_conv[s], (uint32_t)((g / NSLOT) & 1))) {
+                                s_fail = 1;
+                                break;
+                            }
+                            tc_fence_after();
+                            const uint32_t k_hi = smem_u32(ring + s * SLOT), k_lo = k_hi + SLOT / 2;
+#pragma unroll
+                            for (int sub = 0; sub < 2; ++sub) {
+                                const uint32_t qh = q_hi + (uint32_t)((2 * t + sub) * 8192);
+                                const uint32_t ql = q_lo + (uint32_t)((2 * t + sub) * 8192);
+#pragma unroll
+                                for (int ks = 0; ks < 2; ++ks) {
+                                    const uint64_t dqh = desc_k_sw64(qh + ks * 32), dql = desc_k_sw64(ql + ks * 32);
+                                    const uint64_t dkh = desc_k_sw64(k_hi + sub * 4096 + ks * 32);
+                                    const uint64_t dkl = desc_k_sw64(k_lo + sub * 4096 + ks * 32);
+                                    const uint32_t acc = (t > 0 || sub > 0 || ks > 0) ? 1u : 0u;
+                                    mma_tf32(sm, dqh, dkh, idesc_s, acc);
+                                    mma_tf32(sx, dqh, dkl, idesc_s, acc);
+                                    mma_tf32(sx, dql, dkh, idesc_s, 1u);
+                                }
+                            }
+                            mma_commit(&slot_empty[s]);
+                        }
+                        if (s_fail) break;
+                        mma_commit(&s_full[gb & 1]);
+                        if (j == nkb - 1) mma_commit(q_empty);   // q is read by no later MMA of this unit
+                    }
+                    if (j >= 1) {
+                        const int64_t gb = kb0 + j - 1;
+                        const int b = (int)(gb & 1);
+                        // P_{j-1} written by the softmax warps; O buffer b read by the fold warps
+                        if (!mbar_wait(&p_ready[b], (uint32_t)((gb >> 1) & 1)) ||
+                            (gb >= 2 && !mbar_wait(&o_empty[b], (uint32_t)(((gb >> 1) - 1) & 1)))) {
+                            s_fail = 1;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t ph = tmem + (uint32_t)(b * 128), pl = ph + 64;
+                        const uint32_t od = tmem + 256u + (uint32_t)(b * 128);
+                        for (int t = 0; t < 4; ++t, ++g) {
+                            const int s = (int)(g % NSLOT);
+                            if (!mbar_wait(&slot_conv[s], (uint32_t)((g / NSLOT) & 1))) {
+                                s_fail = 1;
+                                break;
+                            }
+                            tc_fence_after();
+                            const uint32_t v_hi = smem_u32(ring + s * SLOT), v_lo = v_hi + SLOT / 2;
+#pragma unroll
+                            for (int ks = 0; ks < 2; ++ks) {
+                                const uint64_t dvh = desc_mn_sw128(v_hi + ks * 1024, 2048, 512);
+                                const uint64_t dvl = desc_mn_sw128(v_lo + ks * 1024, 2048, 512);
+                                const uint32_t col = (uint32_t)(t * 16 + ks * 8);
+                                const uint32_t acc = (t > 0 || ks > 0) ? 1u : 0u;
+                                mma_tf32_ts(od, ph + col, dvh, idesc_o, acc);
+                                mma_tf32_ts(od, ph + col, dvl, idesc_o, 1u);
+                                mma_tf32_ts(od, pl + col, dvh, idesc_o, 1u);
+                            }
+                            mma_commit(&slot_empty[s]);
+                        }
+                        if (s_fail) break;
+                        mma_commit(&o_full[b]);
+                    }
+                }
+                kb = kb0 + nkb;
+            }
+            if (s_fail) {   // release every role that may wait on the MMA thread
+                for (int b = 0; b < 2; ++b) {
+                    mma_commit(&s_full[b]);
+                    mma_commit(&o_full[b]);
+                }
+            }
+        }
+    } else if (warp >= SOFT_WARP0 && warp < FOLD_WARP0) {
+        // ---- softmax: one row per thread ------------------------------------
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;                       // row in the block
+        const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+        int64_t kb = 0;
+        for (int64_t i = 0; i < my_units && !s_fail; ++i) {
+            float m = -INFINITY, l = 0.0f;
+            uint32_t bad = 0;
+            for (int j = 0; j < nkb && !s_fail; ++j, ++kb) {
+                const int b = (int)(kb & 1);
+                if (!mbar_wait(&s_full[b], (uint32_t)((kb >> 1) & 1))) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                if (s_fail) break;
+                const int valid = p.sk - j * BKEY < BKEY ? p.sk - j * BKEY : BKEY;
+                float sv[64];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t a0[16], a1[16], x0[16], x1[16];
+                    const uint32_t base = lane_base + (uint32_t)(b * 128 + h * 32);
+                    tmem_ld16(base, a0);
+                    tmem_ld16(base + 16, a1);
+                    tmem_ld16(base + 64, x0);
+                    tmem_ld16(base + 80, x1);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) {
+                        sv[h * 32 + c] = __uint_as_float(a0[c]) + __uint_as_float(x0[c]);
+                        sv[h * 32 + 16 + c] = __uint_as_float(a1[c]) + __uint_as_float(x1[c]);
+                    }
+                }
+                float bmax = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < 64; ++c) {
+                    if (c < valid) {
+                        bad |= nonfinite_bits(sv[c]);
+                        bmax = fmaxf(bmax, sv[c]);
+                    }
+                }
+                const float m_new = fmaxf(m, bmax);
+                float alpha = 0.0f;
+                if (m != -INFINITY) {
+                    const float dd = m - m_new;
+                    alpha = expf(scaled(dd, p));
+                }
+                float bsum = 0.0f;
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    uint32_t phv[16], plv[16];
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) {
+                        float pv = 0.0f;
+                        if (h * 16 + c < valid) {
+                            const float diff = sv[h * 16 + c] - m_new;
+                            bad |= nonfinite_bits(diff);
+                            pv = expf(scaled(diff, p));
+                        }
+                        bsum += pv;
+                        const float hi = tf32_trunc(pv);
+                        phv[c] = __float_as_uint(hi);
+                        plv[c] = __float_as_uint(pv - hi);
+                    }
+                    tmem_st16(lane_base + (uint32_t)(b * 128 + h * 16), phv);
+                    tmem_st16(lane_base + (uint32_t)(b * 128 + 64 + h * 16), plv);
+                }
+                l = l * alpha + bsum;
+                m = m_new;
+                tmem_wait_st();
+                tc_fence_before();
+                const int rs = (int)(kb & 3);
+                alpha_ring[rs * BQ + r] = alpha;
+                l_ring[rs * BQ + r] = l;
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&p_ready[b]);
+                    mbar_arrive(&a_ready[rs]);
+                }
+            }
+            if (bad) atomicOr(p.flag, 1u);
+        }
+    } else if (warp >= FOLD_WARP0 && warp < SPLIT_WARP0) {
+        // ---- fold: O = O * alpha + O_j in registers; epilogue -------------
+        const int quarter = warp & 3;
+        const int half = (warp - FOLD_WARP0) >> 2;             // columns [64 half, 64 half + 64)
+        const int r = quarter * 32 + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + 256u + (uint32_t)(half * 64);
+        int64_t kb = 0;
+        for (int64_t i = 0; i < my_units && !s_fail; ++i) {
+            const int64_t u = blockIdx.x + i * gridDim.x;
+            const int bh = (int)(u / p.nq), row = (int)(u % p.nq) * BQ + r;
+            float o[64];
+#pragma unroll
+            for (int c = 0; c < 64; ++c) o[c] = 0.0f;
+            float lfin = 1.0f;
+            for (int j = 0; j < nkb && !s_fail; ++j, ++kb) {
+                const int b = (int)(kb & 1);
+                const int rs = (int)(kb & 3);
+                if (!mbar_wait(&o_full[b], (uint32_t)((kb >> 1) & 1)) ||
+                    !mbar_wait(&a_ready[rs], (uint32_t)((kb >> 2) & 1))) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                if (s_fail) break;
+                const float alpha = alpha_ring[rs * BQ + r];
+                if (j == nkb - 1) lfin = l_ring[rs * BQ + r];
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    uint32_t x[16];
+                    tmem_ld16(lane_base + (uint32_t)(b * 128 + h * 16), x);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) o[h * 16 + c] = fmaf(o[h * 16 + c], alpha, __uint_as_float(x[c]));
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&o_empty[b]);
+            }
+            if (s_fail) break;
+            if (row < p.sq) {
+                float *dst = p.out + (int64_t)bh * p.o_bs + (int64_t)row * p.o_rs + half * 64;
+#pragma unroll
+                for (int c = 0; c < 64; c += 4)
+                    *reinterpret_cast<float4 *>(dst + c) =
+                        make_float4(o[c] / lfin, o[c + 1] / lfin, o[c + 2] / lfin, o[c + 3] / lfin);
+            }
+        }
+    } else if (warp >= SPLIT_WARP0) {
+        // ---- split warps: lo parts of q, kt and v -------------------------
+        const int wt = threadIdx.x - SPLIT_WARP0 * 32;
+        int64_t g = 0;
+        uint32_t bad = 0;
+        for (int64_t i = 0; i < my_units && !s_fail; ++i) {
+            if (!mbar_wait(q_full, (uint32_t)(i & 1))) {
+                s_fail = 1;
+                break;
+            }
+            split_buf(smem_u32(smem), Q_BYTES / 16, Q_BYTES, wt);
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(q_conv);
+            for (int e = 0; e < items; ++e, ++g) {
+                const int s = (int)(g % NSLOT);
+                if (!mbar_wait(&slot_full[s], (uint32_t)((g / NSLOT) & 1))) {
+                    s_fail = 1;
+                    break;
+                }
+                bool is_v;
+                int blk, part;
+                slot_item(e, nkb, is_v, blk, part);
+                const uint32_t bits = split_buf(smem_u32(ring + s * SLOT), SLOT / 32, SLOT / 2, wt);
+                if (is_v) {
+                    // rows of v past sk are TMA zero fill: only real keys count
+                    const int real = p.sk - (blk * BKEY + part * 16);
+                    if (real > 0) bad |= bits;
+                }
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&slot_conv[s]);
+            }
+        }
+        if (bad) atomicOr(p.flag, 2u);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+    if (threadIdx.x == 0 && s_fail) atomicOr(p.status, KX_TIMEOUT_FLAG);
+}
+
+}  // namespace attn
+}  // namespace tc
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+// Launch the fused kernel for q [nb, sq, 128], kt given as k [nb, sk, 128]
+// (row stride k_rs, unit stride along the head dimension), v [nb, sk, 128]
+// and a C-contiguous out [nb, sq, 128].  KX_DECLINED when the tensor maps
+// cannot describe the operands.
+int run_attention_fused(Handle *h, const float *q, int64_t q_rs, int64_t q_bs, const float *k, int64_t k_rs,
+                        int64_t k_bs, const float *v, int64_t v_rs, int64_t v_bs, float *out, int64_t nb, int64_t sq,
+                        int64_t sk, float temperature, const char **kernel_name) {
+    using namespace tc;
+    using namespace tc::attn;
+    auto al16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+    if (!al16(q) || !al16(k) || !al16(v) || !al16(out)) return KX_DECLINED;
+    for (int64_t s : {q_rs, k_rs, v_rs})
+        if (s <= 0 || (s * 4) % 16 != 0) return KX_DECLINED;
+    if (nb > 1)
+        for (int64_t s : {q_bs, k_bs, v_bs})
+            if (s <= 0 || (s * 4) % 16 != 0) return KX_DECLINED;
+    if (nb > INT32_MAX || sq > INT32_MAX || sk > INT32_MAX) return KX_DECLINED;
+    auto s2 = [&](int64_t bs, int64_t rs, int64_t rows) {
+        return nb > 1 ? (uint64_t)bs * 4 : (uint64_t)((rs * 4 * rows + 15) / 16 * 16);
+    };
+    CUtensorMap mq, mk, mv;
+    if (!make_map(&mq, q, DH, (uint64_t)sq, (uint64_t)nb, (uint64_t)q_rs * 4, s2(q_bs, q_rs, sq), 16, BQ,
+                  CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map(&mk, k, DH, (uint64_t)sk, (uint64_t)nb, (uint64_t)k_rs * 4, s2(k_bs, k_rs, sk), 16, BKEY,
+                  CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map(&mv, v, DH, (uint64_t)sk, (uint64_t)nb, (uint64_t)v_rs * 4, s2(v_bs, v_rs, sk), 32, 16,
+                  CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+        return KX_DECLINED;
+    Params pp;
+    std::memset(&pp, 0, sizeof(pp));
+    pp.out = out;
+    pp.o_rs = DH;
+    pp.o_bs = sq * DH;
+    pp.sq = (int)sq;
+    pp.sk = (int)sk;
+    pp.nbatch = (int)nb;
+    pp.nq = (int)((sq + BQ - 1) / BQ);
+    pp.units = (int64_t)pp.nq * nb;
+    pp.nkb = (int)((sk + BKEY - 1) / BKEY);
+    pp.temperature = temperature;
+    pp.recip = 1.0f / temperature;
+    pp.use_recip = std::isnormal(pp.recip) && std::isnormal(temperature) &&
+                   std::fabs((double)pp.recip) < 3.4e38 / 4;
+    pp.status = h->flags + kStatusWord;
+    pp.flag = h->flags + kAttnFlagWord;
+    const int64_t grid = pp.units < h->sm_count ? pp.units : h->sm_count;
+    cudaError_t ce = cudaFuncSetAttribute(attn_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (ce == cudaSuccess) {
+        attn_3xtf32_kernel<<<(unsigned)grid, NT, SMEM_BYTES, h->stream>>>(mq, mk, mv, pp);
+        ce = cudaGetLastError();
+    }
+    *kernel_name = "attn_3xtf32_128x64";
+    ++h->launches;
+    return ce == cudaSuccess ? KX_OK : h->cuda_fail(ce);
+}
+
+
+namespace {
+
+// One batch stride for the leading dims of t (all but the last two), when
+// they nest in C order (singleton dims ignored); false otherwise.
+bool collapse_batch(const kx_tensor *t, int64_t *stride) {
+    const int nb = (int)t->rank - 2;
+    int64_t st = 0, expect = 0;
+    bool have = false;
+    for (int d = nb - 1; d >= 0; --d) {
+        if (t->dims[d] == 1) continue;
+        if (!have) {
+            st = t->strides[d];
+            expect = st * (int64_t)t->dims[d];
+            have = true;
+        } else {
+            if (t->strides[d] != expect) return false;
+            expect *= (int64_t)t->dims[d];
+        }
+    }
+    *stride = have ? st : 0;
+    return true;
+}
+
+// A C-contiguous descriptor over `data` with the given dims.
+kx_tensor dense_desc(void *data, const uint64_t *dims, uint32_t rank) {
+    kx_tensor t;
+    std::memset(&t, 0, sizeof(t));
+    t.data = data;
+    t.rank = rank;
+    int64_t st = 1;
+    for (int d = (int)rank - 1; d >= 0; --d) {
+        t.dims[d] = dims[d];
+        t.strides[d] = st;
+        st *= (int64_t)dims[d];
+    }
+    t.storage_len = (uint64_t)st;
+    return t;
+}
+
+}  // namespace
+
+// The composition the fused kernel stands for, run call by call on the
+// handle's stream: S = matmul(q, kt), P = softmax_temperature(S, -1, T),
+// out = matmul(P, v), with S and P in a grow-only buffer of the handle.
+static int attention_composed(kx_handle *hh, const kx_tensor *q, const kx_tensor *kt, const kx_tensor *v,
+                              float temperature, const kx_tensor *out, const MatmulPlan &ps, kx_error *err) {
+    Handle *h = &hh->impl;
+    const uint64_t ns = numel(ps.out_dims, ps.out_rank);
+    int rc = h->grow(&h->attn, &h->attn_bytes, 2 * ns * sizeof(float) + 256);
+    if (rc) return cuda_err(err, h, "attention");
+    float *sbuf = static_cast<float *>(h->attn);
+    float *pbuf = sbuf + (ns + 63) / 64 * 64;
+    kx_tensor sd = dense_desc(sbuf, ps.out_dims, ps.out_rank);
+    kx_tensor pd = dense_desc(pbuf, ps.out_dims, ps.out_rank);
+    rc = kx_matmul_f32(hh, q, kt, &sd, err);
+    if (rc) return rc;
+    rc = kx_softmax_temperature_f32(hh, &sd, -1, temperature, &pd, err);
+    if (rc) return rc;
+    return kx_matmul_f32(hh, &pd, v, out, err);
+}
+
+extern "C" int kx_attention_f32(kx_handle *hh, const kx_tensor *q, const kx_tensor *kt, const kx_tensor *v,
+                                float temperature, const kx_tensor *out, kx_error *err) {
+    static const char *kOp = "attention";
+    if (!hh) return set_err(err, KX_E_PARAM, kOp, "null handle");
+    Handle *h = &hh->impl;
+    Span sq_, sk_, sv_, so_;
+    int rc = validate_tensor(q, 4, &sq_, err);
+    if (rc) return rc;
+    rc = validate_tensor(kt, 4, &sk_, err);
+    if (rc) return rc;
+    // the reference order: matmul(q, kt) validates first ...
+    MatmulPlan ps, po;
+    rc = matmul_shape(q->dims, q->rank, kt->dims, kt->rank, &ps, err);
+    if (rc) return rc;
+    // ... then softmax_temperature (temperature, then the axis -1 of S) ...
+    if (!std::isfinite(temperature) || !(temperature > 0.0f))
+        return set_err(err, KX_E_PARAM, "softmax_temperature", "temperature (must be finite and > 0)");
+    if (ps.out_rank == 0) return set_err(err, KX_E_AXIS, "softmax_temperature", "axis", (uint64_t)-1, 0);
+    // ... then matmul(P, v)
+    rc = validate_tensor(v, 4, &sv_, err);
+    if (rc) return rc;
+    rc = matmul_shape(ps.out_dims, ps.out_rank, v->dims, v->rank, &po, err);
+    if (rc) return rc;
+    rc = validate_tensor(out, 4, &so_, err);
+    if (rc) return rc;
+    if (out->rank != po.out_rank)
+        return set_err(err, KX_E_LAYOUT, kOp, "output shape mismatch", KX_LAYOUT_OUTPUT_SHAPE_MISMATCH);
+    for (uint32_t i = 0; i < po.out_rank; ++i)
+        if (out->dims[i] != po.out_dims[i])
+            return set_err(err, KX_E_LAYOUT, kOp, "output shape mismatch", KX_LAYOUT_OUTPUT_SHAPE_MISMATCH);
+    if (!is_c_contiguous(out))
+        return set_err(err, KX_E_LAYOUT, kOp, "output must be C-contiguous", KX_LAYOUT_OUTPUT_NOT_C_CONTIGUOUS);
+    if (spans_overlap(out->data, so_, q->data, sq_, 4) || spans_overlap(out->data, so_, kt->data, sk_, 4) ||
+        spans_overlap(out->data, so_, v->data, sv_, 4))
+        return set_err(err, KX_E_ALIAS, kOp, "output overlaps an input");
+    if (numel(po.out_dims, po.out_rank) == 0) return KX_OK;
+    DeviceGuard g(h->device);
+    if (!g.ok) return set_err(err, KX_E_NO_DEVICE, kOp, "cannot select device");
+
+    // Fused path: q [B.., sq, 128], kt [B.., 128, sk] (a transposed view of a
+    // row-major k), v [B.., sk, 128], equal batch dims that nest into one
+    // stride each, unit strides along the head dimension.
+    bool fused = !h->ordered && h->f32_variant != KX_F32_FFMA && q->rank >= 2 && kt->rank == q->rank &&
+                 v->rank == q->rank && ps.k == 128 && po.n == 128 && ps.m > 0 && ps.n > 0;
+    int64_t qb = 0, kb_ = 0, vb = 0, nb = 1;
+    if (fused) {
+        const uint32_t br = q->rank - 2;
+        for (uint32_t d = 0; d < br; ++d) {
+            fused &= q->dims[d] == kt->dims[d] && q->dims[d] == v->dims[d];
+            nb *= (int64_t)q->dims[d];
+        }
+        fused &= q->strides[q->rank - 1] == 1 && kt->strides[kt->rank - 2] == 1 && v->strides[v->rank - 1] == 1;
+        fused &= collapse_batch(q, &qb) && collapse_batch(kt, &kb_) && collapse_batch(v, &vb);
+    }
+    if (fused) {
+        cudaError_t ce = cudaMemsetAsync(h->flags + kAttnFlagWord, 0, sizeof(uint32_t), h->stream);
+        if (ce != cudaSuccess) {
+            h->cuda_fail(ce);
+            return cuda_err(err, h, kOp);
+        }
+        const char *name = "none";
+        rc = run_attention_fused(h, static_cast<const float *>(q->data) + q->origin, q->strides[q->rank - 2], qb,
+                                 static_cast<const float *>(kt->data) + kt->origin, kt->strides[kt->rank - 1], kb_,
+                                 static_cast<const float *>(v->data) + v->origin, v->strides[v->rank - 2], vb,
+                                 static_cast<float *>(out->data) + out->origin, nb, (int64_t)ps.m, (int64_t)ps.n,
+                                 temperature, &name);
+        if (rc == KX_E_CUDA) return cuda_err(err, h, kOp);
+        if (rc == KX_OK) {
+            h->last_kernel = name;
+            uint32_t words[8];
+            ce = cudaMemcpyAsync(words, h->flags, sizeof(words), cudaMemcpyDeviceToHost, h->stream);
+            if (ce == cudaSuccess) ce = cudaStreamSynchronize(h->stream);
+            if (ce != cudaSuccess) {
+                h->cuda_fail(ce);
+                return cuda_err(err, h, kOp);
+            }
+            if (words[kStatusWord] & tc::KX_TIMEOUT_FLAG)
+                return set_err(err, KX_E_TIMEOUT, kOp, "a bounded device wait expired");
+            if (words[kAttnFlagWord] == 0) return KX_OK;
+            // an inf/NaN score, an overflowing x - max or an inf/NaN in v: the
+            // composed path gives the reference's result or error
+        }
+    }
+    return attention_composed(hh, q, kt, v, temperature, out, ps, err);
+}
+
+}  // namespace kx

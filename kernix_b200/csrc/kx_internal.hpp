@@ -27,6 +27,8 @@ struct Handle {
     uint64_t ws_bytes = 0;
     void *stage[3] = {nullptr, nullptr, nullptr};   // host-hook device staging (a, b, out)
     uint64_t stage_bytes[3] = {0, 0, 0};
+    void *attn = nullptr;        // scores and probabilities of the composed attention path
+    uint64_t attn_bytes = 0;
     uint32_t *flags = nullptr;   // device status words (nonfinite index, timeouts)
     static constexpr int kFlagWords = 64;
     // Host-hook pipeline: copy streams and per-piece events, created on first use.
@@ -116,9 +118,12 @@ int mc_copy(Handle *h, const void *src, void *mc_dst, uint64_t bytes);
 //   [1]     status written by device code: bit 0 = a bounded wait expired
 //   [2..3]  softmax: 64-bit key of the first nonfinite element (8-byte aligned)
 //   [4]     conv2d: some weight is NaN or infinite
+//   [5]     fused attention: the composed path must run (bit 0: a score or
+//           x - max is inf/NaN; bit 1: v holds an inf/NaN)
 constexpr int kStatusWord = 1;
 constexpr int kSoftmaxWord = 2;
 constexpr int kConvFlagWord = 4;
+constexpr int kAttnFlagWord = 5;
 
 }  // namespace kx
 

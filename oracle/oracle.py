@@ -347,3 +347,27 @@ def _softmax_rows(x: np.ndarray, axis: int, temperature: float, operation: str) 
         idx = outer[:ax] + [pos] + outer[ax:]
         raise OracleError("NonFiniteInput", operation=operation, indices=[int(i) for i in idx])
     return np.moveaxis(out, -1, ax)
+
+
+# ---------------------------------------------------------------------------
+# attention products (matmul -> softmax_temperature -> matmul)
+# ---------------------------------------------------------------------------
+def attention_truth(q: np.ndarray, k: np.ndarray, v: np.ndarray, temperature: float, rows=None):
+    """Attention of f32 inputs q [nb, sq, d], k [nb, sk, d], v [nb, sk, dv]
+    in extended precision: S by the compensated product, P = exp((S - max)/T)
+    / sum in long double, O = P v in f64.  Returns (O, P|v| row sums per
+    output, max over keys of sum|q k|) for the selected query rows."""
+    nb, sq, d = q.shape
+    rows = list(range(sq)) if rows is None else list(rows)
+    outs, absv, sabs = [], [], []
+    for b in range(nb):
+        qb = np.ascontiguousarray(q[b][rows])
+        s, ab = gemm_dot2(View.of(qb), View(np.ascontiguousarray(k[b]), (d, k.shape[1]), (1, d)))
+        sl = s.astype(np.longdouble)
+        e = np.exp((sl - sl.max(axis=1, keepdims=True)) / np.longdouble(temperature))
+        p = (e / e.sum(axis=1, keepdims=True)).astype(np.float64)
+        vb = v[b].astype(np.float64)
+        outs.append(p @ vb)
+        absv.append(p @ np.abs(vb))
+        sabs.append(ab.max(axis=1))
+    return np.stack(outs), np.stack(absv), np.stack(sabs)
