@@ -30,18 +30,24 @@
 // is folded into f32 registers right away, so the tensor core's truncating
 // accumulation never runs over more than 64 keys.
 //
-// Roles (512 threads, one CTA per SM, persistent over (batch, row block) units):
+// Roles (384 threads, one CTA per SM, persistent over (batch, row block) units):
 //   warp 0       TMA producer: q block, then per key block 4 kt slots and
 //                4 v slots through a ring of 16 KB slots
 //   warp 1       TMEM owner (512 columns) and MMA issuer
-//   warps 2..5   softmax: one row each (TMEM lane), S_j -> P_j, m, l
-//   warps 6..13  fold: rows x 64 columns of O in registers; epilogue stores
-//   warps 14,15  split: lo parts of q, kt and v (v checked for inf/NaN)
+//   warps 2..9   rows: two threads per row (TMEM lane), each with half of the
+//                scores (S_j -> P_j, m, l) and half of O in registers (the
+//                fold of block j - 1 right after the softmax of block j);
+//                epilogue stores
+//   warps 10,11  split: lo parts of q, kt and v (v checked for inf/NaN)
+// Two threads per row and two row warps per SM sub-partition keep the
+// softmax (one exponential per score) off the critical path: with one warp
+// per sub-partition doing whole rows it paced the tensor cores.
 // TMEM: S buffer b (b = key block % 2) at columns [128 b, 128 b + 128): hi.hi
 // scores in the first 64, cross terms in the next 64, overwritten in place by
 // P_hi and P_lo; O buffer b at [256 + 128 b, 256 + 128 b + 128).
 // Every mbarrier wait is bounded (2 s); on expiry the kernel stops its loops,
 // waits for its own TMA copies, frees TMEM and sets the handle's status bit.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 
@@ -65,11 +71,12 @@ constexpr int SLOT = 16384;        // hi (8 KB) + lo (8 KB)
 constexpr int Q_BYTES = BQ * DH * 4;          // 64 KB (hi); lo follows
 constexpr int RING_OFF = 2 * Q_BYTES;         // 128 KB
 constexpr int MISC_OFF = RING_OFF + NSLOT * SLOT;   // 208 KB
-// misc: mbarriers (256 B), alpha ring [4][128] and l ring [4][128] f32 (4 KB)
-constexpr int MISC_BYTES = 256 + 2 * 4 * BQ * 4;
+// misc: mbarriers (512 B), the row-maximum exchange [2][2][128] f32 (2 KB)
+// and the row-sum exchange [2][128] f32 (1 KB)
+constexpr int MISC_BYTES = 512 + 3 * 2 * BQ * 4;
 constexpr int SMEM_BYTES = MISC_OFF + MISC_BYTES + 1024;
-constexpr int NT = 512;
-constexpr int SOFT_WARP0 = 2, FOLD_WARP0 = 6, SPLIT_WARP0 = 14, SPLIT_WARPS = 2;
+constexpr int ROW_WARP0 = 2, SPLIT_WARP0 = 10, SPLIT_WARPS = 2;
+constexpr int NT = (SPLIT_WARP0 + SPLIT_WARPS) * 32;   // 384
 constexpr int SPLIT_THREADS = SPLIT_WARPS * 32;
 static_assert(SMEM_BYTES <= 232448, "shared memory");
 
@@ -80,23 +87,24 @@ struct Params {
     int nq;                      // row blocks per batch entry
     int64_t units;               // nbatch * nq
     int nkb;                     // key blocks
-    float temperature, recip;    // T and 1/T (recip used when use_recip)
-    int use_recip;
+    float c, c_lo;               // log2(e)/T rounded to f32, and its rounding error
     uint32_t *status;            // bit 0: a bounded wait expired
     uint32_t *flag;              // nonzero: run the composed path
 };
 
-// (x - m) / T as the softmax kernel computes it: the reciprocal with one
-// Markstein residual correction ("IA-64 and Elementary Functions", 2000),
-// within an ulp of the IEEE quotient; the IEEE division when 1/T is not a
-// normal number.
-__device__ __forceinline__ float scaled(float diff, const Params &p) {
-    if (p.use_recip) {
-        const float q = diff * p.recip;
-        const float r = fmaf(-p.temperature, q, diff);
-        return fmaf(r, p.recip, q);
-    }
-    return diff / p.temperature;
+// exp(x / T) for x = s - max <= 0 as 2^t with t = x * log2(e) / T: c =
+// log2(e)/T rounded to f32 and c_lo its rounding error (both from the host in
+// double precision), t = x c rounded, tl = the exact residual of x c (one FMA)
+// plus x c_lo, then 2^t by the special-function unit (ex2.approx, a few ulp)
+// and the first-order correction 2^(t + tl) = 2^t (1 + tl ln 2).  About 3 ulp
+// from exp(x / T) in all, the order of the reference's own rounding of
+// (x - max) / T before its exp; below 2^-126 the result is flushed to zero.
+__device__ __forceinline__ float exp_scaled(float x, float c, float c_lo) {
+    const float t = x * c;
+    const float tl = fmaf(x, c_lo, fmaf(x, c, -t));
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t));
+    return fmaf(e * tl, 0.693147182f, e);
 }
 
 // 16 consecutive 32-bit columns of this thread's TMEM lane.
@@ -121,10 +129,33 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, ui
         : "memory");
 }
 
+// Bounded wait for waits off the critical path (the producer's, the fold's,
+// the split's wait for a q block): a short sleep between polls leaves the
+// issue slots of the SM sub-partition to the row warps that share it.  Same
+// 2 s deadline as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t *bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    uint64_t deadline = 0;
+    while (true) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+        const uint64_t now = globaltimer();
+        if (deadline == 0) deadline = now + WAIT_NS;
+        else if (now > deadline) return false;
+        __nanosleep(200);
+    }
+}
+
 // Split one buffer of `chunks` 16-byte chunks in place: lo (x - tf32(x)) at
-// `lo_off` bytes past each raw chunk.  Returns the nonfinite bits seen.
-__device__ __forceinline__ uint32_t split_buf(uint32_t base, int chunks, uint32_t lo_off, int wt) {
-    uint32_t bad = 0;
+// `lo_off` bytes past each raw chunk.
+__device__ __forceinline__ void split_buf(uint32_t base, int chunks, uint32_t lo_off, int wt) {
 #pragma unroll 4
     for (int c = wt; c < chunks; c += SPLIT_THREADS * 4) {
         float4 v[4];
@@ -138,15 +169,34 @@ __device__ __forceinline__ uint32_t split_buf(uint32_t base, int chunks, uint32_
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int cc = c + u * SPLIT_THREADS;
-            if (cc < chunks) {
-                bad |= nonfinite_bits(v[u].x) | nonfinite_bits(v[u].y) | nonfinite_bits(v[u].z) |
-                       nonfinite_bits(v[u].w);
+            if (cc < chunks)
                 sts_v4_f32(at[u] + lo_off, v[u].x - tf32_trunc(v[u].x), v[u].y - tf32_trunc(v[u].y),
                            v[u].z - tf32_trunc(v[u].z), v[u].w - tf32_trunc(v[u].w));
-            }
         }
     }
-    return bad;
+}
+
+// lo parts of a [nb, rows, 128] operand (row stride rs, batch stride bs;
+// 16-byte rows) into a dense [nb, rows, 128] array, before the fused kernel:
+// its TMA then brings hi (the operand itself) and lo into each slot, and no
+// warp of the fused kernel splits k or v.  With CHECK, an inf or NaN sets
+// bit 1 of `flag` (v: the composed path propagates it through P v).
+template <bool CHECK>
+__global__ void __launch_bounds__(256) split_lo_kernel(const float *__restrict__ x, int64_t rs, int64_t bs,
+                                                       float *__restrict__ lo, int64_t rows, int64_t nb,
+                                                       uint32_t *flag) {
+    const int64_t n4 = nb * rows * (DH / 4);
+    uint32_t mag = 0;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n4; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t d4 = e % (DH / 4), rr = (e / (DH / 4)) % rows, b = e / (DH / 4) / rows;
+        const float4 v = *reinterpret_cast<const float4 *>(x + b * bs + rr * rs + d4 * 4);
+        if (CHECK)
+            mag = max(mag, max(max(__float_as_uint(v.x) & 0x7fffffffu, __float_as_uint(v.y) & 0x7fffffffu),
+                               max(__float_as_uint(v.z) & 0x7fffffffu, __float_as_uint(v.w) & 0x7fffffffu)));
+        reinterpret_cast<float4 *>(lo)[e] =
+            make_float4(v.x - tf32_trunc(v.x), v.y - tf32_trunc(v.y), v.z - tf32_trunc(v.z), v.w - tf32_trunc(v.w));
+    }
+    if (CHECK && __any_sync(0xffffffffu, mag >= 0x7f800000u) && (threadIdx.x & 31) == 0) atomicOr(flag, 2u);
 }
 
 // Slot stream of one unit, in the order the MMA thread consumes it:
@@ -168,16 +218,18 @@ __device__ __forceinline__ void slot_item(int e, int nkb, bool &is_v, int &blk, 
     }
 }
 
+// Registers are split evenly over the SM's four sub-partitions (16,384
+// each); twelve warps put three on each, so a thread may use up to 168.
 __global__ void __launch_bounds__(NT, 1)
 attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ Params p) {
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKl,
+                   const __grid_constant__ CUtensorMap tmVl, const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *ring = smem + RING_OFF;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + MISC_OFF);
     uint64_t *slot_full = bars;                 // [NSLOT]
-    uint64_t *slot_conv = slot_full + NSLOT;    // [NSLOT]
-    uint64_t *slot_empty = slot_conv + NSLOT;   // [NSLOT]
+    uint64_t *slot_empty = slot_full + NSLOT;   // [NSLOT]
     uint64_t *q_full = slot_empty + NSLOT;
     uint64_t *q_conv = q_full + 1;
     uint64_t *q_empty = q_conv + 1;
@@ -185,10 +237,11 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     uint64_t *p_ready = s_full + 2;             // [2]
     uint64_t *o_full = p_ready + 2;             // [2]
     uint64_t *o_empty = o_full + 2;             // [2]
-    uint64_t *a_ready = o_empty + 2;            // [4]
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(a_ready + 4);
-    float *alpha_ring = reinterpret_cast<float *>(smem + MISC_OFF + 256);   // [4][BQ]
-    float *l_ring = alpha_ring + 4 * BQ;                                    // [4][BQ]
+    uint64_t *xbar = o_empty + 2;               // [4] row-maximum exchange per lane quarter
+    uint64_t *lbar = xbar + 4;                  // [4] row-sum exchange per lane quarter
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(lbar + 4);
+    float *xmax = reinterpret_cast<float *>(smem + MISC_OFF + 512);   // [2][2][BQ]
+    float *lsum = xmax + 4 * BQ;                                      // [2][BQ]
     __shared__ int s_fail_storage;
     volatile int &s_fail = s_fail_storage;
 
@@ -200,7 +253,6 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     if (threadIdx.x == 0) {
         for (int s = 0; s < NSLOT; ++s) {
             mbar_init(&slot_full[s], 1);
-            mbar_init(&slot_conv[s], SPLIT_WARPS);
             mbar_init(&slot_empty[s], 1);
         }
         mbar_init(q_full, 1);
@@ -208,11 +260,14 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         mbar_init(q_empty, 1);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&s_full[b], 1);
-            mbar_init(&p_ready[b], 4);
+            mbar_init(&p_ready[b], 8);
             mbar_init(&o_full[b], 1);
             mbar_init(&o_empty[b], 8);
         }
-        for (int r = 0; r < 4; ++r) mbar_init(&a_ready[r], 4);
+        for (int r = 0; r < 4; ++r) {
+            mbar_init(&xbar[r], 2);
+            mbar_init(&lbar[r], 2);
+        }
         s_fail = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -235,7 +290,7 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             for (; i < my_units && !s_fail; ++i) {
                 const int64_t u = blockIdx.x + i * gridDim.x;
                 const int bh = (int)(u / p.nq), q0 = (int)(u % p.nq) * BQ;
-                if (i > 0 && !mbar_wait(q_empty, (uint32_t)((i - 1) & 1))) {
+                if (i > 0 && !mbar_wait_idle(q_empty, (uint32_t)((i - 1) & 1))) {
                     s_fail = 1;
                     break;
                 }
@@ -244,7 +299,7 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 for (int t = 0; t < DH / 16; ++t) tma_load_3d(smem + t * 8192, &tmQ, t * 16, q0, bh, q_full);
                 for (int e = 0; e < items; ++e, ++g) {
                     const int s = (int)(g % NSLOT);
-                    if (g >= NSLOT && !mbar_wait(&slot_empty[s], (uint32_t)(((g / NSLOT) - 1) & 1))) {
+                    if (g >= NSLOT && !mbar_wait_idle(&slot_empty[s], (uint32_t)(((g / NSLOT) - 1) & 1))) {
                         s_fail = 1;
                         break;
                     }
@@ -252,16 +307,21 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     int blk, part;
                     slot_item(e, nkb, is_v, blk, part);
                     uint8_t *dst = ring + s * SLOT;
-                    mbar_expect_tx(&slot_full[s], SLOT / 2);
+                    mbar_expect_tx(&slot_full[s], SLOT);
                     if (!is_v) {
-                        // kt_j: 64 keys x 32 head columns as two 16-column boxes
+                        // kt_j: 64 keys x 32 head columns as two 16-column boxes, hi then lo
                         tma_load_3d(dst, &tmK, part * 32, blk * BKEY, bh, &slot_full[s]);
                         tma_load_3d(dst + 4096, &tmK, part * 32 + 16, blk * BKEY, bh, &slot_full[s]);
+                        tma_load_3d(dst + SLOT / 2, &tmKl, part * 32, blk * BKEY, bh, &slot_full[s]);
+                        tma_load_3d(dst + SLOT / 2 + 4096, &tmKl, part * 32 + 16, blk * BKEY, bh, &slot_full[s]);
                     } else {
-                        // v_j: 16 keys x 128 columns as four 32-column boxes
+                        // v_j: 16 keys x 128 columns as four 32-column boxes, hi then lo
 #pragma unroll
-                        for (int c = 0; c < 4; ++c)
+                        for (int c = 0; c < 4; ++c) {
                             tma_load_3d(dst + c * 2048, &tmV, c * 32, blk * BKEY + part * 16, bh, &slot_full[s]);
+                            tma_load_3d(dst + SLOT / 2 + c * 2048, &tmVl, c * 32, blk * BKEY + part * 16, bh,
+                                        &slot_full[s]);
+                        }
                     }
                 }
             }
@@ -277,7 +337,7 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         if (lane == 0) {
             constexpr uint32_t idesc_s = idesc_tf32<BKEY>(false);
             constexpr uint32_t idesc_o = idesc_tf32<DH>(true);
-            const uint32_t q_hi = smem_u32(smem), q_lo = q_hi + Q_BYTES;
+            const uint64_t dq_hi = desc_k_sw64(smem_u32(smem)), dq_lo = desc_k_sw64(smem_u32(smem) + Q_BYTES);
             int64_t g = 0;        // slot items consumed
             int64_t kb = 0;       // key blocks started (global, for the TMEM buffers)
             for (int64_t i = 0; i < my_units && !s_fail; ++i) {
@@ -292,30 +352,30 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     if (j < nkb) {
                         const int64_t gb = kb0 + j;
                         const uint32_t sm = tmem + (uint32_t)((gb & 1) * 128), sx = sm + 64;
-                        for (int t = 0; t < 4; ++t, ++g) {
+#pragma unroll 1
+                        for (int t = 0; t < 4; ++t) {
                             const int s = (int)(g % NSLOT);
-                            if (!mbar_wait(&slot_conv[s], (uint32_t)((g / NSLOT) & 1))) {
+                            if (!mbar_wait(&slot_full[s], (uint32_t)((g / NSLOT) & 1))) {
                                 s_fail = 1;
                                 break;
                             }
                             tc_fence_after();
-                            const uint32_t k_hi = smem_u32(ring + s * SLOT), k_lo = k_hi + SLOT / 2;
+                            // descriptors: base + (byte offset >> 4) in the address field
+                            const uint64_t dk = desc_k_sw64(smem_u32(ring + s * SLOT));
 #pragma unroll
                             for (int sub = 0; sub < 2; ++sub) {
-                                const uint32_t qh = q_hi + (uint32_t)((2 * t + sub) * 8192);
-                                const uint32_t ql = q_lo + (uint32_t)((2 * t + sub) * 8192);
 #pragma unroll
                                 for (int ks = 0; ks < 2; ++ks) {
-                                    const uint64_t dqh = desc_k_sw64(qh + ks * 32), dql = desc_k_sw64(ql + ks * 32);
-                                    const uint64_t dkh = desc_k_sw64(k_hi + sub * 4096 + ks * 32);
-                                    const uint64_t dkl = desc_k_sw64(k_lo + sub * 4096 + ks * 32);
+                                    const uint32_t qo = (uint32_t)(((2 * t + sub) * 8192 + ks * 32) >> 4);
+                                    const uint32_t ko = (uint32_t)((sub * 4096 + ks * 32) >> 4);
                                     const uint32_t acc = (t > 0 || sub > 0 || ks > 0) ? 1u : 0u;
-                                    mma_tf32(sm, dqh, dkh, idesc_s, acc);
-                                    mma_tf32(sx, dqh, dkl, idesc_s, acc);
-                                    mma_tf32(sx, dql, dkh, idesc_s, 1u);
+                                    mma_tf32(sm, dq_hi + qo, dk + ko, idesc_s, acc);
+                                    mma_tf32(sx, dq_hi + qo, dk + ko + (SLOT / 2 >> 4), idesc_s, acc);
+                                    mma_tf32(sx, dq_lo + qo, dk + ko, idesc_s, 1u);
                                 }
                             }
                             mma_commit(&slot_empty[s]);
+                            ++g;
                         }
                         if (s_fail) break;
                         mma_commit(&s_full[gb & 1]);
@@ -333,25 +393,26 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         tc_fence_after();
                         const uint32_t ph = tmem + (uint32_t)(b * 128), pl = ph + 64;
                         const uint32_t od = tmem + 256u + (uint32_t)(b * 128);
-                        for (int t = 0; t < 4; ++t, ++g) {
+#pragma unroll 1
+                        for (int t = 0; t < 4; ++t) {
                             const int s = (int)(g % NSLOT);
-                            if (!mbar_wait(&slot_conv[s], (uint32_t)((g / NSLOT) & 1))) {
+                            if (!mbar_wait(&slot_full[s], (uint32_t)((g / NSLOT) & 1))) {
                                 s_fail = 1;
                                 break;
                             }
                             tc_fence_after();
-                            const uint32_t v_hi = smem_u32(ring + s * SLOT), v_lo = v_hi + SLOT / 2;
+                            const uint64_t dv = desc_mn_sw128(smem_u32(ring + s * SLOT), 2048, 512);
 #pragma unroll
                             for (int ks = 0; ks < 2; ++ks) {
-                                const uint64_t dvh = desc_mn_sw128(v_hi + ks * 1024, 2048, 512);
-                                const uint64_t dvl = desc_mn_sw128(v_lo + ks * 1024, 2048, 512);
+                                const uint32_t vo = (uint32_t)((ks * 1024) >> 4);
                                 const uint32_t col = (uint32_t)(t * 16 + ks * 8);
                                 const uint32_t acc = (t > 0 || ks > 0) ? 1u : 0u;
-                                mma_tf32_ts(od, ph + col, dvh, idesc_o, acc);
-                                mma_tf32_ts(od, ph + col, dvl, idesc_o, 1u);
-                                mma_tf32_ts(od, pl + col, dvh, idesc_o, 1u);
+                                mma_tf32_ts(od, ph + col, dv + vo, idesc_o, acc);
+                                mma_tf32_ts(od, ph + col, dv + vo + (SLOT / 2 >> 4), idesc_o, 1u);
+                                mma_tf32_ts(od, pl + col, dv + vo, idesc_o, 1u);
                             }
                             mma_commit(&slot_empty[s]);
+                            ++g;
                         }
                         if (s_fail) break;
                         mma_commit(&o_full[b]);
@@ -366,128 +427,132 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 }
             }
         }
-    } else if (warp >= SOFT_WARP0 && warp < FOLD_WARP0) {
-        // ---- softmax: one row per thread ------------------------------------
+    } else if (warp >= ROW_WARP0 && warp < SPLIT_WARP0) {
+        // ---- row warps: softmax of block j, then the fold of block j-1 ------
+        // Two threads per row: warp w and w + 4 share the TMEM lane quarter
+        // w % 4; `half` picks score columns [32 half, 32 half + 32) and output
+        // columns [64 half, 64 half + 64).  The pair agrees on the row maximum
+        // through shared memory and a two-arrival mbarrier per quarter.
         const int quarter = warp & 3;
+        const int half = (warp - ROW_WARP0) >> 2;
         const int r = quarter * 32 + lane;                       // row in the block
         const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+        const float ct = p.c, ct_lo = p.c_lo;   // log2(e) / T and its rounding error
         int64_t kb = 0;
-        for (int64_t i = 0; i < my_units && !s_fail; ++i) {
-            float m = -INFINITY, l = 0.0f;
-            uint32_t bad = 0;
-            for (int j = 0; j < nkb && !s_fail; ++j, ++kb) {
-                const int b = (int)(kb & 1);
-                if (!mbar_wait(&s_full[b], (uint32_t)((kb >> 1) & 1))) {
-                    s_fail = 1;
-                    break;
-                }
-                tc_fence_after();
-                if (s_fail) break;
-                const int valid = p.sk - j * BKEY < BKEY ? p.sk - j * BKEY : BKEY;
-                float sv[64];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    uint32_t a0[16], a1[16], x0[16], x1[16];
-                    const uint32_t base = lane_base + (uint32_t)(b * 128 + h * 32);
-                    tmem_ld16(base, a0);
-                    tmem_ld16(base + 16, a1);
-                    tmem_ld16(base + 64, x0);
-                    tmem_ld16(base + 80, x1);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int c = 0; c < 16; ++c) {
-                        sv[h * 32 + c] = __uint_as_float(a0[c]) + __uint_as_float(x0[c]);
-                        sv[h * 32 + 16 + c] = __uint_as_float(a1[c]) + __uint_as_float(x1[c]);
-                    }
-                }
-                float bmax = -INFINITY;
-#pragma unroll
-                for (int c = 0; c < 64; ++c) {
-                    if (c < valid) {
-                        bad |= nonfinite_bits(sv[c]);
-                        bmax = fmaxf(bmax, sv[c]);
-                    }
-                }
-                const float m_new = fmaxf(m, bmax);
-                float alpha = 0.0f;
-                if (m != -INFINITY) {
-                    const float dd = m - m_new;
-                    alpha = expf(scaled(dd, p));
-                }
-                float bsum = 0.0f;
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    uint32_t phv[16], plv[16];
-#pragma unroll
-                    for (int c = 0; c < 16; ++c) {
-                        float pv = 0.0f;
-                        if (h * 16 + c < valid) {
-                            const float diff = sv[h * 16 + c] - m_new;
-                            bad |= nonfinite_bits(diff);
-                            pv = expf(scaled(diff, p));
-                        }
-                        bsum += pv;
-                        const float hi = tf32_trunc(pv);
-                        phv[c] = __float_as_uint(hi);
-                        plv[c] = __float_as_uint(pv - hi);
-                    }
-                    tmem_st16(lane_base + (uint32_t)(b * 128 + h * 16), phv);
-                    tmem_st16(lane_base + (uint32_t)(b * 128 + 64 + h * 16), plv);
-                }
-                l = l * alpha + bsum;
-                m = m_new;
-                tmem_wait_st();
-                tc_fence_before();
-                const int rs = (int)(kb & 3);
-                alpha_ring[rs * BQ + r] = alpha;
-                l_ring[rs * BQ + r] = l;
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&p_ready[b]);
-                    mbar_arrive(&a_ready[rs]);
-                }
-            }
-            if (bad) atomicOr(p.flag, 1u);
-        }
-    } else if (warp >= FOLD_WARP0 && warp < SPLIT_WARP0) {
-        // ---- fold: O = O * alpha + O_j in registers; epilogue -------------
-        const int quarter = warp & 3;
-        const int half = (warp - FOLD_WARP0) >> 2;             // columns [64 half, 64 half + 64)
-        const int r = quarter * 32 + lane;
-        const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + 256u + (uint32_t)(half * 64);
-        int64_t kb = 0;
+        uint32_t bad = 0;
         for (int64_t i = 0; i < my_units && !s_fail; ++i) {
             const int64_t u = blockIdx.x + i * gridDim.x;
             const int bh = (int)(u / p.nq), row = (int)(u % p.nq) * BQ + r;
+            float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
             float o[64];
 #pragma unroll
             for (int c = 0; c < 64; ++c) o[c] = 0.0f;
-            float lfin = 1.0f;
-            for (int j = 0; j < nkb && !s_fail; ++j, ++kb) {
-                const int b = (int)(kb & 1);
-                const int rs = (int)(kb & 3);
-                if (!mbar_wait(&o_full[b], (uint32_t)((kb >> 1) & 1)) ||
-                    !mbar_wait(&a_ready[rs], (uint32_t)((kb >> 2) & 1))) {
-                    s_fail = 1;
-                    break;
-                }
+            // O_kb = O * alpha + O_j from TMEM buffer kb % 2, then release it
+            auto fold = [&](int64_t fkb, float alpha) -> bool {
+                const int fb = (int)(fkb & 1);
+                if (!mbar_wait_idle(&o_full[fb], (uint32_t)((fkb >> 1) & 1))) return false;
                 tc_fence_after();
-                if (s_fail) break;
-                const float alpha = alpha_ring[rs * BQ + r];
-                if (j == nkb - 1) lfin = l_ring[rs * BQ + r];
+                const uint32_t obase = lane_base + 256u + (uint32_t)(fb * 128 + half * 64);
 #pragma unroll
                 for (int h = 0; h < 4; ++h) {
                     uint32_t x[16];
-                    tmem_ld16(lane_base + (uint32_t)(b * 128 + h * 16), x);
+                    tmem_ld16(obase + (uint32_t)(h * 16), x);
                     tmem_wait_ld();
 #pragma unroll
                     for (int c = 0; c < 16; ++c) o[h * 16 + c] = fmaf(o[h * 16 + c], alpha, __uint_as_float(x[c]));
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&o_empty[b]);
+                if (lane == 0) mbar_arrive(&o_empty[fb]);
+                return true;
+            };
+            for (int j = 0; j < nkb && !s_fail; ++j, ++kb) {
+                const int b = (int)(kb & 1);
+                if (!mbar_wait_idle(&s_full[b], (uint32_t)((kb >> 1) & 1))) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                if (s_fail) break;
+                const int c0 = half * 32;
+                const int valid = p.sk - j * BKEY - c0;     // valid columns of this half (may be <= 0 or > 32)
+                const uint32_t sbase = lane_base + (uint32_t)(b * 128 + c0);
+                // pass 1: this half's row maximum over the valid keys
+                float bmax = -INFINITY;
+#pragma unroll 1
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t a0[16], x0[16];
+                    tmem_ld16(sbase + (uint32_t)(h * 16), a0);
+                    tmem_ld16(sbase + 64u + (uint32_t)(h * 16), x0);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) {
+                        const float sc = __uint_as_float(a0[c]) + __uint_as_float(x0[c]);
+                        const bool in = h * 16 + c < valid;
+                        bad |= in ? nonfinite_bits(sc) : 0u;
+                        bmax = fmaxf(bmax, in ? sc : -INFINITY);
+                    }
+                }
+                xmax[((kb & 1) * 2 + half) * BQ + r] = bmax;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&xbar[quarter]);
+                if (!mbar_wait(&xbar[quarter], (uint32_t)(kb & 1))) {
+                    s_fail = 1;
+                    break;
+                }
+                bmax = fmaxf(bmax, xmax[((kb & 1) * 2 + (half ^ 1)) * BQ + r]);
+                const float m_new = fmaxf(m, bmax);
+                const float alpha = m != -INFINITY ? exp_scaled(m - m_new, ct, ct_lo) : 0.0f;
+                // pass 2: P = exp((S - m) / T) split into hi and lo, written over S
+                float bsum = 0.0f;
+#pragma unroll 1
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t a0[16], x0[16];
+                    tmem_ld16(sbase + (uint32_t)(h * 16), a0);
+                    tmem_ld16(sbase + 64u + (uint32_t)(h * 16), x0);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) {
+                        const bool in = h * 16 + c < valid;
+                        const float diff = (__uint_as_float(a0[c]) + __uint_as_float(x0[c])) - m_new;
+                        bad |= in ? nonfinite_bits(diff) : 0u;
+                        const float pv = in ? exp_scaled(diff, ct, ct_lo) : 0.0f;
+                        bsum += pv;
+                        const float hi = tf32_trunc(pv);
+                        a0[c] = __float_as_uint(hi);
+                        x0[c] = __float_as_uint(pv - hi);
+                    }
+                    tmem_st16(sbase + (uint32_t)(h * 16), a0);
+                    tmem_st16(sbase + 64u + (uint32_t)(h * 16), x0);
+                }
+                l = l * alpha + bsum;
+                m = m_new;
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_ready[b]);
+                // fold the previous block's O while the tensor cores run this one
+                if (j > 0 && !fold(kb - 1, alpha_prev)) {
+                    s_fail = 1;
+                    break;
+                }
+                alpha_prev = alpha;
             }
-            if (s_fail) break;
+            if (s_fail || !fold(kb - 1, alpha_prev)) {
+                s_fail = 1;
+                break;
+            }
+            // row sum: the two halves' partial sums, added in one order by both
+            lsum[half * BQ + r] = l;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&lbar[quarter]);
+            if (!mbar_wait(&lbar[quarter], (uint32_t)(i & 1))) {
+                s_fail = 1;
+                break;
+            }
+            // the partner reads this unit's sums before it joins the next
+            // unit's first maximum exchange, which this warp's next write follows
+            const float lfin = lsum[r] + lsum[BQ + r];
             if (row < p.sq) {
                 float *dst = p.out + (int64_t)bh * p.o_bs + (int64_t)row * p.o_rs + half * 64;
 #pragma unroll
@@ -496,13 +561,12 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         make_float4(o[c] / lfin, o[c + 1] / lfin, o[c + 2] / lfin, o[c + 3] / lfin);
             }
         }
+        if (bad) atomicOr(p.flag, 1u);
     } else if (warp >= SPLIT_WARP0) {
-        // ---- split warps: lo parts of q, kt and v -------------------------
+        // ---- split warps: lo part of each q block ---------------------------
         const int wt = threadIdx.x - SPLIT_WARP0 * 32;
-        int64_t g = 0;
-        uint32_t bad = 0;
         for (int64_t i = 0; i < my_units && !s_fail; ++i) {
-            if (!mbar_wait(q_full, (uint32_t)(i & 1))) {
+            if (!mbar_wait_idle(q_full, (uint32_t)(i & 1))) {
                 s_fail = 1;
                 break;
             }
@@ -510,27 +574,7 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             fence_proxy_async();
             __syncwarp();
             if (lane == 0) mbar_arrive(q_conv);
-            for (int e = 0; e < items; ++e, ++g) {
-                const int s = (int)(g % NSLOT);
-                if (!mbar_wait(&slot_full[s], (uint32_t)((g / NSLOT) & 1))) {
-                    s_fail = 1;
-                    break;
-                }
-                bool is_v;
-                int blk, part;
-                slot_item(e, nkb, is_v, blk, part);
-                const uint32_t bits = split_buf(smem_u32(ring + s * SLOT), SLOT / 32, SLOT / 2, wt);
-                if (is_v) {
-                    // rows of v past sk are TMA zero fill: only real keys count
-                    const int real = p.sk - (blk * BKEY + part * 16);
-                    if (real > 0) bad |= bits;
-                }
-                fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&slot_conv[s]);
-            }
         }
-        if (bad) atomicOr(p.flag, 2u);
     }
 
     tc_fence_before();
@@ -568,12 +612,21 @@ int run_attention_fused(Handle *h, const float *q, int64_t q_rs, int64_t q_bs, c
     auto s2 = [&](int64_t bs, int64_t rs, int64_t rows) {
         return nb > 1 ? (uint64_t)bs * 4 : (uint64_t)((rs * 4 * rows + 15) / 16 * 16);
     };
-    CUtensorMap mq, mk, mv;
+    // lo parts of k and v, dense [nb, sk, 128] each, in the handle's buffer
+    const uint64_t lo_elems = (uint64_t)nb * (uint64_t)sk * DH;
+    int rc = h->grow(&h->attn, &h->attn_bytes, 2 * lo_elems * sizeof(float));
+    if (rc) return rc;
+    float *k_lo = static_cast<float *>(h->attn), *v_lo = k_lo + lo_elems;
+    const uint64_t lo_bs = (uint64_t)sk * DH * 4;
+    CUtensorMap mq, mk, mv, mkl, mvl;
     if (!make_map(&mq, q, DH, (uint64_t)sq, (uint64_t)nb, (uint64_t)q_rs * 4, s2(q_bs, q_rs, sq), 16, BQ,
                   CU_TENSOR_MAP_SWIZZLE_64B) ||
         !make_map(&mk, k, DH, (uint64_t)sk, (uint64_t)nb, (uint64_t)k_rs * 4, s2(k_bs, k_rs, sk), 16, BKEY,
                   CU_TENSOR_MAP_SWIZZLE_64B) ||
         !make_map(&mv, v, DH, (uint64_t)sk, (uint64_t)nb, (uint64_t)v_rs * 4, s2(v_bs, v_rs, sk), 32, 16,
+                  CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
+        !make_map(&mkl, k_lo, DH, (uint64_t)sk, (uint64_t)nb, DH * 4, lo_bs, 16, BKEY, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map(&mvl, v_lo, DH, (uint64_t)sk, (uint64_t)nb, DH * 4, lo_bs, 32, 16,
                   CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
         return KX_DECLINED;
     Params pp;
@@ -587,16 +640,23 @@ int run_attention_fused(Handle *h, const float *q, int64_t q_rs, int64_t q_bs, c
     pp.nq = (int)((sq + BQ - 1) / BQ);
     pp.units = (int64_t)pp.nq * nb;
     pp.nkb = (int)((sk + BKEY - 1) / BKEY);
-    pp.temperature = temperature;
-    pp.recip = 1.0f / temperature;
-    pp.use_recip = std::isnormal(pp.recip) && std::isnormal(temperature) &&
-                   std::fabs((double)pp.recip) < 3.4e38 / 4;
+    const double cd = 1.4426950408889634 / (double)temperature;
+    pp.c = (float)cd;
+    pp.c_lo = (float)(cd - (double)pp.c);
+    if (!std::isnormal(pp.c) || !std::isfinite(pp.c_lo)) return KX_DECLINED;
     pp.status = h->flags + kStatusWord;
     pp.flag = h->flags + kAttnFlagWord;
     const int64_t grid = pp.units < h->sm_count ? pp.units : h->sm_count;
-    cudaError_t ce = cudaFuncSetAttribute(attn_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    const int64_t n4 = (int64_t)lo_elems / 4;
+    const unsigned lo_grid = (unsigned)std::min<int64_t>((n4 + 255) / 256, 8LL * h->sm_count);
+    split_lo_kernel<false><<<lo_grid, 256, 0, h->stream>>>(k, k_rs, k_bs, k_lo, sk, nb, pp.flag);
+    split_lo_kernel<true><<<lo_grid, 256, 0, h->stream>>>(v, v_rs, v_bs, v_lo, sk, nb, pp.flag);
+    h->launches += 2;
+    cudaError_t ce = cudaGetLastError();
+    if (ce == cudaSuccess)
+        ce = cudaFuncSetAttribute(attn_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (ce == cudaSuccess) {
-        attn_3xtf32_kernel<<<(unsigned)grid, NT, SMEM_BYTES, h->stream>>>(mq, mk, mv, pp);
+        attn_3xtf32_kernel<<<(unsigned)grid, NT, SMEM_BYTES, h->stream>>>(mq, mk, mv, mkl, mvl, pp);
         ce = cudaGetLastError();
     }
     *kernel_name = "attn_3xtf32_128x64";
