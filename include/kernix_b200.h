@@ -154,8 +154,18 @@ int kx_set_f64_variant(kx_handle *h, int variant);
  * 236-316) bit for bit.  Slower: no FMA, no split-K. */
 int kx_set_ordered_matmul(kx_handle *h, int ordered);
 int kx_ordered_matmul(const kx_handle *h);
-/* Wait for outstanding work on the handle's stream (Device::synchronize). */
+/* Wait for outstanding work on the handle's stream (Device::synchronize).
+ * Returns KX_E_TIMEOUT (once, then clears it) when a kernel's bounded
+ * device-side wait expired since the last call: such a kernel stops, frees its
+ * tensor memory and leaves its output unspecified instead of hanging. */
 int kx_synchronize(kx_handle *h, kx_error *err);
+/* Diagnostic, no counterpart in the reference: the next launch of the one-SM
+ * split-TF32 GEMM on this handle (variant KX_F32_3XTF32_1SM, K > 1024, or the
+ * automatic choice where it picks that kernel) issues no operand copies and
+ * bounds each of its waits by `wait_ns` (1 ms .. 2 s), so every wait expires
+ * and the call's kx_synchronize reports KX_E_TIMEOUT.  For exercising a
+ * caller's handling of that status; the output of that call is unspecified. */
+int kx_diag_expire_next_gemm(kx_handle *h, uint64_t wait_ns);
 
 /* ---- Device<T> buffers (device.rs:22-35) -------------------------------- */
 int kx_alloc(kx_handle *h, uint64_t bytes, void **out, kx_error *err);

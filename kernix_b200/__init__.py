@@ -99,6 +99,12 @@ class Handle:
         err = KxError()
         raise_for(lib.kx_synchronize(self._h, C.byref(err)), err)
 
+    def diag_expire_next_gemm(self, wait_ns: int) -> None:
+        """Diagnostic: the next one-SM split-TF32 GEMM on this handle issues no
+        copies and bounds its waits by ``wait_ns`` (1 ms .. 2 s), so they expire
+        and the next ``synchronize`` raises DeviceTimeout."""
+        raise_for(lib.kx_diag_expire_next_gemm(self._h, int(wait_ns)), None)
+
     @property
     def launches(self) -> int:
         return int(lib.kx_launch_count(self._h))

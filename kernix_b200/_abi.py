@@ -102,6 +102,7 @@ _SIGNATURES = {
     "kx_set_ordered_matmul": (C.c_int, [_vp, C.c_int]),
     "kx_ordered_matmul": (C.c_int, [_vp]),
     "kx_synchronize": (C.c_int, [_vp, _P(KxError)]),
+    "kx_diag_expire_next_gemm": (C.c_int, [_vp, C.c_uint64]),
     "kx_alloc": (C.c_int, [_vp, _u64, _P(_vp), _P(KxError)]),
     "kx_free": (C.c_int, [_vp, _vp]),
     "kx_upload": (C.c_int, [_vp, _vp, _vp, _u64, _P(KxError)]),

@@ -7,6 +7,7 @@
 
 #include "gemm_simt.cuh"
 #include "kx_internal.hpp"
+#include "tc_common.cuh"
 
 using namespace kx;
 
@@ -446,6 +447,13 @@ int kx_set_ordered_matmul(kx_handle *hh, int ordered) {
 }
 
 int kx_ordered_matmul(const kx_handle *hh) { return hh && hh->impl.ordered ? 1 : 0; }
+
+int kx_diag_expire_next_gemm(kx_handle *hh, uint64_t wait_ns) {
+    if (!hh) return KX_E_PARAM;
+    if (wait_ns < 1000000ull || wait_ns > tc::WAIT_NS) return KX_E_PARAM;
+    hh->impl.diag_wait_ns = wait_ns;
+    return KX_OK;
+}
 
 int kx_synchronize(kx_handle *hh, kx_error *err) {
     if (!hh) return set_err(err, KX_E_PARAM, "synchronize", "null handle");

@@ -48,6 +48,8 @@ struct TcParams {
     int nbatch;
     int a_batched, b_batched;   // 1 if the operand has its own batch coordinate
     uint32_t *status;
+    uint64_t wait_ns;           // bound of every mbarrier wait (WAIT_NS)
+    int idle_producer;          // diagnostic launch: no copies issued, so every wait expires
 };
 
 template <bool B_MN, int BN>
@@ -108,11 +110,11 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 
     if (warp == 0) {
         // ---- TMA producer ------------------------------------------------
-        if (lane == 0) {
+        if (lane == 0 && !p.idle_producer) {
             int issued = 0;   // k-tiles whose copies were issued
             for (int kt = 0; kt < ktiles && !s_fail; ++kt) {
                 const int s = kt % STAGES;
-                if (kt >= STAGES && !mbar_wait(&empty[s], ((kt / STAGES) - 1) & 1)) {
+                if (kt >= STAGES && !mbar_wait_for(&empty[s], ((kt / STAGES) - 1) & 1, p.wait_ns)) {
                     s_fail = 1;
                     break;
                 }
@@ -131,7 +133,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             // (the last k-tile issued into each stage).
             for (int s = 0; s < STAGES && s < issued; ++s) {
                 const int last = s + STAGES * ((issued - 1 - s) / STAGES);
-                mbar_wait(&full[s], (last / STAGES) & 1);
+                mbar_wait_for(&full[s], (last / STAGES) & 1, p.wait_ns);
             }
         }
     } else if (warp == 1) {
@@ -144,11 +146,11 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             for (int kt = 0; kt < ktiles; ++kt) {
                 const int s = kt % STAGES;
                 const int chunk = kt / KC, kin = kt % KC;
-                if (kin == 0 && chunk > 0 && (s_fail || !mbar_wait(chunk_empty, (chunk - 1) & 1))) {
+                if (kin == 0 && chunk > 0 && (s_fail || !mbar_wait_for(chunk_empty, (chunk - 1) & 1, p.wait_ns))) {
                     s_fail = 1;
                     break;
                 }
-                if (s_fail || !mbar_wait(&conv[s], (kt / STAGES) & 1)) {
+                if (s_fail || !mbar_wait_for(&conv[s], (kt / STAGES) & 1, p.wait_ns)) {
                     s_fail = 1;
                     break;
                 }
@@ -186,7 +188,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         int chunk = 0;
         for (int kt = 0; kt < ktiles; ++kt) {
             const int s = kt % STAGES;
-            if (s_fail || !mbar_wait(&full[s], (kt / STAGES) & 1)) {
+            if (s_fail || !mbar_wait_for(&full[s], (kt / STAGES) & 1, p.wait_ns)) {
                 s_fail = 1;
                 break;
             }
@@ -202,7 +204,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             if (lane == 0) mbar_arrive(&conv[s]);
             if (kt % KC == KC - 1 || kt == ktiles - 1) {
                 // Fold the finished chunk of hi*hi into the register sum.
-                if (!mbar_wait(chunk_full, chunk & 1)) {
+                if (!mbar_wait_for(chunk_full, chunk & 1, p.wait_ns)) {
                     s_fail = 1;
                     break;
                 }
@@ -389,6 +391,9 @@ int run_gemm_tc(Handle *h, const GemmParams<float> &p, const char **kernel_name)
     tp.a_batched = a_batched;
     tp.b_batched = b_batched;
     tp.status = h->flags + kStatusWord;
+    tp.wait_ns = h->diag_wait_ns ? h->diag_wait_ns : WAIT_NS;
+    tp.idle_producer = h->diag_wait_ns ? 1 : 0;
+    h->diag_wait_ns = 0;          // the diagnostic covers one launch
     cudaError_t ce;
     if (b_mn) {
         ce = bn == 224   ? launch_tc<true, 224>(h, ma, mb, tp, nb)

@@ -22,6 +22,10 @@ struct Handle {
     uint64_t launches = 0;
     const char *last_kernel = "none";
     int last_cuda_error = 0;
+    // Diagnostic (kx_diag_expire_next_gemm): nonzero makes the next one-SM
+    // split-TF32 GEMM launch issue no copies and bound its waits by this many
+    // nanoseconds, so that they expire.
+    uint64_t diag_wait_ns = 0;
 
     void *ws = nullptr;          // split-K partials
     uint64_t ws_bytes = 0;

@@ -55,8 +55,9 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
 }
-// Bounded wait for the phase with the given parity; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// Bounded wait for the phase with the given parity; false once `wait_ns`
+// nanoseconds have passed without it.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, uint64_t wait_ns) {
     const uint32_t a = smem_u32(bar);
     uint64_t deadline = 0;
     while (true) {
@@ -70,9 +71,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
             : "memory");
         if (done) return true;
         const uint64_t now = globaltimer();
-        if (deadline == 0) deadline = now + WAIT_NS;
+        if (deadline == 0) deadline = now + wait_ns;
         else if (now > deadline) return false;
     }
+}
+// Bounded wait for the phase with the given parity; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    return mbar_wait_for(bar, parity, WAIT_NS);
 }
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int c0, int c1, int c2,
                                             uint64_t *bar) {

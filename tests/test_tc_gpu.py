@@ -256,3 +256,36 @@ def test_tc_short_k_persistent(kx, torch_cuda):
     fin = np.isfinite(c).all(axis=1)
     assert fin[:5].all() and fin[6:4097].all()
     h.synchronize()
+
+
+def test_expired_waits_report_timeout_and_leave_the_handle_usable(kx, torch_cuda):
+    """The bounded-wait path: a diagnostic launch of the one-SM kernel issues no
+    copies and bounds its waits by 1 ms, so every wait expires.  The kernel
+    stops, frees its tensor memory and sets the status word; synchronize reports
+    DeviceTimeout once; the next products on the same handle are correct."""
+    from kernix_b200 import rng
+    torch = torch_cuda
+    h = kx.handle(0)
+    m, k, n = 256, 2048, 384                    # K > 1024: not the short-K kernel
+    a = rng.uniform(71, m * k, -1.0, 1.0).reshape(m, k)
+    b = rng.uniform(72, k * n, -1.0, 1.0).reshape(k, n)
+    da, db = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    out = torch.full((m, n), 7.0, device="cuda")
+    h.set_f32_variant(3)                         # one-SM split-TF32 tiles
+    try:
+        h.synchronize()
+        h.diag_expire_next_gemm(1_000_000)
+        kx.matmul_into(da, db, out)
+        assert h.last_kernel.startswith("tc_3xtf32_128x")
+        with pytest.raises(kx.DeviceTimeout):
+            h.synchronize()
+        h.synchronize()                          # reported once, then cleared
+        got = kx.matmul(da, db)
+        assert h.last_kernel.startswith("tc_3xtf32_128x")
+        h.synchronize()
+    finally:
+        h.set_f32_variant(0)
+    want, absum = oracle.gemm_dot2(oracle.View.of(a), oracle.View.of(b))
+    assert (np.abs(got.cpu().numpy().astype(np.float64) - want) <= 2e-6 * absum).all()
+    with pytest.raises(kx.InvalidParameter):
+        h.diag_expire_next_gemm(10)               # below 1 ms
