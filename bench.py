@@ -215,7 +215,7 @@ def run_ours(args, rank, world, local):
     rng.uniform(SEEDS["c5"][1], K * N, -1.0, 1.0, np.float32, out=b_host.numpy())
     a_buf = a_host.to(dev)
     b = b_host.to(dev).view(K, N)
-    push = gather in ("p2p", "p2p-ce")
+    push = gather == "p2p"
     push_mc = gather == "p2p-nvls"
     peer_out = PeerOutput(M, N, torch.float32, group, local) if push else None
     if rep is not None:
@@ -231,17 +231,18 @@ def run_ours(args, rank, world, local):
     streams = (torch.cuda.current_stream(dev), torch.cuda.Stream(dev)) if gather == "nccl" else None
     push_streams = None
     if push or push_mc:
-        push_streams = {r: torch.cuda.Stream(dev) for r in range(world) if r != rank}
-        push_streams["comm"] = torch.cuda.Stream(dev)
+        push_streams = {"comm": torch.cuda.Stream(dev)}
+
+    # this rank's rows of A in piece order (the local buffer, row stride 8704)
+    a_local = kx.TensorView(a_buf, (plan.pieces * plan.piece, K), (ROW_STRIDE, 1), 0)
 
     def step():
         if push_mc:
-            sharded_matmul_push_mc(pieces, b, rep, plan, rank, group, streams=push_streams)
+            sharded_matmul_push_mc(a_local, b, rep, plan, rank, group, streams=push_streams)
         elif rep is not None:
             sharded_matmul_replicated(pieces, b, rep, plan, rank, group)
         elif push:
-            sharded_matmul_push(pieces, b, peer_out, plan, rank, group, streams=push_streams,
-                                tail_kernel=gather == "p2p")
+            sharded_matmul_push(a_local, b, peer_out, plan, rank, group, streams=push_streams)
         else:
             sharded_matmul(pieces, b, c, plan, rank, group, streams=streams, scratch=scratch)
 
@@ -323,7 +324,7 @@ def run_ours(args, rank, world, local):
                            "none": "", "nvls": " + NVLS multicast stores from the GEMM epilogue",
                            "p2p-nvls": " + copy-engine push to peers, NVLS multicast store of the last piece",
                            "p2p": " + push to peers over CUDA IPC (copy engines, all-SM kernel for the last piece)",
-                           "p2p-ce": " + copy-engine push to peers (CUDA IPC)", "nccl": " + NCCL all-gather"}[gather],
+                           "nccl": " + NCCL all-gather"}[gather],
                        "l2": "inputs larger than L2 (A span 285 MB, B 268 MB)", "kernel": kname},
             "e2e": e2e,
             "gpu_launches": launches,
@@ -775,18 +776,18 @@ def run_workload(w, steps, warmup, rank=0, world=1, local=0, batch=0, size=0):
                                         "l2": "inputs larger than L2 (134 MB each, C 134 MB)"})
     elif w == "c3":
         total = batch or 16
-        if total % world:
-            raise SystemExit(f"c3: batch {total} does not split over {world} ranks")
-        nb = total // world
+        from kernix_b200.sharded import shard_window
+        b0, nb = shard_window(total, rank, world)       # this rank's batches (library plan)
         shape = (nb, 32, 2048, 128)
         cnt = int(np.prod(shape))
+        unit = 32 * 2048 * 128
         # Q, K and V are consecutive windows of one stream of total * 32 * 2048 * 128
-        # values each; this rank's batches start at rank * cnt inside each
+        # values each; this rank's batches start at b0 * unit inside each
         host = torch.empty(3 * cnt, dtype=torch.float32, pin_memory=True)
         hv = host.numpy()
         for j in range(3):
             rng.normal(SEEDS["c3"][0], cnt, 1.0, np.float32, out=hv[j * cnt:(j + 1) * cnt],
-                       start=j * cnt * world + rank * cnt)
+                       start=j * total * unit + b0 * unit)
         q = host[:cnt].view(shape).to(dev)
         k_ = host[cnt:2 * cnt].view(shape).to(dev)
         v_ = host[2 * cnt:].view(shape).to(dev)
@@ -861,12 +862,12 @@ def run_workload(w, steps, warmup, rank=0, world=1, local=0, batch=0, size=0):
         del o, q, k_, v_
     elif w == "c4":
         total = batch or 64
-        if total % world:
-            raise SystemExit(f"c4: batch {total} does not split over {world} ranks")
-        nb = total // world
+        from kernix_b200.sharded import shard_window
+        i0, nb = shard_window(total, rank, world)       # this rank's images (library plan)
         xn = nb * 128 * 56 * 56
         # this rank's images: a window of the input stream; weights on every rank
-        x_np = rng.uniform(SEEDS["c4"][0], xn, -1.0, 1.0, np.float32, start=rank * xn).reshape(nb, 128, 56, 56)
+        x_np = rng.uniform(SEEDS["c4"][0], xn, -1.0, 1.0, np.float32,
+                           start=i0 * 128 * 56 * 56).reshape(nb, 128, 56, 56)
         w_np = rng.normal(SEEDS["c4"][1], 256 * 128 * 9, math.sqrt(2.0 / 1152.0), np.float32).reshape(256, 128, 3, 3)
         x, wt = torch.from_numpy(x_np).to(dev), torch.from_numpy(w_np).to(dev)
         opts = kx.Conv2dOptions(padding=(1, 1))
@@ -925,10 +926,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--piece", type=int, default=0, help="rows per sharded piece (0: 512 when sharded)")
-    ap.add_argument("--gather", choices=["auto", "p2p", "p2p-ce", "p2p-nvls", "nvls", "nccl"], default="auto",
-                    help="gathered output: pushes into peers' C (copy engines while a piece computes, an "
-                         "all-SM kernel for the last piece; p2p-ce: copy engines only; p2p-nvls: NVLS "
-                         "multicast store for the last piece), NVLS multicast stores from the GEMM "
+    ap.add_argument("--gather", choices=["auto", "p2p", "p2p-nvls", "nvls", "nccl"], default="auto",
+                    help="gathered output: the library's row-sharded product pushing into peers' C (copy "
+                         "engines while a piece computes, an all-SM kernel for the last piece; p2p-nvls: an "
+                         "NVLS multicast store for the last piece), NVLS multicast stores from the GEMM "
                          "epilogue, or NCCL all-gather; auto = p2p-nvls where the node has NVLink "
                          "multicast, else p2p")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)

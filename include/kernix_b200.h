@@ -308,6 +308,39 @@ int kx_peer_broadcast(kx_handle *h, const void *src, void *const *dsts, int ndst
  * imported peer pointer.  Returns once the copy is enqueued. */
 int kx_copy_async(kx_handle *h, void *dst, const void *src, uint64_t bytes, void *stream, kx_error *err);
 
+/* ---- work split across the GPUs of one node ------------------------------ */
+/* Kernix splits a product over worker threads (CpuExecutor::matmul_into,
+ * execution.rs:188-233: chunks of output rows per worker).  Across GPUs each
+ * process owns one device; these plans are what every rank computes alike.
+ * kx_shard_window: the contiguous window [start, start + count) of `total`
+ * independent units (attention heads, images) that `rank` of `world` takes;
+ * the first total % world ranks take one more.  Host only. */
+int kx_shard_window(uint64_t total, uint32_t rank, uint32_t world, uint64_t *start, uint64_t *count);
+/* kx_row_piece: the row plan of a row-sharded product: the largest piece of
+ * at most `target_piece` rows that tiles M evenly over the ranks, and the
+ * number of pieces per rank.  Piece i of rank r is global rows
+ * [(i * world + r) * piece, + piece).  Host only. */
+int kx_row_piece(uint64_t m, uint32_t world, uint64_t target_piece, uint64_t *piece, uint64_t *pieces);
+/* One rank's share of the row-sharded f32 product out = A B over the GPUs of
+ * one node (one process and handle per GPU).  `a_local` holds this rank's rows
+ * of A, piece after piece ([pieces * piece, K], any strides: e.g. a strided
+ * slice of a wider buffer); `b` [K, N] is this rank's replica; `out` [M, N] is
+ * C-contiguous.  Each piece is multiplied into its global rows of `out`; with
+ * `peer_out` (world pointers: the start of every rank's `out` storage as
+ * mapped in this process by kx_ipc_import, this rank's entry unused) it is
+ * then written into the same rows of every peer's output -- by the copy
+ * engines while the next piece multiplies, and the last piece either through
+ * `out_mc`, the NVLink multicast address of `out`'s storage (one store, the
+ * NVSwitch delivers it to every rank), or, when that is null, by a kernel on
+ * all SMs.  Every rank's `out` has the same layout.  Returns once the work is
+ * enqueued on the handle's stream; when every rank's call has completed on its
+ * device (the caller orders that: a collective after the call, or
+ * kx_synchronize on every rank and a host barrier), every rank's `out` holds
+ * the whole product.  peer_out NULL: only this rank's rows are written. */
+int kx_matmul_rows_sharded_f32(kx_handle *h, const kx_tensor *a_local, const kx_tensor *b, const kx_tensor *out,
+                               uint32_t rank, uint32_t world, uint64_t piece, void *const *peer_out, void *out_mc,
+                               kx_error *err);
+
 /* ---- introspection ------------------------------------------------------ */
 /* Number of kernel launches this handle has issued since creation. */
 uint64_t kx_launch_count(const kx_handle *h);

@@ -137,6 +137,10 @@ _SIGNATURES = {
     "kx_ipc_close": (C.c_int, [_vp, _vp]),
     "kx_peer_broadcast": (C.c_int, [_vp, _vp, _P(_vp), C.c_int, C.c_uint64, _P(KxError)]),
     "kx_copy_async": (C.c_int, [_vp, _vp, _vp, C.c_uint64, _vp, _P(KxError)]),
+    "kx_shard_window": (C.c_int, [_u64, C.c_uint32, C.c_uint32, _P(_u64), _P(_u64)]),
+    "kx_row_piece": (C.c_int, [_u64, C.c_uint32, _u64, _P(_u64), _P(_u64)]),
+    "kx_matmul_rows_sharded_f32": (C.c_int, [_vp, _P(KxTensor), _P(KxTensor), _P(KxTensor), C.c_uint32, C.c_uint32,
+                                             _u64, _P(_vp), _vp, _P(KxError)]),
     "kx_launch_count": (C.c_uint64, [_vp]),
     "kx_last_kernel": (C.c_char_p, [_vp]),
     "kx_status_name": (C.c_char_p, [C.c_int]),

@@ -415,6 +415,14 @@ int kx_destroy(kx_handle *hh) {
         cudaFree(h.flags);
         for (auto &e : h.ev)
             if (e) cudaEventDestroy(e);
+        for (int r = 0; r < Handle::kMaxWorld; ++r) {
+            if (h.peer_stream[r]) {
+                cudaStreamSynchronize(h.peer_stream[r]);
+                cudaStreamDestroy(h.peer_stream[r]);
+            }
+            if (h.peer_done[r]) cudaEventDestroy(h.peer_done[r]);
+        }
+        if (h.peer_ready) cudaEventDestroy(h.peer_ready);
         if (h.h2d) cudaStreamDestroy(h.h2d);
         if (h.d2h) cudaStreamDestroy(h.d2h);
     }

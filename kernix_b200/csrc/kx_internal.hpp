@@ -38,6 +38,12 @@ struct Handle {
     // Host-hook pipeline: copy streams and per-piece events, created on first use.
     cudaStream_t h2d = nullptr, d2h = nullptr;
     static constexpr int kMaxPieces = 16;
+    // Row-sharded products (kx_sharded.cu): one copy stream per peer GPU and
+    // events to order them after a piece and before the end of the call.
+    static constexpr int kMaxWorld = 8;
+    cudaStream_t peer_stream[kMaxWorld] = {};
+    cudaEvent_t peer_ready = nullptr;
+    cudaEvent_t peer_done[kMaxWorld] = {};
     cudaEvent_t ev[3 * kMaxPieces + 2] = {};
 
     int cuda_fail(cudaError_t ce) {

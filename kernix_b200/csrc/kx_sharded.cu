@@ -1,0 +1,157 @@
+// Work split across the GPUs of one node, one process (and one handle) per GPU.
+//
+// Kernix splits a product over host threads inside one process:
+// CpuExecutor::matmul_into (crates/kernix-ops/src/execution.rs:188-233) gives
+// each worker a chunk of output rows.  Across GPUs each process owns its
+// device, so the split is a plan every rank computes the same way, and the one
+// exchange the row split needs -- every rank ending with the whole output --
+// is done by this library over NVLink:
+//
+//   * kx_shard_window: a contiguous window of a batch axis (independent
+//     units: attention heads, conv2d images); no exchange.
+//   * kx_row_piece: the block-cyclic row plan of a row-sharded product:
+//     global row block i * world + rank of `piece` rows is rank's piece i, so
+//     each rank's pieces interleave and piece i of all ranks fills one
+//     contiguous band of the output.
+//   * kx_matmul_rows_sharded_f32: one rank's share of the row-sharded product,
+//     each piece pushed into every peer's output as soon as it is computed:
+//     copy engines (one stream per peer) while the next piece multiplies, and
+//     for the last piece, with nothing left to overlap, either one store
+//     through an NVLink multicast address (the NVSwitch fans it out) or a
+//     kernel on all SMs writing to every peer.
+#include <algorithm>
+#include <cstring>
+
+#include "kx_internal.hpp"
+
+extern "C" int kx_matmul_f32(kx_handle *h, const kx_tensor *a, const kx_tensor *b, const kx_tensor *out,
+                             kx_error *err);
+extern "C" int kx_peer_broadcast(kx_handle *h, const void *src, void *const *dsts, int ndst, uint64_t bytes,
+                                 kx_error *err);
+
+namespace kx {
+namespace {
+
+constexpr int kMaxWorld = Handle::kMaxWorld;
+
+// The handle's peer streams and events, created on first use.
+bool push_streams(Handle *h) {
+    if (h->peer_ready) return true;
+    for (int r = 0; r < kMaxWorld; ++r) {
+        if (cudaStreamCreateWithFlags(&h->peer_stream[r], cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&h->peer_done[r], cudaEventDisableTiming) != cudaSuccess)
+            return false;
+    }
+    return cudaEventCreateWithFlags(&h->peer_ready, cudaEventDisableTiming) == cudaSuccess;
+}
+
+}  // namespace
+}  // namespace kx
+
+using namespace kx;
+
+extern "C" {
+
+int kx_shard_window(uint64_t total, uint32_t rank, uint32_t world, uint64_t *start, uint64_t *count) {
+    if (!start || !count || world == 0 || rank >= world) return KX_E_PARAM;
+    // the first total % world ranks take one unit more
+    const uint64_t base = total / world, extra = total % world;
+    *start = rank * base + std::min<uint64_t>(rank, extra);
+    *count = base + (rank < extra ? 1 : 0);
+    return KX_OK;
+}
+
+int kx_row_piece(uint64_t m, uint32_t world, uint64_t target_piece, uint64_t *piece, uint64_t *pieces) {
+    if (!piece || !pieces || world == 0 || m % world != 0 || target_piece == 0) return KX_E_PARAM;
+    // the largest piece <= target_piece that tiles M evenly across the ranks
+    const uint64_t per_rank = m / world;
+    uint64_t p = std::min<uint64_t>(target_piece, per_rank);
+    while (p > 1 && per_rank % p) --p;
+    if (p == 0) return KX_E_PARAM;
+    *piece = p;
+    *pieces = per_rank / p;
+    return KX_OK;
+}
+
+int kx_matmul_rows_sharded_f32(kx_handle *hh, const kx_tensor *a_local, const kx_tensor *b, const kx_tensor *out,
+                               uint32_t rank, uint32_t world, uint64_t piece, void *const *peer_out, void *out_mc,
+                               kx_error *err) {
+    static const char *kOp = "matmul_rows_sharded";
+    if (!hh) return set_err(err, KX_E_PARAM, kOp, "null handle");
+    Handle *h = &hh->impl;
+    if (world == 0 || world > kMaxWorld || rank >= world)
+        return set_err(err, KX_E_PARAM, kOp, "rank and world (1..8 GPUs)", rank, world);
+    if (!a_local || !out || a_local->rank != 2 || out->rank != 2)
+        return set_err(err, KX_E_PARAM, kOp, "rank-two local A and output");
+    const uint64_t m = out->dims[0], n = out->dims[1];
+    if (piece == 0 || m % ((uint64_t)world * piece) != 0)
+        return set_err(err, KX_E_PARAM, kOp, "piece rows must tile M over the ranks", m, piece);
+    const uint64_t pieces = m / ((uint64_t)world * piece);
+    if (a_local->dims[0] != pieces * piece)
+        return set_err(err, KX_E_LAYOUT, kOp, "local A must hold this rank's rows", a_local->dims[0], pieces * piece);
+    if (!is_c_contiguous(out))
+        return set_err(err, KX_E_LAYOUT, kOp, "output must be C-contiguous", KX_LAYOUT_OUTPUT_NOT_C_CONTIGUOUS);
+    DeviceGuard g(h->device);
+    if (!g.ok) return set_err(err, KX_E_NO_DEVICE, kOp, "cannot select device");
+    const bool push = peer_out != nullptr && world > 1;
+    if (push && !push_streams(h)) return set_err(err, KX_E_CUDA, kOp, "cannot create the push streams");
+    float *c = static_cast<float *>(out->data) + out->origin;
+    const uint64_t row_bytes = n * sizeof(float);
+    for (uint64_t i = 0; i < pieces; ++i) {
+        const uint64_t g0 = (i * world + rank) * piece;       // global rows of this piece
+        kx_tensor ap = *a_local;                               // local rows [i * piece, (i + 1) * piece)
+        ap.dims[0] = piece;
+        ap.origin = a_local->origin + (uint64_t)((int64_t)(i * piece) * a_local->strides[0]);
+        kx_tensor cp = *out;
+        cp.dims[0] = piece;
+        cp.origin = out->origin + g0 * n;
+        int rc = kx_matmul_f32(hh, &ap, b, &cp, err);
+        if (rc) return rc;
+        if (!push) continue;
+        const uint64_t off = g0 * row_bytes, bytes = piece * row_bytes;
+        const char *src = reinterpret_cast<const char *>(c) + off;
+        if (i + 1 == pieces) {
+            // the last piece: nothing left to overlap with
+            if (out_mc) {
+                rc = mc_copy(h, src, static_cast<char *>(out_mc) + out->origin * sizeof(float) + off, bytes);
+                if (rc) return cuda_err(err, h, kOp);
+            } else {
+                void *dsts[kMaxWorld];
+                int nd = 0;
+                for (uint32_t r = 0; r < world; ++r)
+                    if (r != rank) dsts[nd++] = static_cast<char *>(peer_out[r]) + out->origin * sizeof(float) + off;
+                rc = kx_peer_broadcast(hh, src, dsts, nd, bytes, err);
+                if (rc) return rc;
+            }
+            continue;
+        }
+        // earlier pieces: copy engines, one stream per peer, after the piece's GEMM
+        cudaError_t ce = cudaEventRecord(h->peer_ready, h->stream);
+        for (uint32_t r = 0; r < world && ce == cudaSuccess; ++r) {
+            if (r == rank) continue;
+            ce = cudaStreamWaitEvent(h->peer_stream[r], h->peer_ready, 0);
+            if (ce == cudaSuccess)
+                ce = cudaMemcpyAsync(static_cast<char *>(peer_out[r]) + out->origin * sizeof(float) + off, src, bytes,
+                                     cudaMemcpyDeviceToDevice, h->peer_stream[r]);
+        }
+        if (ce != cudaSuccess) {
+            h->cuda_fail(ce);
+            return cuda_err(err, h, kOp);
+        }
+    }
+    if (push) {
+        // the handle's stream completes only after every push has
+        for (uint32_t r = 0; r < world; ++r) {
+            if (r == rank) continue;
+            cudaError_t ce = cudaEventRecord(h->peer_done[r], h->peer_stream[r]);
+            if (ce == cudaSuccess) ce = cudaStreamWaitEvent(h->stream, h->peer_done[r], 0);
+            if (ce != cudaSuccess) {
+                h->cuda_fail(ce);
+                return cuda_err(err, h, kOp);
+            }
+        }
+    }
+    return KX_OK;
+}
+
+}  // extern "C"

@@ -18,13 +18,14 @@ Three ways to gather on GPUs:
   rank's C.  Each rank sends its rows once instead of once per peer, the
   gather overlaps the GEMM's later tiles, and one small all-reduce closes the
   step.
-* ``PeerOutput`` + ``sharded_matmul_push``: C lives in
-  library-allocated memory that every rank maps into every other rank (CUDA
-  IPC over NVLink).  After each piece's GEMM a rank pushes that piece's rows
-  straight into the same rows of every peer's C with the copy engines, one
-  stream per peer, so the exchange overlaps the next piece's GEMM without
-  taking any of its SMs; one 4-byte NCCL all-reduce at the end of the step
-  tells every rank that all pushes into its C have landed.
+* ``PeerOutput`` + ``sharded_matmul_push`` (or symmetric memory +
+  ``sharded_matmul_push_mc``): C lives in library-allocated memory that every
+  rank maps into every other rank (CUDA IPC over NVLink).  The library's
+  ``kx_matmul_rows_sharded_f32`` computes the rank's pieces and pushes each
+  into the same rows of every peer's C: with the copy engines, one stream per
+  peer, while the next piece multiplies, and the last piece with an all-SM
+  kernel (or one NVLink multicast store); one 4-byte NCCL all-reduce at the
+  end of the step tells every rank that all pushes into its C have landed.
 * ``sharded_matmul`` with ``all_gather_into_tensor`` per piece (NCCL; also the
   gloo path the CPU tests use).
 
@@ -69,14 +70,44 @@ class RowPlan:
 
 
 def plan_rows(m: int, world: int, target_piece: int = 512) -> RowPlan:
-    """Largest piece <= target_piece that tiles M evenly across ranks."""
+    """Largest piece <= target_piece that tiles M evenly across ranks
+    (``kx_row_piece``)."""
+    import ctypes as C
+
+    from . import _abi
     if m % world:
         raise ValueError(f"M={m} is not divisible by world={world}")
-    per_rank = m // world
-    piece = min(target_piece, per_rank)
-    while per_rank % piece:
-        piece -= 1
-    return RowPlan(m, world, piece)
+    piece, pieces = C.c_uint64(), C.c_uint64()
+    _abi.raise_for(_abi.lib.kx_row_piece(m, world, target_piece, C.byref(piece), C.byref(pieces)), None)
+    return RowPlan(m, world, int(piece.value))
+
+
+def shard_window(total: int, rank: int, world: int) -> tuple[int, int]:
+    """The contiguous window (start, count) of ``total`` independent units that
+    ``rank`` of ``world`` takes (``kx_shard_window``)."""
+    import ctypes as C
+
+    from . import _abi
+    start, count = C.c_uint64(), C.c_uint64()
+    _abi.raise_for(_abi.lib.kx_shard_window(total, rank, world, C.byref(start), C.byref(count)), None)
+    return int(start.value), int(count.value)
+
+
+def rows_sharded(a_local, b, out, plan: RowPlan, rank: int, peer_ptrs=None, out_mc: int = 0) -> None:
+    """``kx_matmul_rows_sharded_f32``: this rank's pieces of ``out`` = A B,
+    each pushed into the peers' outputs (``peer_ptrs``: every rank's output
+    storage as mapped here; ``out_mc``: its multicast address, used for the
+    last piece) -- enqueued on the current stream."""
+    import ctypes as C
+
+    from . import _abi, _bind, _descriptor
+    h = _bind(out)
+    da, db, do = _descriptor(a_local), _descriptor(b), _descriptor(out)
+    peers = (C.c_void_p * plan.world)(*peer_ptrs) if peer_ptrs is not None else None
+    err = _abi.KxError()
+    rc = _abi.lib.kx_matmul_rows_sharded_f32(h.ptr, C.byref(da), C.byref(db), C.byref(do), rank, plan.world,
+                                             plan.piece, peers, C.c_void_p(int(out_mc) or None), C.byref(err))
+    _abi.raise_for(rc, err)
 
 
 def sharded_matmul(a_pieces, b, c, plan: RowPlan, rank: int, group=None,
@@ -177,37 +208,6 @@ class PeerOutput:
             self.peers.append(int(pp.value))
         self.done = torch.zeros(1, dtype=torch.int32, device=f"cuda:{device}")
 
-    def push_rows(self, r0: int, r1: int, streams: dict) -> None:
-        """Enqueue copies of rows [r0, r1) of this rank's C into the same rows
-        of every peer's C, one copy per peer on ``streams[peer]``."""
-        import ctypes as C
-
-        from . import _abi
-        off, nbytes = r0 * self.row_bytes, (r1 - r0) * self.row_bytes
-        err = _abi.KxError()
-        for r, dst in enumerate(self.peers):
-            if r == self.rank:
-                continue
-            rc = _abi.lib.kx_copy_async(self.h.ptr, C.c_void_p(dst + off), C.c_void_p(self.ptr + off), nbytes,
-                                        C.c_void_p(streams[r].cuda_stream), C.byref(err))
-            _abi.raise_for(rc, err)
-
-    def broadcast_rows(self, r0: int, r1: int) -> None:
-        """Write rows [r0, r1) of this rank's C into every peer's C with a
-        kernel on the current stream (all SMs drive the NVLink stores)."""
-        import ctypes as C
-
-        import torch
-
-        from . import _abi
-        off, nbytes = r0 * self.row_bytes, (r1 - r0) * self.row_bytes
-        dsts = [p + off for r, p in enumerate(self.peers) if r != self.rank]
-        arr = (C.c_void_p * len(dsts))(*dsts)
-        self.h.set_stream(torch.cuda.current_stream(self.h.device))
-        err = _abi.KxError()
-        rc = _abi.lib.kx_peer_broadcast(self.h.ptr, C.c_void_p(self.ptr + off), arr, len(dsts), nbytes, C.byref(err))
-        _abi.raise_for(rc, err)
-
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (collective: every
         rank calls it, after its last push has completed)."""
@@ -230,46 +230,22 @@ class PeerOutput:
         self.peers = []
 
 
-def sharded_matmul_push(a_pieces, b, out: PeerOutput, plan: RowPlan, rank: int, group=None,
-                        matmul_into: Callable | None = None, streams: dict | None = None,
-                        tail_kernel: bool = True) -> None:
-    """Compute this rank's pieces into ``out.tensor`` and push each piece into
-    every peer's copy as soon as its GEMM has finished: with the copy engines
-    while a later piece computes, and (``tail_kernel``) with an all-SM copy
-    kernel for the last piece.
-
-    ``streams`` maps each peer rank to a CUDA stream for its pushes and key
-    ``"comm"`` to the stream of the closing all-reduce.  On return the work is
-    enqueued on the current stream: once it completes, every rank's C holds
-    the full product.
-    """
+def sharded_matmul_push(a_local, b, out: PeerOutput, plan: RowPlan, rank: int, group=None,
+                        streams: dict | None = None) -> None:
+    """This rank's pieces into ``out.tensor``, each pushed into every peer's
+    copy by the library (copy engines while a later piece computes, an all-SM
+    kernel for the last piece), then a 4-byte all-reduce on ``streams["comm"]``
+    that tells every rank all pushes into its C have landed.  ``a_local`` is
+    this rank's rows of A in piece order.  On return the work is enqueued on
+    the current stream."""
     import torch
     import torch.distributed as dist
 
-    if matmul_into is None:
-        from . import matmul_into as _mi
-        matmul_into = _mi
     c = out.tensor
     compute = torch.cuda.current_stream(c.device)
-    if streams is None:
-        streams = {r: torch.cuda.Stream(c.device) for r in range(plan.world) if r != rank}
-        streams["comm"] = torch.cuda.Stream(c.device)
-    peers = [r for r in range(plan.world) if r != rank]
-    for i in range(plan.pieces):
-        s, e = plan.rows_of(rank, i)
-        matmul_into(a_pieces[i], b, c[s:e])
-        if i == plan.pieces - 1 and tail_kernel:
-            # nothing left to overlap: every SM pushes the last piece
-            out.broadcast_rows(s, e)
-            continue
-        ev = torch.cuda.Event()
-        ev.record(compute)
-        for r in peers:
-            streams[r].wait_event(ev)
-        out.push_rows(s, e, streams)
-    comm = streams["comm"]
-    for r in peers:
-        comm.wait_stream(streams[r])
+    rows_sharded(a_local, b, c, plan, rank, peer_ptrs=out.peers)
+    comm = streams["comm"] if streams else torch.cuda.Stream(c.device)
+    comm.wait_stream(compute)
     with torch.cuda.stream(comm):
         dist.all_reduce(out.done, group=group)
     compute.wait_stream(comm)
@@ -299,39 +275,6 @@ class ReplicatedOutput:
         self.row_bytes = n * self.tensor.element_size()
         self.done = torch.zeros(1, dtype=torch.int32, device=f"cuda:{device}")
 
-    def push_rows(self, r0: int, r1: int, streams: dict) -> None:
-        """Copy-engine copies of rows [r0, r1) into every peer's buffer (the
-        symmetric-memory peer mappings), one per peer on ``streams[peer]``."""
-        import ctypes as C
-
-        from . import _abi, handle
-        h = handle(self.tensor.device.index)
-        off, nbytes = r0 * self.row_bytes, (r1 - r0) * self.row_bytes
-        src = self.tensor.data_ptr() + off
-        err = _abi.KxError()
-        for r, base in enumerate(self.hdl.buffer_ptrs):
-            if r == self.rank:
-                continue
-            rc = _abi.lib.kx_copy_async(h.ptr, C.c_void_p(int(base) + off), C.c_void_p(src), nbytes,
-                                        C.c_void_p(streams[r].cuda_stream), C.byref(err))
-            _abi.raise_for(rc, err)
-
-    def multicast_rows(self, r0: int, r1: int) -> None:
-        """Store rows [r0, r1) once through the multicast address (all SMs, on
-        the current stream); the NVSwitch delivers them to every rank."""
-        import ctypes as C
-
-        import torch
-
-        from . import _abi, handle
-        h = handle(self.tensor.device.index)
-        h.set_stream(torch.cuda.current_stream(self.tensor.device))
-        off, nbytes = r0 * self.row_bytes, (r1 - r0) * self.row_bytes
-        err = _abi.KxError()
-        rc = _abi.lib.kx_multicast_store(h.ptr, C.c_void_p(self.tensor.data_ptr() + off), C.c_void_p(self.mc + off),
-                                         nbytes, C.byref(err))
-        _abi.raise_for(rc, err)
-
     def close(self) -> None:
         self.hdl = None
         self.tensor = None
@@ -351,8 +294,8 @@ def sharded_matmul_replicated(a_pieces, b, out: ReplicatedOutput, plan: RowPlan,
     dist.all_reduce(out.done, group=group)
 
 
-def sharded_matmul_push_mc(a_pieces, b, out: ReplicatedOutput, plan: RowPlan, rank: int, group=None,
-                           matmul_into: Callable | None = None, streams: dict | None = None) -> None:
+def sharded_matmul_push_mc(a_local, b, out: ReplicatedOutput, plan: RowPlan, rank: int, group=None,
+                           streams: dict | None = None) -> None:
     """As ``sharded_matmul_push``, on symmetric memory: pieces before the last
     go to the peers' buffers on the copy engines while the next piece
     computes; the last piece is stored once through the NVLink multicast
@@ -360,26 +303,10 @@ def sharded_matmul_push_mc(a_pieces, b, out: ReplicatedOutput, plan: RowPlan, ra
     import torch
     import torch.distributed as dist
 
-    if matmul_into is None:
-        from . import matmul_into as _mi
-        matmul_into = _mi
     c = out.tensor
     compute = torch.cuda.current_stream(c.device)
-    peers = [r for r in range(plan.world) if r != rank]
-    for i in range(plan.pieces):
-        s, e = plan.rows_of(rank, i)
-        matmul_into(a_pieces[i], b, c[s:e])
-        if i == plan.pieces - 1:
-            out.multicast_rows(s, e)
-            continue
-        ev = torch.cuda.Event()
-        ev.record(compute)
-        for r in peers:
-            streams[r].wait_event(ev)
-        out.push_rows(s, e, streams)
-    comm = streams["comm"]
-    for r in peers:
-        comm.wait_stream(streams[r])
+    rows_sharded(a_local, b, c, plan, rank, peer_ptrs=[int(p) for p in out.hdl.buffer_ptrs], out_mc=out.mc)
+    comm = streams["comm"] if streams else torch.cuda.Stream(c.device)
     comm.wait_stream(compute)
     with torch.cuda.stream(comm):
         dist.all_reduce(out.done, group=group)

@@ -97,3 +97,22 @@ def test_stream_windows_reassemble_the_unsharded_inputs():
     assert np.array_equal(np.concatenate(parts), full_u)
     with pytest.raises(ValueError):
         rng.normal(7, 4, start=3)
+
+
+def test_library_plans_partition_the_work():
+    """kx_shard_window and kx_row_piece (host-only C entries): windows cover
+    every unit once, in rank order, differing in size by at most one; row
+    pieces tile M and are the largest divisor of the per-rank rows within the
+    target."""
+    from kernix_b200.sharded import shard_window
+    for total in (0, 1, 5, 16, 64, 67):
+        for world in (1, 2, 3, 4, 8):
+            wins = [shard_window(total, r, world) for r in range(world)]
+            assert sum(c for _, c in wins) == total
+            assert all(wins[r][0] + wins[r][1] == wins[r + 1][0] for r in range(world - 1))
+            assert max(c for _, c in wins) - min(c for _, c in wins) <= 1
+    for m, world, target in ((8192, 8, 512), (8192, 2, 512), (96, 3, 10), (8192, 8, 768)):
+        plan = plan_rows(m, world, target_piece=target)
+        per_rank = m // world
+        assert per_rank % plan.piece == 0 and plan.piece <= target
+        assert all(per_rank % p for p in range(plan.piece + 1, min(target, per_rank) + 1))
