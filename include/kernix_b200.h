@@ -17,6 +17,8 @@
  *   - softmax_temperature               crates/kernix-ops/src/ops/math_extra.rs:394-401,425-500,544-557
  *   - softmax                           crates/kernix-ops/src/ops/math.rs:398-465,531-536
  *   - CpuExecutor::matmul_into          crates/kernix-ops/src/execution.rs:149-240
+ *   - Tape::matmul backward (VJP)       crates/kernix/src/autograd.rs:622-690
+ *   - conv2d_backward                   crates/kernix-ops/src/neural.rs:379-430
  *   - the C bridge convention           crates/kernix-ops/src/accelerate.c:15-30
  *     (int status, caller-owned buffers, row-major output)
  *
@@ -236,6 +238,31 @@ int kx_softmax_f64(kx_handle *h, const kx_tensor *src, int64_t axis, const kx_te
  * allocates.  Synchronises the handle's stream (the nonfinite flag is read). */
 int kx_attention_f32(kx_handle *h, const kx_tensor *q, const kx_tensor *kt, const kx_tensor *v, float temperature,
                      const kx_tensor *out, kx_error *err);
+
+/* ---- backward products -------------------------------------------------- */
+/* Tape::matmul's vector-Jacobian products (crates/kernix/src/autograd.rs:
+ * 622-690): grad_a = grad . b^T and grad_b = a^T . grad on the operands with
+ * vectors as [1, k] / [k, 1], each summed back over the batch axes its operand
+ * was broadcast along.  `grad` has matmul(a, b)'s dims (else KX_E_PARAM,
+ * "gradient shape differs from forward output"); grad_a / grad_b (either may
+ * be NULL) are C-contiguous with a's / b's dims.  Transposed operands are read
+ * as strided views; a broadcast batch is reduced on the device. */
+int kx_matmul_backward_f32(kx_handle *h, const kx_tensor *a, const kx_tensor *b, const kx_tensor *grad,
+                           const kx_tensor *grad_a, const kx_tensor *grad_b, kx_error *err);
+int kx_matmul_backward_f64(kx_handle *h, const kx_tensor *a, const kx_tensor *b, const kx_tensor *grad,
+                           const kx_tensor *grad_a, const kx_tensor *grad_b, kx_error *err);
+/* conv2d_backward (crates/kernix-ops/src/neural.rs:379-430): grad_input and
+ * grad_weight (either may be NULL; C-contiguous, the input's / weight's dims)
+ * of conv2d(input, weight, options) for the output gradient `grad` (the
+ * forward output's dims, else KX_E_PARAM).  Every element adds the same
+ * contributions in the reference loop's order, product and sum rounded
+ * separately: the results equal the reference's bit for bit. */
+int kx_conv2d_backward_f32(kx_handle *h, const kx_tensor *input, const kx_tensor *weight, const kx_tensor *grad,
+                           const kx_conv2d_options *options, const kx_tensor *grad_input,
+                           const kx_tensor *grad_weight, kx_error *err);
+int kx_conv2d_backward_f64(kx_handle *h, const kx_tensor *input, const kx_tensor *weight, const kx_tensor *grad,
+                           const kx_conv2d_options *options, const kx_tensor *grad_input,
+                           const kx_tensor *grad_weight, kx_error *err);
 
 /* ---- host-buffer hooks (MatmulElement) ---------------------------------- */
 /* try_dense_matmul: C-order a[m*k], b[k*n] -> out[m*n] in HOST memory.

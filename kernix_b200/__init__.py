@@ -37,7 +37,7 @@ MAX_RANK = _abi.MAX_RANK
 
 __all__ = [
     "matmul", "matmul_reference", "matmul_shape", "matmul_into", "conv2d", "conv2d_reference", "conv2d_shape",
-    "Conv2dOptions", "attention", "attention_into", "softmax", "softmax_into", "softmax_temperature", "matmul_into_replicated", "conv2d_into", "softmax_temperature_into",
+    "Conv2dOptions", "attention", "attention_into", "matmul_backward", "conv2d_backward", "softmax", "softmax_into", "softmax_temperature", "matmul_into_replicated", "conv2d_into", "softmax_temperature_into",
     "MatrixInput", "try_dense_matmul", "try_strided_matmul", "TensorView", "CudaExecutor", "Handle",
     "handle", "OpsError", "InvalidRank", "ContractDimensionMismatch", "BroadcastIncompatible",
     "ElementCountOverflow", "DimensionOverflow", "LayoutError", "InvalidParameter", "ExactRank",
@@ -346,6 +346,40 @@ def conv2d_reference(x, w, options: Conv2dOptions = Conv2dOptions()):
     (neural.rs:188-198, 341-357), bitwise equal to Kernix's CPU result."""
     with _Ordered(_bind(x)):
         return conv2d(x, w, options)
+
+
+# ---------------------------------------------------------------------------
+# backward products
+# ---------------------------------------------------------------------------
+def matmul_backward(a, b, grad, need_a: bool = True, need_b: bool = True):
+    """Tape::matmul's VJP (autograd.rs:622-690): (grad . b^T, a^T . grad), each
+    summed back over the batch axes its operand was broadcast along; a
+    gradient not asked for is None."""
+    fn = _fn("kx_matmul_backward", a.dtype)
+    h = _bind(a)
+    da = _empty(tuple(a.shape), a.dtype, a.device) if need_a else None
+    db = _empty(tuple(b.shape), b.dtype, b.device) if need_b else None
+    err = KxError()
+    ta, tb, tg = _descriptor(a), _descriptor(b), _descriptor(grad)
+    oa = C.byref(_descriptor(da)) if da is not None else None
+    ob = C.byref(_descriptor(db)) if db is not None else None
+    raise_for(fn(h.ptr, C.byref(ta), C.byref(tb), C.byref(tg), oa, ob, C.byref(err)), err)
+    return da, db
+
+
+def conv2d_backward(x, w, grad, options: Conv2dOptions = Conv2dOptions()):
+    """conv2d_backward (neural.rs:379-430): (grad_input, grad_weight), bit for
+    bit the reference loop's sums."""
+    fn = _fn("kx_conv2d_backward", x.dtype)
+    h = _bind(x)
+    dx = _empty(tuple(x.shape), x.dtype, x.device)
+    dw = _empty(tuple(w.shape), w.dtype, w.device)
+    err = KxError()
+    o = options.to_c()
+    tx, tw, tg, ox, ow = (_descriptor(t) for t in (x, w, grad, dx, dw))
+    raise_for(fn(h.ptr, C.byref(tx), C.byref(tw), C.byref(tg), C.byref(o), C.byref(ox), C.byref(ow), C.byref(err)),
+              err)
+    return dx, dw
 
 
 # ---------------------------------------------------------------------------

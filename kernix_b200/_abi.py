@@ -122,6 +122,14 @@ _SIGNATURES = {
                                    _P(KxError)]),
     "kx_softmax_f32": (C.c_int, [_vp, _P(KxTensor), C.c_int64, _P(KxTensor), _P(KxError)]),
     "kx_softmax_f64": (C.c_int, [_vp, _P(KxTensor), C.c_int64, _P(KxTensor), _P(KxError)]),
+    "kx_matmul_backward_f32": (C.c_int, [_vp, _P(KxTensor), _P(KxTensor), _P(KxTensor), _P(KxTensor),
+                                         _P(KxTensor), _P(KxError)]),
+    "kx_matmul_backward_f64": (C.c_int, [_vp, _P(KxTensor), _P(KxTensor), _P(KxTensor), _P(KxTensor),
+                                         _P(KxTensor), _P(KxError)]),
+    "kx_conv2d_backward_f32": (C.c_int, [_vp, _P(KxTensor), _P(KxTensor), _P(KxTensor), _P(KxConv2dOptions),
+                                         _P(KxTensor), _P(KxTensor), _P(KxError)]),
+    "kx_conv2d_backward_f64": (C.c_int, [_vp, _P(KxTensor), _P(KxTensor), _P(KxTensor), _P(KxConv2dOptions),
+                                         _P(KxTensor), _P(KxTensor), _P(KxError)]),
     "kx_try_dense_matmul_f32": (C.c_int, [_vp, _vp, _u64, _vp, _u64, _vp, _u64, _u64, _u64, _u64]),
     "kx_try_dense_matmul_f64": (C.c_int, [_vp, _vp, _u64, _vp, _u64, _vp, _u64, _u64, _u64, _u64]),
     "kx_try_strided_matmul_f32": (C.c_int, [_vp, _P(KxMatrix), _P(KxMatrix), _vp, _u64]),

@@ -412,6 +412,7 @@ int kx_destroy(kx_handle *hh) {
         cudaFree(h.ws);
         for (auto &s : h.stage) cudaFree(s);
         cudaFree(h.attn);
+        cudaFree(h.bwd);
         cudaFree(h.flags);
         for (auto &e : h.ev)
             if (e) cudaEventDestroy(e);

@@ -33,6 +33,8 @@ struct Handle {
     uint64_t stage_bytes[3] = {0, 0, 0};
     void *attn = nullptr;        // scores and probabilities of the composed attention path
     uint64_t attn_bytes = 0;
+    void *bwd = nullptr;         // full-batch gradients before their broadcast sum (kx_backward.cu)
+    uint64_t bwd_bytes = 0;
     uint32_t *flags = nullptr;   // device status words (nonfinite index, timeouts)
     static constexpr int kFlagWords = 64;
     // Host-hook pipeline: copy streams and per-piece events, created on first use.

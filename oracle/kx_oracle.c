@@ -294,3 +294,40 @@ int kxo_openmp_threads(void) {
     return 1;
 #endif
 }
+
+/* ------------------------------------------------------------------------ */
+/* conv2d_backward (crates/kernix-ops/src/neural.rs:379-430): for every       */
+/* output gradient element in C order (n, co, oy, ox) and every tap          */
+/* (ci, ky, kx) inside the padded input, dx[n, g*cg+ci, y, x] += dy * w and   */
+/* dw[co, ci, ky, kx] += dy * x, separately rounded (no FMA).  Same geometry  */
+/* arguments as kxo_conv2d_reference; dx and dw must be zeroed by the caller. */
+/* ------------------------------------------------------------------------ */
+#define CONV_BWD(NAME, T)                                                                               \
+    void NAME(const T *x, const int64_t *xd, const int64_t *xs, const T *w, const int64_t *wd,             \
+              const int64_t *ws, const T *dy, const int64_t *yd, T *dx, T *dw, const int64_t *opt) {      \
+        const int64_t sy = opt[0], sx = opt[1], py = opt[2], px = opt[3], dly = opt[4], dlx = opt[5];     \
+        const int64_t groups = opt[6], cg = wd[1], kh = wd[2], kw = wd[3];                                \
+        const int64_t cpg = yd[1] / groups;                                                               \
+        for (int64_t n = 0; n < yd[0]; ++n)                                                               \
+            for (int64_t co = 0; co < yd[1]; ++co)                                                        \
+                for (int64_t oy = 0; oy < yd[2]; ++oy)                                                    \
+                    for (int64_t ox = 0; ox < yd[3]; ++ox) {                                              \
+                        const T g = dy[((n * yd[1] + co) * yd[2] + oy) * yd[3] + ox];                     \
+                        const int64_t grp = co / cpg;                                                     \
+                        for (int64_t ci = 0; ci < cg; ++ci)                                               \
+                            for (int64_t ky = 0; ky < kh; ++ky)                                           \
+                                for (int64_t kx = 0; kx < kw; ++kx) {                                     \
+                                    const int64_t y = oy * sy + ky * dly - py, xx = ox * sx + kx * dlx - px; \
+                                    if (y < 0 || y >= xd[2] || xx < 0 || xx >= xd[3]) continue;           \
+                                    const int64_t c = grp * cg + ci;                                      \
+                                    const int64_t ai = ((n * xd[1] + c) * xd[2] + y) * xd[3] + xx;        \
+                                    const int64_t wi = ((co * wd[1] + ci) * kh + ky) * kw + kx;           \
+                                    const T wv = w[co * ws[0] + ci * ws[1] + ky * ws[2] + kx * ws[3]];    \
+                                    const T xv = x[n * xs[0] + c * xs[1] + y * xs[2] + xx * xs[3]];       \
+                                    dx[ai] = dx[ai] + g * wv;                                             \
+                                    dw[wi] = dw[wi] + g * xv;                                             \
+                                }                                                                         \
+                    }                                                                                     \
+    }
+CONV_BWD(kxo_conv2d_backward_f32, float)
+CONV_BWD(kxo_conv2d_backward_f64, double)

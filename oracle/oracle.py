@@ -50,6 +50,7 @@ def _load() -> C.CDLL:
         getattr(lib, f"kxo_gemm_dot2_{t}").argtypes = [vp, i64, i64, vp, i64, i64, vp, vp, i64, i64, i64, C.c_int]
         getattr(lib, f"kxo_conv2d_reference_{t}").argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp]
         getattr(lib, f"kxo_conv2d_dot2_{t}").argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, C.c_int]
+        getattr(lib, f"kxo_conv2d_backward_{t}").argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
         getattr(lib, f"kxo_softmax_rows_{t}").argtypes = [vp, vp, i64, i64, C.c_float if t == "f32" else dbl]
         getattr(lib, f"kxo_softmax_rows_{t}").restype = i64
         getattr(lib, f"kxo_engine_gemm_{t}").argtypes = [vp, i64, i64, vp, i64, i64, vp, i64, i64, i64, C.c_int]
@@ -371,3 +372,50 @@ def attention_truth(q: np.ndarray, k: np.ndarray, v: np.ndarray, temperature: fl
         absv.append(p @ np.abs(vb))
         sabs.append(ab.max(axis=1))
     return np.stack(outs), np.stack(absv), np.stack(sabs)
+
+
+# ---------------------------------------------------------------------------
+# backward products
+# ---------------------------------------------------------------------------
+def conv2d_backward(x: View, w: View, dy: np.ndarray, stride=(1, 1), padding=(0, 0), dilation=(1, 1), groups=1):
+    """conv2d_backward (neural.rs:379-430): (dx, dw) by the reference's loop,
+    every contribution `dy * w` / `dy * x` added separately rounded."""
+    yd, xd, xs, wd, ws, yda, opt = _conv_args(x, w, stride, padding, dilation, groups)
+    if list(dy.shape) != list(yd):
+        raise OracleError("InvalidParameter", parameter="gradient shape differs from forward output")
+    dx = np.zeros(x.dims, dtype=x.dtype)
+    dw = np.zeros(w.dims, dtype=x.dtype)
+    if dy.size:
+        g = np.ascontiguousarray(dy, dtype=x.dtype)
+        getattr(lib, f"kxo_conv2d_backward_{_t(x.dtype)}")(x.ptr(), _p(xd), _p(xs), w.ptr(), _p(wd), _p(ws), _p(g),
+                                                           _p(yda), _p(dx), _p(dw), _p(opt))
+    return dx, dw
+
+
+def _unbroadcast(full: np.ndarray, dims) -> np.ndarray:
+    """Sum a gradient over the batch axes its operand was broadcast along
+    (missing leading axes and axes of extent 1), to the operand's dims."""
+    lead = full.ndim - len(dims)
+    out = full.sum(axis=tuple(range(lead))) if lead else full
+    axes = tuple(i for i, d in enumerate(dims) if d == 1 and out.shape[i] != 1)
+    if axes:
+        out = out.sum(axis=axes, keepdims=True)
+    return out.reshape(dims)
+
+
+def matmul_backward(a: np.ndarray, b: np.ndarray, g: np.ndarray):
+    """Tape::matmul's VJP (crates/kernix/src/autograd.rs:622-690) in float64:
+    dA = G B^T and dB = A^T G on the vector-extended operands, each summed
+    back over the batch axes its operand was broadcast along.  Exact for
+    dyadic data whose sums stay within 53 bits."""
+    out_dims, _, (av, bv, _, _, m, k, n) = matmul_shape(a.shape, b.shape)
+    if list(g.shape) != list(out_dims):
+        raise OracleError("InvalidParameter", parameter="gradient shape differs from forward output")
+    a2 = a.astype(np.float64).reshape((1, k) if av else a.shape)
+    b2 = b.astype(np.float64).reshape((k, 1) if bv else b.shape)
+    seed = g.astype(np.float64).reshape(tuple(out_dims[:len(out_dims) - (not av) - (not bv)]) + (m, n))
+    da = np.matmul(seed, np.swapaxes(b2, -1, -2))
+    db = np.matmul(np.swapaxes(a2, -1, -2), seed)
+    da = _unbroadcast(da, (1, k) if av else a.shape).reshape(a.shape)
+    db = _unbroadcast(db, (k, 1) if bv else b.shape).reshape(b.shape)
+    return da, db

@@ -208,3 +208,41 @@ def test_parallel_ordered_equals_serial():
     ser = oracle.dense_matmul(a.reshape(-1), b.reshape(-1), 129, 67, 33).reshape(129, 33)
     par = oracle.gemm_ordered_par(oracle.View.of(a), oracle.View.of(b), threads=4)
     assert np.array_equal(ser, par)
+
+
+def test_conv2d_backward_oracle_central_differences():
+    """grouped_dilated_padded_convolution_gradients (neural_vision_tests.rs:46-79)
+    on the oracle's restatement of conv2d_backward (neural.rs:379-430)."""
+    def generated(dims):
+        n = int(np.prod(dims))
+        return ((np.arange(n) * 7 % 19 - 9.0) / 10.0).reshape(dims)
+    x, w = generated((1, 2, 4, 5)), generated((2, 1, 2, 2))
+    o = dict(groups=2, padding=(1, 1), stride=(2, 1), dilation=(2, 1))
+    y = oracle.conv2d_reference(oracle.View.of(x), oracle.View.of(w), **o)
+    dx, dw = oracle.conv2d_backward(oracle.View.of(x), oracle.View.of(w), y, **o)
+
+    def objective(xx, ww):
+        yy = oracle.conv2d_reference(oracle.View.of(xx), oracle.View.of(ww), **o)
+        return float((yy * yy / 2.0).sum())
+    h = 1e-5
+    for arr, grad, first in ((x, dx, True), (w, dw, False)):
+        flat = grad.reshape(-1)
+        for i in range(arr.size):
+            p, q = arr.copy().reshape(-1), arr.copy().reshape(-1)
+            p[i] += h
+            q[i] -= h
+            fp = objective(p.reshape(arr.shape), w) if first else objective(x, p.reshape(arr.shape))
+            fq = objective(q.reshape(arr.shape), w) if first else objective(x, q.reshape(arr.shape))
+            fd = (fp - fq) / (2 * h)
+            assert abs(flat[i] - fd) <= 2e-7 * (1 + abs(flat[i]) + abs(fd))
+
+
+def test_matmul_backward_oracle_known_answers():
+    """large_matmul_gradients_use_positive_transpose_kernels_without_changing_the_api
+    (autograd_tensor_tests.rs:637-668) on the oracle's VJP restatement."""
+    for m, k, n in ((65, 67, 69), (128, 32, 128)):
+        a = ((np.arange(m * k) % 23) / 16.0 - 0.5).reshape(m, k)
+        b = ((np.arange(k * n) % 13) / 8.0 - 0.5).reshape(k, n)
+        da, db = oracle.matmul_backward(a, b, np.ones((m, n)))
+        assert np.array_equal(da, np.broadcast_to(b.sum(axis=1), (m, k)))
+        assert np.array_equal(db, np.broadcast_to(a.sum(axis=0)[:, None], (k, n)))
