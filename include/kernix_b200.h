@@ -16,6 +16,7 @@
  *   - neural::conv2d / ConvGeometry     crates/kernix-ops/src/neural.rs:22-133,177-183
  *   - softmax_temperature               crates/kernix-ops/src/ops/math_extra.rs:394-401,425-500,544-557
  *   - softmax                           crates/kernix-ops/src/ops/math.rs:398-465,531-536
+ *   - tensordot                         crates/kernix-ops/src/ops/linalg_extra.rs:164-276
  *   - CpuExecutor::matmul_into          crates/kernix-ops/src/execution.rs:149-240
  *   - Tape::matmul backward (VJP)       crates/kernix/src/autograd.rs:622-690
  *   - conv2d_backward                   crates/kernix-ops/src/neural.rs:379-430
@@ -59,7 +60,9 @@ typedef enum kx_status {
     KX_E_CUDA = 13,             /* a CUDA runtime call failed (kx_error.cuda_error) */
     KX_E_NO_DEVICE = 14,        /* no usable sm_100 device for this handle */
     KX_E_TIMEOUT = 15,          /* a bounded device-side wait expired */
-    KX_E_UNSUPPORTED = 16       /* valid request outside this library's scope (e.g. rank > 8) */
+    KX_E_UNSUPPORTED = 16,      /* valid request outside this library's scope (e.g. rank > 8) */
+    KX_E_AXES_MISMATCH = 17,    /* OpsError::ContractAxesMismatch {left, right} (axis counts) */
+    KX_E_DUPLICATE_AXIS = 18    /* OpsError::DuplicateAxis {axis} */
 } kx_status;
 
 /* Sub-codes in kx_error.values[0] for KX_E_LAYOUT (layout/geometry.rs:40-80, affine.rs:186-199). */
@@ -238,6 +241,19 @@ int kx_softmax_f64(kx_handle *h, const kx_tensor *src, int64_t axis, const kx_te
  * allocates.  Synchronises the handle's stream (the nonfinite flag is read). */
 int kx_attention_f32(kx_handle *h, const kx_tensor *q, const kx_tensor *kt, const kx_tensor *v, float temperature,
                      const kx_tensor *out, kx_error *err);
+
+/* tensordot (ops/linalg_extra.rs:164-276): out (C-contiguous; left's free
+ * axes then right's, in order) = the contraction of a and b over the axis
+ * pairs (a_axes[i], b_axes[i]) (negative axes count from the end).  Errors in
+ * the reference order: KX_E_AXES_MISMATCH (na != nb), then per pair
+ * KX_E_AXIS (left, then right), KX_E_DUPLICATE_AXIS, KX_E_CONTRACT.  One GEMM
+ * over [free(a), contracted] x [contracted, free(b)], on strided views when
+ * the axes nest (else after a gather into the handle's buffer); in ordered
+ * mode the sums equal the reference's bit for bit. */
+int kx_tensordot_f32(kx_handle *h, const kx_tensor *a, const kx_tensor *b, const int64_t *a_axes, uint32_t na,
+                     const int64_t *b_axes, uint32_t nb, const kx_tensor *out, kx_error *err);
+int kx_tensordot_f64(kx_handle *h, const kx_tensor *a, const kx_tensor *b, const int64_t *a_axes, uint32_t na,
+                     const int64_t *b_axes, uint32_t nb, const kx_tensor *out, kx_error *err);
 
 /* ---- backward products -------------------------------------------------- */
 /* Tape::matmul's vector-Jacobian products (crates/kernix/src/autograd.rs:

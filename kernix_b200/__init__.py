@@ -27,8 +27,8 @@ import numpy as np
 
 from . import _abi
 from ._abi import (  # noqa: F401  (re-exported error types)
-    AxisOutOfBounds, BroadcastIncompatible, CapacityOverflow, ContractDimensionMismatch, CudaError, DeviceTimeout,
-    DimensionOverflow, ElementCountOverflow, ExactRank, InvalidParameter, InvalidRank, KxConv2dOptions,
+    AxisOutOfBounds, BroadcastIncompatible, CapacityOverflow, ContractAxesMismatch, ContractDimensionMismatch,
+    CudaError, DeviceTimeout, DimensionOverflow, DuplicateAxis, ElementCountOverflow, ExactRank, InvalidParameter, InvalidRank, KxConv2dOptions,
     KxError, KxMatrix, KxTensor, LayoutError, NoDevice, NonFiniteInput, OpsError, OverlappingOutput,
     Unsupported, raise_for, u64_array)
 
@@ -37,12 +37,12 @@ MAX_RANK = _abi.MAX_RANK
 
 __all__ = [
     "matmul", "matmul_reference", "matmul_shape", "matmul_into", "conv2d", "conv2d_reference", "conv2d_shape",
-    "Conv2dOptions", "attention", "attention_into", "matmul_backward", "conv2d_backward", "softmax", "softmax_into", "softmax_temperature", "matmul_into_replicated", "conv2d_into", "softmax_temperature_into",
+    "Conv2dOptions", "attention", "attention_into", "matmul_backward", "conv2d_backward", "tensordot", "softmax", "softmax_into", "softmax_temperature", "matmul_into_replicated", "conv2d_into", "softmax_temperature_into",
     "MatrixInput", "try_dense_matmul", "try_strided_matmul", "TensorView", "CudaExecutor", "Handle",
     "handle", "OpsError", "InvalidRank", "ContractDimensionMismatch", "BroadcastIncompatible",
     "ElementCountOverflow", "DimensionOverflow", "LayoutError", "InvalidParameter", "ExactRank",
     "NonFiniteInput", "AxisOutOfBounds", "OverlappingOutput", "CudaError", "NoDevice", "Unsupported",
-    "CapacityOverflow",
+    "CapacityOverflow", "ContractAxesMismatch", "DuplicateAxis",
 ]
 
 
@@ -346,6 +346,26 @@ def conv2d_reference(x, w, options: Conv2dOptions = Conv2dOptions()):
     (neural.rs:188-198, 341-357), bitwise equal to Kernix's CPU result."""
     with _Ordered(_bind(x)):
         return conv2d(x, w, options)
+
+
+def tensordot(a, b, a_axes: Sequence[int], b_axes: Sequence[int]):
+    """tensordot (ops/linalg_extra.rs:164-276): contract the axis pairs
+    (a_axes[i], b_axes[i]); the result has a's free axes then b's.  One GEMM
+    on the device (bit for bit the reference's sums in ordered mode)."""
+    ra, rb = len(a.shape), len(b.shape)
+    fa = [i for i in range(ra) if i not in {(x + ra if x < 0 else x) for x in a_axes}]
+    fb = [i for i in range(rb) if i not in {(x + rb if x < 0 else x) for x in b_axes}]
+    dims = [a.shape[i] for i in fa] + [b.shape[i] for i in fb]
+    ok = len(a_axes) == len(b_axes) and all(-ra <= x < ra for x in a_axes) and all(-rb <= x < rb for x in b_axes)
+    out = _empty(tuple(dims) if ok else (), a.dtype, a.device)
+    fn = _fn("kx_tensordot", a.dtype)
+    h = _bind(a)
+    la = (C.c_int64 * max(1, len(a_axes)))(*[int(x) for x in a_axes])
+    lb = (C.c_int64 * max(1, len(b_axes)))(*[int(x) for x in b_axes])
+    err = KxError()
+    ta, tb, to = _descriptor(a), _descriptor(b), _descriptor(out)
+    raise_for(fn(h.ptr, C.byref(ta), C.byref(tb), la, len(a_axes), lb, len(b_axes), C.byref(to), C.byref(err)), err)
+    return out
 
 
 # ---------------------------------------------------------------------------

@@ -30,6 +30,8 @@ KX_E_CUDA = 13
 KX_E_NO_DEVICE = 14
 KX_E_TIMEOUT = 15
 KX_E_UNSUPPORTED = 16
+KX_E_AXES_MISMATCH = 17
+KX_E_DUPLICATE_AXIS = 18
 
 # kx_layout_error sub-codes
 LAYOUT_ERRORS = {
@@ -122,6 +124,10 @@ _SIGNATURES = {
                                    _P(KxError)]),
     "kx_softmax_f32": (C.c_int, [_vp, _P(KxTensor), C.c_int64, _P(KxTensor), _P(KxError)]),
     "kx_softmax_f64": (C.c_int, [_vp, _P(KxTensor), C.c_int64, _P(KxTensor), _P(KxError)]),
+    "kx_tensordot_f32": (C.c_int, [_vp, _P(KxTensor), _P(KxTensor), _P(C.c_int64), C.c_uint32, _P(C.c_int64),
+                                   C.c_uint32, _P(KxTensor), _P(KxError)]),
+    "kx_tensordot_f64": (C.c_int, [_vp, _P(KxTensor), _P(KxTensor), _P(C.c_int64), C.c_uint32, _P(C.c_int64),
+                                   C.c_uint32, _P(KxTensor), _P(KxError)]),
     "kx_matmul_backward_f32": (C.c_int, [_vp, _P(KxTensor), _P(KxTensor), _P(KxTensor), _P(KxTensor),
                                          _P(KxTensor), _P(KxError)]),
     "kx_matmul_backward_f64": (C.c_int, [_vp, _P(KxTensor), _P(KxTensor), _P(KxTensor), _P(KxTensor),
@@ -258,6 +264,16 @@ class Unsupported(OpsError):
     status = KX_E_UNSUPPORTED
 
 
+class ContractAxesMismatch(OpsError):
+    """OpsError::ContractAxesMismatch {left, right}: axis-count mismatch."""
+    status = KX_E_AXES_MISMATCH
+
+
+class DuplicateAxis(OpsError):
+    """OpsError::DuplicateAxis {axis}."""
+    status = KX_E_DUPLICATE_AXIS
+
+
 class CapacityOverflow(OpsError):
     """StorageError::CapacityOverflow {len, element_size} (kernix-core
     storage/error.rs:23-30): an output allocation whose byte size exceeds
@@ -311,6 +327,10 @@ def raise_for(rc: int, err: KxError | None) -> None:
         raise DeviceTimeout(msg)
     if rc == KX_E_UNSUPPORTED:
         raise Unsupported(msg)
+    if rc == KX_E_AXES_MISMATCH:
+        raise ContractAxesMismatch(msg, left=v[0], right=v[1])
+    if rc == KX_E_DUPLICATE_AXIS:
+        raise DuplicateAxis(msg, axis=v[0])
     raise OpsError(msg, status=rc)
 
 

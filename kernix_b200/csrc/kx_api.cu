@@ -413,6 +413,7 @@ int kx_destroy(kx_handle *hh) {
         for (auto &s : h.stage) cudaFree(s);
         cudaFree(h.attn);
         cudaFree(h.bwd);
+        cudaFree(h.perm);
         cudaFree(h.flags);
         for (auto &e : h.ev)
             if (e) cudaEventDestroy(e);
@@ -615,6 +616,8 @@ const char *kx_status_name(int status) {
         case KX_E_NO_DEVICE: return "KX_E_NO_DEVICE";
         case KX_E_TIMEOUT: return "KX_E_TIMEOUT";
         case KX_E_UNSUPPORTED: return "KX_E_UNSUPPORTED";
+        case KX_E_AXES_MISMATCH: return "KX_E_AXES_MISMATCH";
+        case KX_E_DUPLICATE_AXIS: return "KX_E_DUPLICATE_AXIS";
         default: return "KX_UNKNOWN";
     }
 }

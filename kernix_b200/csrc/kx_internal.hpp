@@ -35,6 +35,8 @@ struct Handle {
     uint64_t attn_bytes = 0;
     void *bwd = nullptr;         // full-batch gradients before their broadcast sum (kx_backward.cu)
     uint64_t bwd_bytes = 0;
+    void *perm = nullptr;        // tensordot operands gathered into GEMM order (kx_tensordot.cu)
+    uint64_t perm_bytes = 0;
     uint32_t *flags = nullptr;   // device status words (nonfinite index, timeouts)
     static constexpr int kFlagWords = 64;
     // Host-hook pipeline: copy streams and per-piece events, created on first use.

@@ -419,3 +419,39 @@ def matmul_backward(a: np.ndarray, b: np.ndarray, g: np.ndarray):
     da = _unbroadcast(da, (1, k) if av else a.shape).reshape(a.shape)
     db = _unbroadcast(db, (k, 1) if bv else b.shape).reshape(b.shape)
     return da, db
+
+
+def tensordot(a: np.ndarray, b: np.ndarray, a_axes, b_axes) -> np.ndarray:
+    """tensordot (ops/linalg_extra.rs:164-276): validation in the reference
+    order, then every output element summed over the contraction index space
+    in C order (`sum += a * b`, separately rounded) -- the ordered matrix
+    product of a permuted to [free, contracted] and b to [contracted, free]."""
+    if len(a_axes) != len(b_axes):
+        raise OracleError("ContractAxesMismatch", left=len(a_axes), right=len(b_axes))
+    cl, cr, al, ar = set(), set(), [], []
+    for l, r in zip(a_axes, b_axes):
+        li = l + a.ndim if l < 0 else l
+        if not 0 <= li < a.ndim:
+            raise OracleError("AxisOutOfBounds", axis=l, rank=a.ndim)
+        ri = r + b.ndim if r < 0 else r
+        if not 0 <= ri < b.ndim:
+            raise OracleError("AxisOutOfBounds", axis=r, rank=b.ndim)
+        if li in cl or ri in cr:
+            raise OracleError("DuplicateAxis", axis=li if li in cl else ri)
+        if a.shape[li] != b.shape[ri]:
+            raise OracleError("ContractDimensionMismatch", left=a.shape[li], right=b.shape[ri])
+        cl.add(li)
+        cr.add(ri)
+        al.append(li)
+        ar.append(ri)
+    fl = [i for i in range(a.ndim) if i not in cl]
+    fr = [i for i in range(b.ndim) if i not in cr]
+    out_dims = [a.shape[i] for i in fl] + [b.shape[i] for i in fr]
+    m = int(np.prod([a.shape[i] for i in fl]))
+    k = int(np.prod([a.shape[i] for i in al]))
+    n = int(np.prod([b.shape[i] for i in fr]))
+    if int(np.prod(out_dims)) == 0:
+        return np.zeros(out_dims, dtype=a.dtype)
+    a2 = np.ascontiguousarray(np.transpose(a, fl + al)).reshape(m, k)
+    b2 = np.ascontiguousarray(np.transpose(b, ar + fr)).reshape(k, n)
+    return matmul_reference(View.of(a2), View.of(b2)).reshape(out_dims)

@@ -246,3 +246,32 @@ def test_matmul_backward_oracle_known_answers():
         da, db = oracle.matmul_backward(a, b, np.ones((m, n)))
         assert np.array_equal(da, np.broadcast_to(b.sum(axis=1), (m, k)))
         assert np.array_equal(db, np.broadcast_to(a.sum(axis=0)[:, None], (k, n)))
+
+
+def test_tensordot_oracle_known_answers_and_errors():
+    """tensordot_contracts_arbitrary_axes_and_empty_k and
+    tensordot_scalar_outer_and_zero_result_shapes (ops_completeness_03.rs:
+    224-237, 312-323), the reversed-axis case (contraction_paths.rs:90-101),
+    agreement with numpy's tensordot on exactly representable values, and the
+    errors in the reference order (linalg_extra.rs:164-200)."""
+    x = np.array([[1, 2, 3], [4, 5, 6]], np.float64)
+    y = np.array([[1, 0, 0], [0, 1, 0], [0, 0, 1], [1, 1, 1]], np.float64)
+    assert oracle.tensordot(x, y, [1], [1]).reshape(-1).tolist() == [1, 2, 3, 6, 4, 5, 6, 15]
+    z = oracle.tensordot(np.zeros((2, 0)), np.zeros((0, 3)), [1], [0])
+    assert z.shape == (2, 3) and not z.any()
+    assert oracle.tensordot(np.array(3.0), np.array([5.0, 7.0]), [], []).tolist() == [15.0, 21.0]
+    assert oracle.tensordot(np.zeros((0, 2)), np.ones((2, 3)), [1], [0]).shape == (0, 3)
+    a = np.arange(6, dtype=np.float64).reshape(2, 3)[:, ::-1]
+    assert oracle.tensordot(a, np.ones((3, 2)), [1], [0]).reshape(-1).tolist() == [3.0, 3.0, 12.0, 12.0]
+    a = (np.arange(120) % 7 - 3.0).reshape(4, 5, 6)
+    b = (np.arange(180) % 5 - 2.0).reshape(6, 5, 6)
+    assert np.array_equal(oracle.tensordot(a, b, [2, 1], [0, 1]), np.tensordot(a, b, ([2, 1], [0, 1])))
+    cases = {"ContractAxesMismatch": ([1, 2], [0]), "AxisOutOfBounds": ([3], [0]),
+             "DuplicateAxis": ([2, -1], [0, 1]), "ContractDimensionMismatch": ([1], [0])}
+    for kind, (aa, ba) in cases.items():
+        with pytest.raises(oracle.OracleError) as e:
+            oracle.tensordot(np.zeros((2, 3, 4)), np.zeros((4, 3)), aa, ba)
+        assert e.value.kind == kind
+    with pytest.raises(oracle.OracleError) as e:
+        oracle.tensordot(np.zeros((2, 3, 4)), np.zeros((4, 3)), [2], [-3])
+    assert e.value.fields == {"axis": -3, "rank": 2}
