@@ -18,6 +18,7 @@
  *   - softmax                           crates/kernix-ops/src/ops/math.rs:398-465,531-536
  *   - tensordot                         crates/kernix-ops/src/ops/linalg_extra.rs:164-276
  *   - CpuExecutor::matmul_into          crates/kernix-ops/src/execution.rs:149-240
+ *   - Config / Context::new ([cuda])    crates/kernix/src/config.rs:28-40,84-95,133-137
  *   - Tape::matmul backward (VJP)       crates/kernix/src/autograd.rs:622-690
  *   - conv2d_backward                   crates/kernix-ops/src/neural.rs:379-430
  *   - the C bridge convention           crates/kernix-ops/src/accelerate.c:15-30
@@ -171,6 +172,30 @@ int kx_synchronize(kx_handle *h, kx_error *err);
  * and the call's kx_synchronize reports KX_E_TIMEOUT.  For exercising a
  * caller's handling of that status; the output of that call is unspecified. */
 int kx_diag_expire_next_gemm(kx_handle *h, uint64_t wait_ns);
+
+/* ---- execution context from configuration --------------------------------
+ * The [cuda] table a Kernix configuration gains beside [cpu]
+ * (config.rs:28-40 CpuConfig {threads, ordered_matmul}; kernix.toml:1-7):
+ * everything a CUDA execution context fixes when it is created.  The Rust
+ * side parses it with the rest of Config (serde, unknown keys rejected) and
+ * passes it here from Context::new (config.rs:133-137). */
+typedef struct kx_cuda_config {
+    int32_t device;          /* CUDA ordinal */
+    int32_t f32_variant;     /* kx_f32_variant */
+    int32_t f64_variant;     /* kx_f64_variant */
+    int32_t ordered_matmul;  /* 0 or 1: as [cpu] ordered_matmul, for this context's products */
+    uint64_t workspace_bytes;    /* device scratch reserved at creation; 0 = grown on first use */
+} kx_cuda_config;
+/* Defaults: device 0, automatic variants, native (unordered) products, no
+ * reserved scratch -- what an absent [cuda] table means. */
+void kx_cuda_config_default(kx_cuda_config *cfg);
+/* Validate `cfg` field by field (KX_E_PARAM naming the key, before any device
+ * work), then create a handle on cfg->device with those settings
+ * (KX_E_NO_DEVICE as kx_create) and reserve the scratch (KX_E_CUDA if the
+ * device cannot hold it; no handle is returned then). */
+int kx_context_create(const kx_cuda_config *cfg, kx_handle **out, kx_error *err);
+/* The settings a handle runs with now (Context::config). */
+int kx_handle_config(const kx_handle *h, kx_cuda_config *out);
 
 /* ---- Device<T> buffers (device.rs:22-35) -------------------------------- */
 int kx_alloc(kx_handle *h, uint64_t bytes, void **out, kx_error *err);

@@ -19,7 +19,9 @@ as :class:`OpsError` subclasses carrying the reference variant's fields.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
+import threading
 from dataclasses import dataclass, field
 from typing import Sequence
 
@@ -42,7 +44,7 @@ __all__ = [
     "handle", "OpsError", "InvalidRank", "ContractDimensionMismatch", "BroadcastIncompatible",
     "ElementCountOverflow", "DimensionOverflow", "LayoutError", "InvalidParameter", "ExactRank",
     "NonFiniteInput", "AxisOutOfBounds", "OverlappingOutput", "CudaError", "NoDevice", "Unsupported",
-    "CapacityOverflow", "ContractAxesMismatch", "DuplicateAxis",
+    "CapacityOverflow", "ContractAxesMismatch", "DuplicateAxis", "using", "Config", "Context", "ConfigError",
 ]
 
 
@@ -58,6 +60,14 @@ class Handle:
         err = KxError()
         raise_for(lib.kx_create(device, C.byref(ptr), C.byref(err)), err)
         self._h = ptr
+
+    @classmethod
+    def adopt(cls, ptr: C.c_void_p, device: int) -> "Handle":
+        """Own a handle the library created elsewhere (kx_context_create)."""
+        h = cls.__new__(cls)
+        h.device = device
+        h._h = ptr
+        return h
 
     @property
     def ptr(self) -> C.c_void_p:
@@ -115,6 +125,25 @@ class Handle:
 
 
 _handles: dict[int, Handle] = {}
+_active = threading.local()
+
+
+@contextlib.contextmanager
+def using(h: Handle):
+    """Route this thread's calls on ``h.device`` through ``h`` (a context's
+    handle with its own variants and ordered mode) instead of the default."""
+    stack = getattr(_active, "handles", None)
+    if stack is None:
+        stack = _active.handles = {}
+    prev = stack.get(h.device)
+    stack[h.device] = h
+    try:
+        yield h
+    finally:
+        if prev is None:
+            del stack[h.device]
+        else:
+            stack[h.device] = prev
 
 
 def handle(device: int | None = None) -> Handle:
@@ -191,7 +220,7 @@ def _device_index(t) -> int:
 def _bind(t) -> Handle:
     import torch
     dev = _device_index(t)
-    h = handle(dev)
+    h = getattr(_active, "handles", {}).get(dev) or handle(dev)
     h.set_stream(torch.cuda.current_stream(dev))
     return h
 
@@ -593,4 +622,18 @@ class CudaExecutor:
         for t in (left, right):
             if _device_index(t) != self.device:
                 raise InvalidParameter("tensor belongs to another device", operation="matmul", parameter="device")
-        return matmul(left, right)
+        with using(self.h):
+            return matmul(left, right)
+
+    def matmul_into(self, left, right, out) -> None:
+        """CpuExecutor::matmul_into's contract (execution.rs:149-240) on the
+        device: the caller's C-contiguous output is reused, nothing allocated."""
+        for t in (left, right, out):
+            if _device_index(t) != self.device:
+                raise InvalidParameter("tensor belongs to another device", operation="matmul_into",
+                                       parameter="device")
+        with using(self.h):
+            matmul_into(left, right, out)
+
+
+from .config import Config, ConfigError, Context  # noqa: E402  (needs Handle and CudaExecutor above)

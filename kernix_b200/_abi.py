@@ -82,6 +82,17 @@ class KxMatrix(C.Structure):
     ]
 
 
+class KxCudaConfig(C.Structure):
+    """kx_cuda_config: the [cuda] table of a configuration."""
+    _fields_ = [
+        ("device", C.c_int32),
+        ("f32_variant", C.c_int32),
+        ("f64_variant", C.c_int32),
+        ("ordered_matmul", C.c_int32),
+        ("workspace_bytes", C.c_uint64),
+    ]
+
+
 class KxConv2dOptions(C.Structure):
     _fields_ = [
         ("stride", C.c_uint64 * 2),
@@ -105,6 +116,9 @@ _SIGNATURES = {
     "kx_ordered_matmul": (C.c_int, [_vp]),
     "kx_synchronize": (C.c_int, [_vp, _P(KxError)]),
     "kx_diag_expire_next_gemm": (C.c_int, [_vp, C.c_uint64]),
+    "kx_cuda_config_default": (None, [_P(KxCudaConfig)]),
+    "kx_context_create": (C.c_int, [_P(KxCudaConfig), _P(_vp), _P(KxError)]),
+    "kx_handle_config": (C.c_int, [_vp, _P(KxCudaConfig)]),
     "kx_alloc": (C.c_int, [_vp, _u64, _P(_vp), _P(KxError)]),
     "kx_free": (C.c_int, [_vp, _vp]),
     "kx_upload": (C.c_int, [_vp, _vp, _vp, _u64, _P(KxError)]),

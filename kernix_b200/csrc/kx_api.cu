@@ -465,6 +465,56 @@ int kx_diag_expire_next_gemm(kx_handle *hh, uint64_t wait_ns) {
     return KX_OK;
 }
 
+void kx_cuda_config_default(kx_cuda_config *cfg) {
+    if (!cfg) return;
+    std::memset(cfg, 0, sizeof(*cfg));
+    cfg->f32_variant = KX_F32_AUTO;
+    cfg->f64_variant = KX_F64_AUTO;
+}
+
+int kx_context_create(const kx_cuda_config *cfg, kx_handle **out, kx_error *err) {
+    static const char *kOp = "Context::new";
+    if (!out) return set_err(err, KX_E_PARAM, kOp, "null output");
+    *out = nullptr;
+    if (!cfg) return set_err(err, KX_E_PARAM, kOp, "null configuration");
+    if (cfg->device < 0) return set_err(err, KX_E_PARAM, kOp, "cuda.device must be non-negative");
+    if (cfg->f32_variant < KX_F32_AUTO || cfg->f32_variant > KX_F32_3XTF32_1SM)
+        return set_err(err, KX_E_PARAM, kOp, "cuda.f32_variant is not a kernel family");
+    if (cfg->f64_variant < KX_F64_AUTO || cfg->f64_variant > KX_F64_DMMA)
+        return set_err(err, KX_E_PARAM, kOp, "cuda.f64_variant is not a kernel family");
+    if (cfg->ordered_matmul != 0 && cfg->ordered_matmul != 1)
+        return set_err(err, KX_E_PARAM, kOp, "cuda.ordered_matmul must be 0 or 1");
+    kx_handle *hh = nullptr;
+    int rc = kx_create(cfg->device, &hh, err);
+    if (rc) return rc;
+    Handle &h = hh->impl;
+    h.f32_variant = cfg->f32_variant;
+    h.f64_variant = cfg->f64_variant;
+    h.ordered = cfg->ordered_matmul != 0;
+    if (cfg->workspace_bytes) {
+        DeviceGuard g(h.device);
+        if (h.grow(&h.ws, &h.ws_bytes, cfg->workspace_bytes)) {
+            rc = cuda_err(err, &h, kOp);
+            kx_destroy(hh);
+            return rc;
+        }
+    }
+    *out = hh;
+    return KX_OK;
+}
+
+int kx_handle_config(const kx_handle *hh, kx_cuda_config *out) {
+    if (!hh || !out) return KX_E_PARAM;
+    const Handle &h = hh->impl;
+    std::memset(out, 0, sizeof(*out));
+    out->device = h.device;
+    out->f32_variant = h.f32_variant;
+    out->f64_variant = h.f64_variant;
+    out->ordered_matmul = h.ordered ? 1 : 0;
+    out->workspace_bytes = h.ws_bytes;
+    return KX_OK;
+}
+
 int kx_synchronize(kx_handle *hh, kx_error *err) {
     if (!hh) return set_err(err, KX_E_PARAM, "synchronize", "null handle");
     DeviceGuard g(hh->impl.device);

@@ -225,6 +225,28 @@ def test_tc_short_k_output_paths(kx, torch_cuda):
     h.synchronize()
 
 
+@pytest.mark.parametrize("m,n,nb", [(2048 + 45, 2304 + 36, 1), (2048 + 100, 2304 + 92, 1), (2048 + 70, 2304 + 124, 1),
+                                    (2048 + 1, 2304 + 4, 1), (333, 300, 40)])
+def test_tc_short_k_box_edges_every_position(kx, torch_cuda, m, n, nb):
+    """The staged 32 x 32 box stores with the matrix edge inside each of the
+    four row quarters and each of the four 32-column blocks of a 128 x 128
+    tile (partially clipped boxes there, wholly clipped ones beyond), and a
+    batched product whose last rows of every batch end inside a box (the
+    tensor map's batch dimension clips them); every element against f64."""
+    torch = torch_cuda
+    h = kx.handle(0)
+    h.set_f32_variant(0)
+    rng = np.random.default_rng(m * 7 + n)
+    a = rng.uniform(-1, 1, (nb, m, 96)).astype(np.float32)
+    b = rng.uniform(-1, 1, (nb, 96, n)).astype(np.float32)
+    c = kx.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()).cpu().numpy().astype(np.float64)
+    assert h.last_kernel == "tc_3xtf32_short_128x128_bmn", h.last_kernel
+    a64, b64 = a.astype(np.float64), b.astype(np.float64)
+    bound = 2e-6 * (np.abs(a64) @ np.abs(b64)) + 1e-30
+    assert (np.abs(c - a64 @ b64) <= bound).all()
+    h.synchronize()
+
+
 def test_tc_short_k_persistent(kx, torch_cuda):
     """K <= 1024 over many tiles: the persistent kernel (TMEM double-buffered,
     epilogue overlapping the next tile) -- attention scores Q K^T with a
