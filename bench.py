@@ -746,6 +746,21 @@ def run_workload(w, steps, warmup, rank=0, world=1, local=0, batch=0, size=0):
         c = torch.empty(512, 512, device=dev)
         ms, clocks, launches = _timed(lambda: kx.matmul_into(a, b, c), steps, warmup, dev, 1, h)
         flops = 2.0 * 512 ** 3
+        # the same calls captured once in a CUDA graph and replayed: device time
+        # per product without the per-call host path (ctypes, validation, launch)
+        graph_calls = 50
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                kx.matmul_into(a, b, c)             # workspace grown before capture
+        torch.cuda.current_stream(dev).wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(graph_calls):
+                kx.matmul_into(a, b, c)
+        g_ms, _, _ = _timed(g.replay, max(1, steps // graph_calls), 2, dev, 1, None)
+        graph_us = 1000.0 * g_ms / graph_calls
         va, vb = oracle.View.of(a_np), oracle.View.of(b_np)
         exp, ab = oracle.gemm_dot2(va, vb)
         ours = err_metrics(c.cpu().numpy(), exp, ab)
@@ -754,7 +769,11 @@ def run_workload(w, steps, warmup, rank=0, world=1, local=0, batch=0, size=0):
                  "elementwise_target": 1e-5, "cpu_fp32_engine": eng,
                  "pass": ours["max_err_over_sum_abs"] <= 2e-6 and ours["normwise"] <= 1e-5}
         res.update(dtype="f32", config={"workload": "c1", "M": 512, "N": 512, "K": 512,
-                                        "l2": "inputs (3 MB) stay L2-resident: latency-bound"})
+                                        "l2": "inputs (3 MB) stay L2-resident: latency-bound"},
+                   cuda_graph={"us_per_product": round(graph_us, 3),
+                               "tflops": round(flops / graph_us / 1e6, 3), "products_per_graph": graph_calls,
+                               "what": "the same matmul_into calls captured in one CUDA graph and replayed: "
+                                       "device time per product without the host call path"})
     elif w == "c2":
         n = size or 4096
         v = rng.normal(SEEDS["c2"][0], 2 * n * n, 1.0, np.float64)
@@ -996,8 +1015,9 @@ def main():
                 if r is not None:
                     per[w] = {k: r[k] for k in ("value", "unit", "ms_per_step", "steps", "warmup", "dtype", "kernel",
                                                 "gpu_launches", "check", "roofline", "clocks", "config")}
-                    if "parts" in r:
-                        per[w]["parts"] = r["parts"]
+                    for extra in ("parts", "cuda_graph"):
+                        if extra in r:
+                            per[w][extra] = r[extra]
             if res is not None:
                 res["per_config"] = per
         if res is not None:
