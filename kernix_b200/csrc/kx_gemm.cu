@@ -88,8 +88,10 @@ int run_gemm(Handle *h, GemmParams<T> p, const char **kernel_name) {
         // Split-TF32 tensor-core path: eligible layouts, enough 128x256 tiles to
         // fill the machine, and not the ordered (bitwise reference) mode.
         if (!h->ordered && h->f32_variant != KX_F32_FFMA && tc_eligible(p)) {
+            // SMs this launch plans for: all, or a share when another GEMM runs beside it
+            const int64_t sms = h->sm_budget > 0 ? h->sm_budget : h->sm_count;
             const int64_t tc_tiles = (int64_t)((p.M + 127) / 128) * ((p.N + 255) / 256) * p.nbatch;
-            const bool big = tc_tiles >= h->sm_count / 2 && p.K >= 64;
+            const bool big = tc_tiles >= sms / 2 && p.K >= 64;
             if (h->f32_variant == KX_F32_3XTF32 || h->f32_variant == KX_F32_3XTF32_1SM || big) {
                 // CTA pairs or one-SM tiles by the wave model: waves of
                 // sm_count CTAs times a per-CTA cost of (width + 32), a
@@ -98,7 +100,7 @@ int run_gemm(Handle *h, GemmParams<T> p, const char **kernel_name) {
                 // TFLOP/s at 8192^3; the 224-wide pair, which stages 128 B
                 // columns for 112, is slower than one-SM 224-wide tiles);
                 // pairs only for K long enough to amortise their cluster set-up.
-                auto waves = [&](int64_t ctas) { return (ctas + h->sm_count - 1) / h->sm_count; };
+                auto waves = [&](int64_t ctas) { return (ctas + sms - 1) / sms; };
                 const int64_t tm1 = (p.M + 127) / 128, tmp = (p.M + 255) / 256;
                 double best1 = 1e30, bestp = 1e30;
                 for (int bn : {256, 224, 128})
@@ -108,7 +110,7 @@ int run_gemm(Handle *h, GemmParams<T> p, const char **kernel_name) {
                 // Short contractions over many tiles: the persistent kernel,
                 // whose epilogue overlaps the next tile.
                 const int64_t tiles128 = tm1 * ((p.N + 127) / 128) * p.nbatch;
-                if (h->f32_variant == KX_F32_AUTO && !p.C_mc && p.K <= 1024 && tiles128 >= 2LL * h->sm_count)
+                if (h->f32_variant == KX_F32_AUTO && !p.C_mc && p.K <= 1024 && tiles128 >= 2LL * sms)
                     rc = run_gemm_tc_short(h, p, kernel_name);
                 if (rc == KX_DECLINED && h->f32_variant != KX_F32_3XTF32_1SM && !p.C_mc && p.M >= 256 &&
                     (h->f32_variant == KX_F32_3XTF32 || (p.K >= 512 && bestp < best1)))
