@@ -13,7 +13,9 @@
 // 512 FMAs per warp, so the FP64 pipe, not shared memory, sets the pace.
 //
 // CTA: 128 x 128 outputs, 8 warps as 2 (m) x 4 (n), warp tile 64 x 32 (4 x 4
-// MMAs per k-step of 4), k depth 16 per stage, 3-stage cp.async ring.
+// MMAs per k-step of 4), k depth 32 per stage, 3-stage cp.async ring (one
+// barrier per 32 k); each k-step's fragments are read while the previous
+// step's MMAs run, and a stage's copies are issued after its first k-step.
 // Shared layouts follow the operand's contiguous axis so that cp.async copies
 // stay contiguous; row pitches are padded so the fragment loads of a warp hit
 // each bank at most twice (the minimum for 32 doubles).
@@ -25,12 +27,13 @@
 namespace kx {
 namespace dmma {
 
-constexpr int BM = 128, BN = 128, BK = 16, STAGES = 3, NT = 256;
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3, NT = 256;
 constexpr int PK = BK + 4;     // pitch of a k-contiguous tile row (m or n major index)
 constexpr int PMN = BM + 8;    // pitch of an m/n-contiguous tile row (k major index)
 static_assert(BM == BN, "one pitch for both operands");
-constexpr int TILE_DOUBLES = BM * PK > BK * PMN ? BM * PK : BK * PMN;   // 2560
-constexpr int SMEM_BYTES = STAGES * 2 * TILE_DOUBLES * 8;                 // 122880
+constexpr int TILE_DOUBLES = BM * PK > BK * PMN ? BM * PK : BK * PMN;   // 4608
+constexpr int SMEM_BYTES = STAGES * 2 * TILE_DOUBLES * 8;                 // 221184
+static_assert(SMEM_BYTES <= 232448, "shared memory");
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -138,26 +141,42 @@ __global__ void __launch_bounds__(NT, 1) gemm_dmma_kernel(const __grid_constant_
             cp_wait<STAGES - 2>();
             __syncthreads();
             const int nxt = kt + STAGES - 1;
-            if (nxt < ktiles) {
-                load_tile<A_KC, V2>(sA(nxt % STAGES), A, a_sr, a_sk, m0, p.M, nxt * BK, p.K, tid);
-                load_tile<B_KC, V2>(sB(nxt % STAGES), B, b_sr, b_sk, n0, p.N, nxt * BK, p.K, tid);
-            }
-            cp_commit();
             const double *a_s = sA(kt % STAGES), *b_s = sB(kt % STAGES);
+            // fragments of k step kk + 4 are read while step kk's MMAs run;
+            // the next stage's copies go out after the first step's MMAs, so
+            // the tensor pipe restarts right after the barrier
+            double af[2][4][2], bf[2][4];
 #pragma unroll
-            for (int kk = 0; kk < BK; kk += 4) {
-                double af[4][2], bf[4];
+            for (int i = 0; i < 4; ++i) {
+                af[0][i][0] = frag<A_KC>(a_s, wm + i * 16 + g, t4);
+                af[0][i][1] = frag<A_KC>(a_s, wm + i * 16 + g + 8, t4);
+            }
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    af[i][0] = frag<A_KC>(a_s, wm + i * 16 + g, kk + t4);
-                    af[i][1] = frag<A_KC>(a_s, wm + i * 16 + g + 8, kk + t4);
+            for (int j = 0; j < 4; ++j) bf[0][j] = frag<B_KC>(b_s, wn + j * 8 + g, t4);
+#pragma unroll
+            for (int s4 = 0; s4 < BK / 4; ++s4) {
+                const int cur = s4 & 1;
+                if (s4 + 1 < BK / 4) {
+                    const int kn = (s4 + 1) * 4 + t4;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        af[cur ^ 1][i][0] = frag<A_KC>(a_s, wm + i * 16 + g, kn);
+                        af[cur ^ 1][i][1] = frag<A_KC>(a_s, wm + i * 16 + g + 8, kn);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) bf[cur ^ 1][j] = frag<B_KC>(b_s, wn + j * 8 + g, kn);
                 }
-#pragma unroll
-                for (int j = 0; j < 4; ++j) bf[j] = frag<B_KC>(b_s, wn + j * 8 + g, kk + t4);
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) mma_f64(acc[i][j], af[i][0], af[i][1], bf[j]);
+                    for (int j = 0; j < 4; ++j) mma_f64(acc[i][j], af[cur][i][0], af[cur][i][1], bf[cur][j]);
+                if (s4 == 0) {
+                    if (nxt < ktiles) {
+                        load_tile<A_KC, V2>(sA(nxt % STAGES), A, a_sr, a_sk, m0, p.M, nxt * BK, p.K, tid);
+                        load_tile<B_KC, V2>(sB(nxt % STAGES), B, b_sr, b_sk, n0, p.N, nxt * BK, p.K, tid);
+                    }
+                    cp_commit();
+                }
             }
         }
         cp_wait<0>();
