@@ -201,10 +201,12 @@ __global__ void __launch_bounds__(256) split_lo_kernel(const float *__restrict__
 
 // Slot stream of one unit, in the order the MMA thread consumes it:
 // kt_0, kt_1, v_0, kt_2, v_1, ..., kt_{n-1}, v_{n-2}, v_{n-1}; each kt_j and
-// v_j is 4 slots.  Slot item e (0-based) of a unit -> (is_v, block, part).
+// v_j is SPB slots (4 on one SM; 2 in each CTA of a pair, which stages half
+// of every block).  Slot item e (0-based) of a unit -> (is_v, block, part).
+template <int SPB>
 __device__ __forceinline__ void slot_item(int e, int nkb, bool &is_v, int &blk, int &part) {
-    part = e & 3;
-    const int grp = e >> 2;   // 0: kt_0; then pairs (kt_j, v_{j-1}); last: v_{n-1}
+    part = e % SPB;
+    const int grp = e / SPB;  // 0: kt_0; then pairs (kt_j, v_{j-1}); last: v_{n-1}
     if (grp == 0) {
         is_v = false;
         blk = 0;
@@ -218,12 +220,38 @@ __device__ __forceinline__ void slot_item(int e, int nkb, bool &is_v, int &blk, 
     }
 }
 
+// D (TMEM of both CTAs) += A (TMEM of both CTAs, 128 lanes x 8 tf32 columns
+// each) x B (shared memory: each CTA's half of the columns), for a pair.
+__device__ __forceinline__ void mma_pair_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Registers are split evenly over the SM's four sub-partitions (16,384
 // each); twelve warps put three on each, so a thread may use up to 168.
+//
+// PAIR: a cluster of two CTAs takes 256 query rows, 128 in each CTA, and the
+// leader (cluster rank 0) issues tcgen05.mma.cta_group::2 for both: scores
+// with M = 256, N = 64 (each CTA stages 32 of the block's keys) and P.v with
+// M = 256, N = 128 (each CTA stages 64 of v's columns, P comes from each CTA's
+// own TMEM).  Per SM that halves the key and value bytes loaded and the
+// operand bytes the tensor core reads per MMA falls from 6 KB to 5 KB.  Each
+// CTA's TMA completes on its own slot barrier; in the second CTA the otherwise
+// idle warp 1 relays every filled slot to the leader with a remote arrive; the
+// row warps' and split warps' arrivals go to the leader's barriers, and the
+// leader commits every MMA completion to the barriers of both CTAs.  The
+// softmax, the fold and the epilogue are each CTA's own, as on one SM.
+template <bool PAIR>
 __global__ void __launch_bounds__(NT, 1)
 attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKl,
                    const __grid_constant__ CUtensorMap tmVl, const __grid_constant__ Params p) {
+    constexpr int SPB = PAIR ? 2 : 4;           // slots per key block and operand
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *ring = smem + RING_OFF;
@@ -239,30 +267,41 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     uint64_t *o_empty = o_full + 2;             // [2]
     uint64_t *xbar = o_empty + 2;               // [4] row-maximum exchange per lane quarter
     uint64_t *lbar = xbar + 4;                  // [4] row-sum exchange per lane quarter
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(lbar + 4);
+    uint64_t *peer_full = lbar + 4;             // [NSLOT] pair leader: the second CTA's slot is full
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(peer_full + NSLOT);
     float *xmax = reinterpret_cast<float *>(smem + MISC_OFF + 512);   // [2][2][BQ]
     float *lsum = xmax + 4 * BQ;                                      // [2][BQ]
     __shared__ int s_fail_storage;
     volatile int &s_fail = s_fail_storage;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t my_units = p.units > blockIdx.x ? (p.units - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    const uint32_t rank = PAIR ? cluster_rank() : 0u;
+    const bool leader = rank == 0;
+    const int64_t unit0 = PAIR ? blockIdx.x / 2 : blockIdx.x;        // this CTA's (pair's) first unit
+    const int64_t ustride = PAIR ? gridDim.x / 2 : gridDim.x;
+    const int64_t my_units = p.units > unit0 ? (p.units - unit0 + ustride - 1) / ustride : 0;
     const int nkb = p.nkb;
-    const int items = 8 * nkb;        // slot items per unit
+    const int items = 2 * SPB * nkb;  // slot items per unit
+    // arrivals that the leader's MMA thread waits for
+    auto arrive_leader = [&](uint64_t *bar) {
+        if constexpr (PAIR) mbar_arrive_cluster(map_to(smem_u32(bar), 0));
+        else mbar_arrive(bar);
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NSLOT; ++s) {
             mbar_init(&slot_full[s], 1);
             mbar_init(&slot_empty[s], 1);
+            mbar_init(&peer_full[s], 1);
         }
         mbar_init(q_full, 1);
-        mbar_init(q_conv, SPLIT_WARPS);
+        mbar_init(q_conv, PAIR ? 2 * SPLIT_WARPS : SPLIT_WARPS);
         mbar_init(q_empty, 1);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&s_full[b], 1);
-            mbar_init(&p_ready[b], 8);
+            mbar_init(&p_ready[b], PAIR ? 16 : 8);
             mbar_init(&o_full[b], 1);
-            mbar_init(&o_empty[b], 8);
+            mbar_init(&o_empty[b], PAIR ? 16 : 8);
         }
         for (int r = 0; r < 4; ++r) {
             mbar_init(&xbar[r], 2);
@@ -272,13 +311,21 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(TMEM_COLS)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        if constexpr (PAIR) {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                         ::"r"(smem_u32(tmem_slot)), "r"(TMEM_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                         ::"r"(smem_u32(tmem_slot)), "r"(TMEM_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) cluster_sync_any();    // both CTAs' barriers initialised, TMEM allocated
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -288,8 +335,8 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             int64_t g = 0;        // slot loads issued so far
             int64_t i = 0;
             for (; i < my_units && !s_fail; ++i) {
-                const int64_t u = blockIdx.x + i * gridDim.x;
-                const int bh = (int)(u / p.nq), q0 = (int)(u % p.nq) * BQ;
+                const int64_t u = unit0 + i * ustride;
+                const int bh = (int)(u / p.nq), q0 = (int)(u % p.nq) * (PAIR ? 2 * BQ : BQ) + (int)rank * BQ;
                 if (i > 0 && !mbar_wait_idle(q_empty, (uint32_t)((i - 1) & 1))) {
                     s_fail = 1;
                     break;
@@ -305,10 +352,32 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     }
                     bool is_v;
                     int blk, part;
-                    slot_item(e, nkb, is_v, blk, part);
+                    slot_item<SPB>(e, nkb, is_v, blk, part);
                     uint8_t *dst = ring + s * SLOT;
                     mbar_expect_tx(&slot_full[s], SLOT);
-                    if (!is_v) {
+                    if (PAIR && !is_v) {
+                        // this CTA's 32 keys of kt_j x 64 head columns [64 part, +64): four
+                        // 16-column boxes, hi then lo
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            tma_load_3d(dst + c * 2048, &tmK, part * 64 + c * 16, blk * BKEY + (int)rank * 32, bh,
+                                        &slot_full[s]);
+                            tma_load_3d(dst + SLOT / 2 + c * 2048, &tmKl, part * 64 + c * 16,
+                                        blk * BKEY + (int)rank * 32, bh, &slot_full[s]);
+                        }
+                    } else if (PAIR) {
+                        // keys [32 part, +32) of v_j x this CTA's 64 columns [64 rank, +64):
+                        // per 16 keys two 32-column boxes, hi then lo
+#pragma unroll
+                        for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+                            for (int c = 0; c < 2; ++c) {
+                                const int col = (int)rank * 64 + c * 32, key = blk * BKEY + part * 32 + kh * 16;
+                                tma_load_3d(dst + kh * 4096 + c * 2048, &tmV, col, key, bh, &slot_full[s]);
+                                tma_load_3d(dst + SLOT / 2 + kh * 4096 + c * 2048, &tmVl, col, key, bh,
+                                            &slot_full[s]);
+                            }
+                    } else if (!is_v) {
                         // kt_j: 64 keys x 32 head columns as two 16-column boxes, hi then lo
                         tma_load_3d(dst, &tmK, part * 32, blk * BKEY, bh, &slot_full[s]);
                         tma_load_3d(dst + 4096, &tmK, part * 32 + 16, blk * BKEY, bh, &slot_full[s]);
@@ -332,16 +401,58 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             }
             if (i > 0) mbar_wait(q_full, (uint32_t)((i - 1) & 1));
         }
-    } else if (warp == 1) {
-        // ---- MMA issuer --------------------------------------------------
+    } else if (warp == 1 && PAIR && !leader) {
+        // ---- relay (second CTA of a pair): each filled slot -> the leader --
         if (lane == 0) {
-            constexpr uint32_t idesc_s = idesc_tf32<BKEY>(false);
-            constexpr uint32_t idesc_o = idesc_tf32<DH>(true);
+            const uint32_t pf0 = map_to(smem_u32(&peer_full[0]), 0);
+            int64_t g = 0;
+            for (int64_t i = 0; i < my_units && !s_fail; ++i) {
+                for (int e = 0; e < items; ++e, ++g) {
+                    const int s = (int)(g % NSLOT);
+                    if (!mbar_wait(&slot_full[s], (uint32_t)((g / NSLOT) & 1))) {   // no sleep: on the MMA path
+                        s_fail = 1;
+                        break;
+                    }
+                    mbar_arrive_cluster(pf0 + (uint32_t)(s * 8));
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer (one SM, or the leader of a pair) -----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = PAIR ? idesc_pair(false, BKEY) : idesc_tf32<BKEY>(false);
+            constexpr uint32_t idesc_o = PAIR ? idesc_pair(true, DH) : idesc_tf32<DH>(true);
             const uint64_t dq_hi = desc_k_sw64(smem_u32(smem)), dq_lo = desc_k_sw64(smem_u32(smem) + Q_BYTES);
+            // the slot's data in this CTA and, for a pair, in the second CTA
+            auto slot_ready = [&](int s, int64_t g) -> bool {
+                if (!mbar_wait(&slot_full[s], (uint32_t)((g / NSLOT) & 1))) return false;
+                if constexpr (PAIR)
+                    if (!mbar_wait_cluster(&peer_full[s], (uint32_t)((g / NSLOT) & 1))) return false;
+                return true;
+            };
+            // completion of the MMAs issued so far -> the barrier in every CTA that has it
+            auto commit = [&](uint64_t *bar) {
+                if constexpr (PAIR) {
+                    commit_pair(smem_u32(bar));
+                    commit_pair(map_to(smem_u32(bar), 1));
+                } else {
+                    mma_commit(bar);
+                }
+            };
+            auto mma_s = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+                if constexpr (PAIR) mma_pair(d, a, b, idesc_s, acc);
+                else mma_tf32(d, a, b, idesc_s, acc);
+            };
+            auto mma_o = [&](uint32_t d, uint32_t a, uint64_t b, uint32_t acc) {
+                if constexpr (PAIR) mma_pair_ts(d, a, b, idesc_o, acc);
+                else mma_tf32_ts(d, a, b, idesc_o, acc);
+            };
             int64_t g = 0;        // slot items consumed
             int64_t kb = 0;       // key blocks started (global, for the TMEM buffers)
             for (int64_t i = 0; i < my_units && !s_fail; ++i) {
-                if (!mbar_wait(q_conv, (uint32_t)(i & 1))) {
+                const bool q_ready = PAIR ? mbar_wait_cluster(q_conv, (uint32_t)(i & 1))
+                                          : mbar_wait(q_conv, (uint32_t)(i & 1));
+                if (!q_ready) {
                     s_fail = 1;
                     break;
                 }
@@ -353,40 +464,48 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         const int64_t gb = kb0 + j;
                         const uint32_t sm = tmem + (uint32_t)((gb & 1) * 128), sx = sm + 64;
 #pragma unroll 1
-                        for (int t = 0; t < 4; ++t) {
+                        for (int t = 0; t < SPB; ++t) {
                             const int s = (int)(g % NSLOT);
-                            if (!mbar_wait(&slot_full[s], (uint32_t)((g / NSLOT) & 1))) {
+                            if (!slot_ready(s, g)) {
                                 s_fail = 1;
                                 break;
                             }
                             tc_fence_after();
-                            // descriptors: base + (byte offset >> 4) in the address field
+                            // descriptors: base + (byte offset >> 4) in the address field.
+                            // One SM: the slot holds head columns [32 t, +32) of all 64
+                            // keys as two 16-column boxes of 4 KB; a pair CTA: columns
+                            // [64 t, +64) of its 32 keys as four boxes of 2 KB.
                             const uint64_t dk = desc_k_sw64(smem_u32(ring + s * SLOT));
+                            constexpr int BOXES = PAIR ? 4 : 2, BOX = PAIR ? 2048 : 4096;
 #pragma unroll
-                            for (int sub = 0; sub < 2; ++sub) {
+                            for (int sub = 0; sub < BOXES; ++sub) {
 #pragma unroll
                                 for (int ks = 0; ks < 2; ++ks) {
-                                    const uint32_t qo = (uint32_t)(((2 * t + sub) * 8192 + ks * 32) >> 4);
-                                    const uint32_t ko = (uint32_t)((sub * 4096 + ks * 32) >> 4);
+                                    const uint32_t qo = (uint32_t)(((BOXES * t + sub) * 8192 + ks * 32) >> 4);
+                                    const uint32_t ko = (uint32_t)((sub * BOX + ks * 32) >> 4);
                                     const uint32_t acc = (t > 0 || sub > 0 || ks > 0) ? 1u : 0u;
-                                    mma_tf32(sm, dq_hi + qo, dk + ko, idesc_s, acc);
-                                    mma_tf32(sx, dq_hi + qo, dk + ko + (SLOT / 2 >> 4), idesc_s, acc);
-                                    mma_tf32(sx, dq_lo + qo, dk + ko, idesc_s, 1u);
+                                    mma_s(sm, dq_hi + qo, dk + ko, acc);
+                                    mma_s(sx, dq_hi + qo, dk + ko + (SLOT / 2 >> 4), acc);
+                                    mma_s(sx, dq_lo + qo, dk + ko, 1u);
                                 }
                             }
-                            mma_commit(&slot_empty[s]);
+                            commit(&slot_empty[s]);
                             ++g;
                         }
                         if (s_fail) break;
-                        mma_commit(&s_full[gb & 1]);
-                        if (j == nkb - 1) mma_commit(q_empty);   // q is read by no later MMA of this unit
+                        commit(&s_full[gb & 1]);
+                        if (j == nkb - 1) commit(q_empty);   // q is read by no later MMA of this unit
                     }
                     if (j >= 1) {
                         const int64_t gb = kb0 + j - 1;
                         const int b = (int)(gb & 1);
                         // P_{j-1} written by the softmax warps; O buffer b read by the fold warps
-                        if (!mbar_wait(&p_ready[b], (uint32_t)((gb >> 1) & 1)) ||
-                            (gb >= 2 && !mbar_wait(&o_empty[b], (uint32_t)(((gb >> 1) - 1) & 1)))) {
+                        const bool ready =
+                            PAIR ? (mbar_wait_cluster(&p_ready[b], (uint32_t)((gb >> 1) & 1)) &&
+                                    (gb < 2 || mbar_wait_cluster(&o_empty[b], (uint32_t)(((gb >> 1) - 1) & 1))))
+                                 : (mbar_wait(&p_ready[b], (uint32_t)((gb >> 1) & 1)) &&
+                                    (gb < 2 || mbar_wait(&o_empty[b], (uint32_t)(((gb >> 1) - 1) & 1))));
+                        if (!ready) {
                             s_fail = 1;
                             break;
                         }
@@ -394,36 +513,41 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         const uint32_t ph = tmem + (uint32_t)(b * 128), pl = ph + 64;
                         const uint32_t od = tmem + 256u + (uint32_t)(b * 128);
 #pragma unroll 1
-                        for (int t = 0; t < 4; ++t) {
+                        for (int t = 0; t < SPB; ++t) {
                             const int s = (int)(g % NSLOT);
-                            if (!mbar_wait(&slot_full[s], (uint32_t)((g / NSLOT) & 1))) {
+                            if (!slot_ready(s, g)) {
                                 s_fail = 1;
                                 break;
                             }
                             tc_fence_after();
-                            const uint64_t dv = desc_mn_sw128(smem_u32(ring + s * SLOT), 2048, 512);
+                            // One SM: the slot holds keys [16 t, +16) x all 128 columns as
+                            // four 32-column boxes; a pair CTA: keys [32 t, +32) x its 64
+                            // columns, per 16 keys two 32-column boxes (4 KB apart).
+                            constexpr int KSTEPS = PAIR ? 4 : 2;
 #pragma unroll
-                            for (int ks = 0; ks < 2; ++ks) {
-                                const uint32_t vo = (uint32_t)((ks * 1024) >> 4);
-                                const uint32_t col = (uint32_t)(t * 16 + ks * 8);
+                            for (int ks = 0; ks < KSTEPS; ++ks) {
+                                const uint32_t vbyte = PAIR ? (uint32_t)((ks >> 1) * 4096 + (ks & 1) * 1024)
+                                                            : (uint32_t)(ks * 1024);
+                                const uint64_t dv = desc_mn_sw128(smem_u32(ring + s * SLOT), 2048, 512) + (vbyte >> 4);
+                                const uint32_t col = (uint32_t)(t * 8 * KSTEPS + ks * 8);
                                 const uint32_t acc = (t > 0 || ks > 0) ? 1u : 0u;
-                                mma_tf32_ts(od, ph + col, dv + vo, idesc_o, acc);
-                                mma_tf32_ts(od, ph + col, dv + vo + (SLOT / 2 >> 4), idesc_o, 1u);
-                                mma_tf32_ts(od, pl + col, dv + vo, idesc_o, 1u);
+                                mma_o(od, ph + col, dv, acc);
+                                mma_o(od, ph + col, dv + (SLOT / 2 >> 4), 1u);
+                                mma_o(od, pl + col, dv, 1u);
                             }
-                            mma_commit(&slot_empty[s]);
+                            commit(&slot_empty[s]);
                             ++g;
                         }
                         if (s_fail) break;
-                        mma_commit(&o_full[b]);
+                        commit(&o_full[b]);
                     }
                 }
                 kb = kb0 + nkb;
             }
             if (s_fail) {   // release every role that may wait on the MMA thread
                 for (int b = 0; b < 2; ++b) {
-                    mma_commit(&s_full[b]);
-                    mma_commit(&o_full[b]);
+                    commit(&s_full[b]);
+                    commit(&o_full[b]);
                 }
             }
         }
@@ -441,8 +565,8 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         int64_t kb = 0;
         uint32_t bad = 0;
         for (int64_t i = 0; i < my_units && !s_fail; ++i) {
-            const int64_t u = blockIdx.x + i * gridDim.x;
-            const int bh = (int)(u / p.nq), row = (int)(u % p.nq) * BQ + r;
+            const int64_t u = unit0 + i * ustride;
+            const int bh = (int)(u / p.nq), row = (int)(u % p.nq) * (PAIR ? 2 * BQ : BQ) + (int)rank * BQ + r;
             float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
             float o[64];
 #pragma unroll
@@ -463,7 +587,7 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&o_empty[fb]);
+                if (lane == 0) arrive_leader(&o_empty[fb]);
                 return true;
             };
             for (int j = 0; j < nkb && !s_fail; ++j, ++kb) {
@@ -530,7 +654,7 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&p_ready[b]);
+                if (lane == 0) arrive_leader(&p_ready[b]);
                 // fold the previous block's O while the tensor cores run this one
                 if (j > 0 && !fold(kb - 1, alpha_prev)) {
                     s_fail = 1;
@@ -573,15 +697,24 @@ attn_3xtf32_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             split_buf(smem_u32(smem), Q_BYTES / 16, Q_BYTES, wt);
             fence_proxy_async();
             __syncwarp();
-            if (lane == 0) mbar_arrive(q_conv);
+            if (lane == 0) arrive_leader(q_conv);
         }
     }
 
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) {
+        cluster_sync_any();   // no CTA leaves while the pair's MMAs or the other CTA's arrivals may touch it
+    } else {
+        __syncthreads();
+    }
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+        if constexpr (PAIR)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS)
+                         : "memory");
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS)
+                         : "memory");
     }
     if (threadIdx.x == 0 && s_fail) atomicOr(p.status, KX_TIMEOUT_FLAG);
 }
@@ -618,14 +751,19 @@ int run_attention_fused(Handle *h, const float *q, int64_t q_rs, int64_t q_bs, c
     if (rc) return rc;
     float *k_lo = static_cast<float *>(h->attn), *v_lo = k_lo + lo_elems;
     const uint64_t lo_bs = (uint64_t)sk * DH * 4;
+    // CTA pairs when there are enough 256-row units to keep the pairs busy:
+    // each CTA then stages 32 of a block's keys (a 32-row box of kt)
+    const int64_t pair_units = (sq + 2 * BQ - 1) / (2 * BQ) * nb;
+    const bool pair = pair_units >= h->sm_count / 2;
+    const uint32_t krows = pair ? BKEY / 2 : BKEY;
     CUtensorMap mq, mk, mv, mkl, mvl;
     if (!make_map(&mq, q, DH, (uint64_t)sq, (uint64_t)nb, (uint64_t)q_rs * 4, s2(q_bs, q_rs, sq), 16, BQ,
                   CU_TENSOR_MAP_SWIZZLE_64B) ||
-        !make_map(&mk, k, DH, (uint64_t)sk, (uint64_t)nb, (uint64_t)k_rs * 4, s2(k_bs, k_rs, sk), 16, BKEY,
+        !make_map(&mk, k, DH, (uint64_t)sk, (uint64_t)nb, (uint64_t)k_rs * 4, s2(k_bs, k_rs, sk), 16, krows,
                   CU_TENSOR_MAP_SWIZZLE_64B) ||
         !make_map(&mv, v, DH, (uint64_t)sk, (uint64_t)nb, (uint64_t)v_rs * 4, s2(v_bs, v_rs, sk), 32, 16,
                   CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
-        !make_map(&mkl, k_lo, DH, (uint64_t)sk, (uint64_t)nb, DH * 4, lo_bs, 16, BKEY, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map(&mkl, k_lo, DH, (uint64_t)sk, (uint64_t)nb, DH * 4, lo_bs, 16, krows, CU_TENSOR_MAP_SWIZZLE_64B) ||
         !make_map(&mvl, v_lo, DH, (uint64_t)sk, (uint64_t)nb, DH * 4, lo_bs, 32, 16,
                   CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
         return KX_DECLINED;
@@ -637,7 +775,7 @@ int run_attention_fused(Handle *h, const float *q, int64_t q_rs, int64_t q_bs, c
     pp.sq = (int)sq;
     pp.sk = (int)sk;
     pp.nbatch = (int)nb;
-    pp.nq = (int)((sq + BQ - 1) / BQ);
+    pp.nq = (int)(pair ? (sq + 2 * BQ - 1) / (2 * BQ) : (sq + BQ - 1) / BQ);
     pp.units = (int64_t)pp.nq * nb;
     pp.nkb = (int)((sk + BKEY - 1) / BKEY);
     const double cd = 1.4426950408889634 / (double)temperature;
@@ -646,20 +784,45 @@ int run_attention_fused(Handle *h, const float *q, int64_t q_rs, int64_t q_bs, c
     if (!std::isnormal(pp.c) || !std::isfinite(pp.c_lo)) return KX_DECLINED;
     pp.status = h->flags + kStatusWord;
     pp.flag = h->flags + kAttnFlagWord;
-    const int64_t grid = pp.units < h->sm_count ? pp.units : h->sm_count;
+    const int64_t slots = pair ? h->sm_count / 2 : h->sm_count;      // pairs, or CTAs
+    const int64_t grid = (pp.units < slots ? pp.units : slots) * (pair ? 2 : 1);
     const int64_t n4 = (int64_t)lo_elems / 4;
     const unsigned lo_grid = (unsigned)std::min<int64_t>((n4 + 255) / 256, 8LL * h->sm_count);
     split_lo_kernel<false><<<lo_grid, 256, 0, h->stream>>>(k, k_rs, k_bs, k_lo, sk, nb, pp.flag);
     split_lo_kernel<true><<<lo_grid, 256, 0, h->stream>>>(v, v_rs, v_bs, v_lo, sk, nb, pp.flag);
     h->launches += 2;
     cudaError_t ce = cudaGetLastError();
-    if (ce == cudaSuccess)
-        ce = cudaFuncSetAttribute(attn_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (ce == cudaSuccess) {
-        attn_3xtf32_kernel<<<(unsigned)grid, NT, SMEM_BYTES, h->stream>>>(mq, mk, mv, mkl, mvl, pp);
-        ce = cudaGetLastError();
+    if (pair) {
+        if (ce == cudaSuccess)
+            ce = cudaFuncSetAttribute(attn_3xtf32_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      SMEM_BYTES);
+        if (ce == cudaSuccess) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)grid, 1, 1);
+            cfg.blockDim = dim3(NT, 1, 1);
+            cfg.dynamicSmemBytes = SMEM_BYTES;
+            cfg.stream = h->stream;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 2;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            ce = cudaLaunchKernelEx(&cfg, attn_3xtf32_kernel<true>, mq, mk, mv, mkl, mvl, pp);
+            if (ce == cudaSuccess) ce = cudaGetLastError();
+        }
+        *kernel_name = "attn_3xtf32_pair_256x64";
+    } else {
+        if (ce == cudaSuccess)
+            ce = cudaFuncSetAttribute(attn_3xtf32_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      SMEM_BYTES);
+        if (ce == cudaSuccess) {
+            attn_3xtf32_kernel<false><<<(unsigned)grid, NT, SMEM_BYTES, h->stream>>>(mq, mk, mv, mkl, mvl, pp);
+            ce = cudaGetLastError();
+        }
+        *kernel_name = "attn_3xtf32_128x64";
     }
-    *kernel_name = "attn_3xtf32_128x64";
     ++h->launches;
     return ce == cudaSuccess ? KX_OK : h->cuda_fail(ce);
 }

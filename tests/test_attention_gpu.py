@@ -19,6 +19,7 @@ from kernix_b200 import rng
 
 pytestmark = pytest.mark.gpu
 FUSED = "attn_3xtf32_128x64"
+PAIR = "attn_3xtf32_pair_256x64"       # CTA pairs: chosen from 74 units of 256 query rows
 
 
 def _inputs(seed, nb, sq, sk, d=128, dv=128, std=1.0):
@@ -59,6 +60,45 @@ def test_fused_matches_exact_attention(kx, torch_cuda, nb, sq, sk):
     got = out.cpu().numpy()
     rows = None if sq <= 300 else sorted({0, 1, 127, 128, 1000, sq - 1})
     _check(got, q, k, v, t, rows)
+
+
+@pytest.mark.parametrize("nb,sq,sk", [(74, 256, 64), (40, 520, 1000), (38, 300, 33), (80, 129, 2048)])
+def test_pair_kernel_matches_exact_attention(kx, torch_cuda, nb, sq, sk):
+    """The CTA-pair kernel: query rows ending inside either CTA's half of a
+    256-row unit (520, 300, 129), key blocks ending inside either CTA's 32
+    keys (1000 = 15 blocks + 40, 33), and one key block in all (64, 33)."""
+    torch = torch_cuda
+    q, k, v = _inputs(200 + sq + sk, nb, sq, sk)
+    t = math.sqrt(128.0)
+    dq, dk, dv = _dev(torch, q, k, v)
+    out = kx.attention(dq, dk.transpose(1, 2), dv, t)
+    assert kx.handle(0).last_kernel == PAIR
+    got = out.cpu().numpy()
+    rows = sorted({r for r in (0, 1, 127, 128, 129, 255, 256, 300, 383, 384, 511, 512, sq - 1) if r < sq})
+    heads = [0, 1, nb // 2, nb - 1]
+    _check(got[heads], q[heads], k[heads], v[heads], t, rows)
+
+
+def test_pair_kernel_four_dim_heads_and_nonfinite_fallback(kx, torch_cuda):
+    """[2, 37, 256, 128] heads on CTA pairs, then an inf score in one head:
+    the composed path's NonFiniteInput, and the pair kernel again after it."""
+    torch = torch_cuda
+    q, k, v = _inputs(51, 74, 256, 192, std=0.5)
+    dq, dk, dv = _dev(torch, q.reshape(2, 37, 256, 128), k.reshape(2, 37, 192, 128), v.reshape(2, 37, 192, 128))
+    out = kx.attention(dq, dk.transpose(2, 3), dv, 0.9)
+    assert kx.handle(0).last_kernel == PAIR
+    heads = [0, 36, 37, 73]
+    _check(out.cpu().numpy().reshape(74, 256, 128)[heads], q[heads], k[heads], v[heads], 0.9)
+    q[40, 200, 3] = np.inf
+    dq, = _dev(torch, q.reshape(2, 37, 256, 128))
+    with pytest.raises(kx.NonFiniteInput) as e:
+        kx.attention(dq, dk.transpose(2, 3), dv, 0.9)
+    assert e.value.indices[:3] == [1, 3, 200]
+    q[40, 200, 3] = 0.25
+    dq, = _dev(torch, q.reshape(2, 37, 256, 128))
+    out = kx.attention(dq, dk.transpose(2, 3), dv, 0.9)
+    assert kx.handle(0).last_kernel == PAIR
+    _check(out.cpu().numpy().reshape(74, 256, 128)[[40]], q[[40]], k[[40]], v[[40]], 0.9)
 
 
 def test_fused_four_dim_batches_and_small_temperature(kx, torch_cuda):
