@@ -47,6 +47,10 @@
 // P_hi and P_lo; O buffer b at [256 + 128 b, 256 + 128 b + 128).
 // Every mbarrier wait is bounded (2 s); on expiry the kernel stops its loops,
 // waits for its own TMA copies, frees TMEM and sets the handle's status bit.
+// With at least 74 units of 256 query rows the same kernel runs on CTA pairs
+// (template PAIR, described at the kernel): the leader issues cta_group::2
+// MMAs for both CTAs' rows and each CTA stages half of every key and value
+// block; otherwise one CTA per SM as above.
 #include <algorithm>
 #include <cmath>
 #include <cstring>
