@@ -117,6 +117,56 @@ int run_gemm(Handle *h, GemmParams<T> p, const char **kernel_name) {
                     rc = run_gemm_tc_pair(h, p, kernel_name);
                 if (rc == KX_DECLINED) rc = run_gemm_tc(h, p, kernel_name);   // one-SM tiles
                 if (rc != KX_DECLINED) return rc;
+            } else if (h->f32_variant == KX_F32_AUTO && p.nbatch == 1 && !p.C_mc && p.K >= 256) {
+                // Too few tiles to fill the SMs: split K over the tensor-core
+                // kernel, describing the K slices as a batch (A's batch stride
+                // the slice width, B's that many rows, the partial products in
+                // the workspace) and summing the slices in increasing order.
+                // A single tile over a long K is latency-bound on one SM
+                // (about 4x its MMA time); slices of >= 64 k spread it out.
+                const int64_t tiles = ((p.M + 127) / 128) * ((p.N + 127) / 128);
+                int splits = 1;
+                while (tiles * splits * 2 <= sms && p.K % (int64_t)(splits * 2 * 16) == 0 &&
+                       p.K / (splits * 2) >= 64)
+                    splits *= 2;
+                // (a CTA's few microseconds of latency against 10-20 us for the
+                // SIMT split-K kernel on such shapes, measured: worth it from 32 CTAs)
+                if (splits >= 2 && tiles * splits >= 32) {
+                    const int kps = p.K / splits;
+                    const uint64_t need = (uint64_t)splits * p.M * p.N * sizeof(float);
+                    float *ws = nullptr;
+                    int rc = h->workspace(need, reinterpret_cast<void **>(&ws));
+                    if (rc) return rc;
+                    GemmParams<T> q = p;
+                    q.K = kps;
+                    q.C = ws;
+                    q.c_rs = p.N;
+                    q.c_cs = 1;
+                    q.nbatch = splits;
+                    q.batch.ndims = 1;
+                    q.batch.dims[0] = splits;
+                    q.batch.a_str[0] = (int64_t)kps * p.a_cs;
+                    q.batch.b_str[0] = (int64_t)kps * p.b_rs;
+                    q.batch.c_str[0] = (int64_t)p.M * p.N;
+                    if (tc_eligible(q)) {
+                        rc = run_gemm_tc(h, q, kernel_name);
+                        if (rc == KX_OK) {
+                            GemmParams<T> r = p;
+                            r.ws = ws;
+                            r.splits = splits;
+                            const int64_t total = (int64_t)p.M * p.N;
+                            int64_t blocks = (total + 255) / 256;
+                            if (blocks > 8LL * h->sm_count) blocks = 8LL * h->sm_count;
+                            splitk_reduce_kernel<T><<<(unsigned)blocks, 256, 0, h->stream>>>(r);
+                            ++h->launches;
+                            ce = cudaGetLastError();
+                            if (ce != cudaSuccess) return h->cuda_fail(ce);
+                            *kernel_name = "tc_3xtf32_splitk";
+                            return KX_OK;
+                        }
+                        if (rc != KX_DECLINED) return rc;
+                    }
+                }
             }
         }
     }

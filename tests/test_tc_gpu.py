@@ -247,6 +247,51 @@ def test_tc_short_k_box_edges_every_position(kx, torch_cuda, m, n, nb):
     h.synchronize()
 
 
+@pytest.mark.parametrize("m,k,n", [(512, 512, 512), (256, 1024, 256), (128, 4096, 128), (1024, 512, 1024),
+                                   (200, 768, 132)])
+def test_small_products_split_k_on_the_tensor_cores(kx, torch_cuda, m, k, n):
+    """Products with too few tiles to fill the SMs split K over the tensor-core
+    kernel (the K slices described as a batch) and sum the slices in order:
+    every output against the compensated oracle with the f32 bound."""
+    torch = torch_cuda
+    h = kx.handle(0)
+    h.set_f32_variant(0)
+    from kernix_b200 import rng
+    v = rng.uniform(131, m * k + k * n, -1, 1)
+    a_np, b_np = v[:m * k].reshape(m, k), v[m * k:].reshape(k, n)
+    c = kx.matmul(torch.from_numpy(a_np).cuda(), torch.from_numpy(b_np).cuda()).cpu().numpy()
+    assert h.last_kernel == "tc_3xtf32_splitk", h.last_kernel
+    want, absum = oracle.gemm_dot2(oracle.View.of(a_np), oracle.View.of(b_np))
+    assert (np.abs(c.astype(np.float64) - want) <= 2e-6 * absum + 1e-30).all()
+
+
+def test_split_k_nonfinite_and_uneven_k(kx, torch_cuda):
+    """inf and NaN in A propagate through the split slices as through one
+    f32 accumulation; a K the slices cannot divide evenly keeps the SIMT
+    split-K kernel."""
+    torch = torch_cuda
+    h = kx.handle(0)
+    h.set_f32_variant(0)
+    rs = np.random.default_rng(3)
+    a = rs.uniform(-1, 1, (512, 512)).astype(np.float32)
+    b = rs.uniform(-1, 1, (512, 512)).astype(np.float32)
+    a[7, 300] = np.inf
+    a[9, 10] = np.nan
+    c = kx.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()).cpu().numpy()
+    assert h.last_kernel == "tc_3xtf32_splitk"
+    assert np.isnan(c[9]).all()
+    assert np.array_equal(np.isinf(c[7]), b[300] != 0) and not np.isnan(c[7][b[300] != 0]).any()
+    fin = np.ones(512, bool)
+    fin[[7, 9]] = False
+    assert np.isfinite(c[fin]).all()
+    a2 = rs.uniform(-1, 1, (512, 520)).astype(np.float32)
+    b2 = rs.uniform(-1, 1, (520, 512)).astype(np.float32)
+    c2 = kx.matmul(torch.from_numpy(a2).cuda(), torch.from_numpy(b2).cuda()).cpu().numpy()
+    assert h.last_kernel.startswith("simt"), h.last_kernel
+    want, absum = oracle.gemm_dot2(oracle.View.of(a2), oracle.View.of(b2))
+    assert (np.abs(c2.astype(np.float64) - want) <= 2e-6 * absum + 1e-30).all()
+
+
 def test_tc_short_k_persistent(kx, torch_cuda):
     """K <= 1024 over many tiles: the persistent kernel (TMEM double-buffered,
     epilogue overlapping the next tile) -- attention scores Q K^T with a
