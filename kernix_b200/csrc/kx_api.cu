@@ -425,12 +425,6 @@ int kx_destroy(kx_handle *hh) {
             if (h.peer_done[r]) cudaEventDestroy(h.peer_done[r]);
         }
         if (h.peer_ready) cudaEventDestroy(h.peer_ready);
-        if (h.aux) {
-            cudaStreamSynchronize(h.aux);
-            cudaStreamDestroy(h.aux);
-        }
-        for (auto &e : h.aux_ev)
-            if (e) cudaEventDestroy(e);
         cudaFree(h.tail);
         if (h.h2d) cudaStreamDestroy(h.h2d);
         if (h.d2h) cudaStreamDestroy(h.d2h);

@@ -88,8 +88,7 @@ int run_gemm(Handle *h, GemmParams<T> p, const char **kernel_name) {
         // Split-TF32 tensor-core path: eligible layouts, enough 128x256 tiles to
         // fill the machine, and not the ordered (bitwise reference) mode.
         if (!h->ordered && h->f32_variant != KX_F32_FFMA && tc_eligible(p)) {
-            // SMs this launch plans for: all, or a share when another GEMM runs beside it
-            const int64_t sms = h->sm_budget > 0 ? h->sm_budget : h->sm_count;
+            const int64_t sms = h->sm_count;
             const int64_t tc_tiles = (int64_t)((p.M + 127) / 128) * ((p.N + 255) / 256) * p.nbatch;
             const bool big = tc_tiles >= sms / 2 && p.K >= 64;
             if (h->f32_variant == KX_F32_3XTF32 || h->f32_variant == KX_F32_3XTF32_1SM || big) {

@@ -48,15 +48,10 @@ struct Handle {
     cudaStream_t peer_stream[kMaxWorld] = {};
     cudaEvent_t peer_ready = nullptr;
     cudaEvent_t peer_done[kMaxWorld] = {};
-    // The last piece of a row-sharded product runs as two row halves, each as
-    // two K halves on two streams at once (kx_sharded.cu): the second stream,
-    // its events, the K-half partial sums, and the SM count the GEMM
-    // dispatcher plans waves for while two GEMMs share the machine (0: all).
-    cudaStream_t aux = nullptr;
-    cudaEvent_t aux_ev[4] = {};
+    // The K-half partial products of a row-sharded product's split last piece
+    // (kx_sharded.cu).
     void *tail = nullptr;
     uint64_t tail_bytes = 0;
-    int sm_budget = 0;
     cudaEvent_t ev[3 * kMaxPieces + 2] = {};
 
     int cuda_fail(cudaError_t ce) {

@@ -45,35 +45,26 @@ bool push_streams(Handle *h) {
     return cudaEventCreateWithFlags(&h->peer_ready, cudaEventDisableTiming) == cudaSuccess;
 }
 
-// The second stream and the events of the split last piece, created on first use.
-bool tail_streams(Handle *h) {
-    if (h->aux) return true;
-    for (auto &e : h->aux_ev)
-        if (!e && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return false;
-    return cudaStreamCreateWithFlags(&h->aux, cudaStreamNonBlocking) == cudaSuccess;
-}
-
-// c[i] += p[i] for n floats of two C-contiguous row blocks.
-__global__ void tail_add_kernel(float *__restrict__ c, const float *__restrict__ p, uint64_t n) {
+// c[i] = p0[i] + p1[i] for n floats (C-contiguous row blocks): the two K
+// halves of the split last piece, summed into the output rows.
+__global__ void tail_sum_kernel(float *__restrict__ c, const float *__restrict__ p0, const float *__restrict__ p1,
+                                uint64_t n) {
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t i0 = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
     uint64_t done = 0;
-    if (((reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(p)) & 15) == 0) {
+    if (((reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(p0) | reinterpret_cast<uintptr_t>(p1)) & 15) ==
+        0) {
         float4 *c4 = reinterpret_cast<float4 *>(c);
-        const float4 *p4 = reinterpret_cast<const float4 *>(p);
+        const float4 *a4 = reinterpret_cast<const float4 *>(p0);
+        const float4 *b4 = reinterpret_cast<const float4 *>(p1);
         const uint64_t n4 = n / 4;
         for (uint64_t j = i0; j < n4; j += stride) {
-            float4 x = c4[j];
-            const float4 y = p4[j];
-            x.x += y.x;
-            x.y += y.y;
-            x.z += y.z;
-            x.w += y.w;
-            c4[j] = x;
+            const float4 x = a4[j], y = b4[j];
+            c4[j] = make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
         }
         done = n4 * 4;
     }
-    for (uint64_t j = done + i0; j < n; j += stride) c[j] += p[j];
+    for (uint64_t j = done + i0; j < n; j += stride) c[j] = p0[j] + p1[j];
 }
 
 // The last piece's fan-out below this many bytes (all peers together) costs
@@ -167,75 +158,59 @@ int kx_matmul_rows_sharded_f32(kx_handle *hh, const kx_tensor *a_local, const kx
         return kx_peer_broadcast(hh, src, dsts, nd, bytes, err);
     };
     // The last piece's push has no GEMM left to hide behind.  When its fan-out
-    // is large, the piece runs as two row halves, each as its two K halves at
-    // once (the handle's stream and a second one, each planned for half the
-    // SMs: one wave between them), summed by a small kernel; the first half's
-    // rows then go out on the copy engines while the second half multiplies,
-    // and only the second half's push is exposed.
+    // is large, the piece runs as two row halves, each ONE batched GEMM whose
+    // batch is its two K halves (the same number of CTAs as the whole piece:
+    // one wave, half as long), the halves' partial products summed into the
+    // output rows by a small kernel; the first half's rows then go out on the
+    // copy engines while the second half multiplies, and only the second
+    // half's push is exposed.
     const uint64_t k = a_local->dims[1];
     const bool tail_split = push && !h->ordered && h->f32_variant == KX_F32_AUTO && piece % 256 == 0 &&
                             k % 8 == 0 && k >= 2048 && (uint64_t)(world - 1) * piece * row_bytes >= kTailSplitBytes;
-    if (tail_split) {
-        if (!tail_streams(h)) return set_err(err, KX_E_CUDA, kOp, "cannot create the second stream");
-        if (h->grow(&h->tail, &h->tail_bytes, piece * row_bytes)) return cuda_err(err, h, kOp);
-    }
+    if (tail_split && h->grow(&h->tail, &h->tail_bytes, piece * row_bytes)) return cuda_err(err, h, kOp);
     for (uint64_t i = 0; i < pieces; ++i) {
         const uint64_t g0 = (i * world + rank) * piece;       // global rows of this piece
         if (i + 1 == pieces && tail_split) {
             const uint64_t hr = piece / 2, kh = k / 2;
-            float *part = static_cast<float *>(h->tail);
-            // the second stream starts after everything the handle's stream holds so far
-            cudaError_t ce = cudaEventRecord(h->aux_ev[0], h->stream);
-            if (ce == cudaSuccess) ce = cudaStreamWaitEvent(h->aux, h->aux_ev[0], 0);
-            if (ce != cudaSuccess) {
-                h->cuda_fail(ce);
-                return cuda_err(err, h, kOp);
-            }
+            float *part = static_cast<float *>(h->tail);      // [2][hr][n]: the two K halves
             for (uint64_t half = 0; half < 2; ++half) {
                 const uint64_t lr = i * piece + half * hr, gr = g0 + half * hr;
-                kx_tensor a1 = *a_local;                      // rows, first K half
-                a1.dims[0] = hr;
-                a1.dims[1] = kh;
-                a1.origin = a_local->origin + (uint64_t)((int64_t)lr * a_local->strides[0]);
-                kx_tensor a2 = a1;                            // second K half
-                a2.origin = a1.origin + (uint64_t)((int64_t)kh * a_local->strides[1]);
-                kx_tensor b1 = *b;
-                b1.dims[0] = kh;
-                kx_tensor b2 = b1;
-                b2.origin = b->origin + (uint64_t)((int64_t)kh * b->strides[0]);
-                kx_tensor c1 = *out;
-                c1.dims[0] = hr;
-                c1.origin = out->origin + gr * n;
-                kx_tensor p2;
-                std::memset(&p2, 0, sizeof(p2));
-                p2.data = part + half * hr * n;
-                p2.storage_len = hr * n;
-                p2.rank = 2;
-                p2.dims[0] = hr;
-                p2.dims[1] = n;
-                p2.strides[0] = (int64_t)n;
-                p2.strides[1] = 1;
-                const int budget = h->sm_budget;
-                h->sm_budget = h->sm_count / 2;
-                int rc = kx_matmul_f32(hh, &a1, &b1, &c1, err);
-                if (rc == KX_OK) {
-                    cudaStream_t main_stream = h->stream;
-                    h->stream = h->aux;
-                    rc = kx_matmul_f32(hh, &a2, &b2, &p2, err);
-                    h->stream = main_stream;
-                }
-                h->sm_budget = budget;
+                kx_tensor a3 = *a_local;                      // [2, hr, kh]: K halves as a batch
+                a3.rank = 3;
+                a3.dims[0] = 2;
+                a3.dims[1] = hr;
+                a3.dims[2] = kh;
+                a3.strides[0] = (int64_t)kh * a_local->strides[1];
+                a3.strides[1] = a_local->strides[0];
+                a3.strides[2] = a_local->strides[1];
+                a3.origin = a_local->origin + (uint64_t)((int64_t)lr * a_local->strides[0]);
+                kx_tensor b3 = *b;                            // [2, kh, n]
+                b3.rank = 3;
+                b3.dims[0] = 2;
+                b3.dims[1] = kh;
+                b3.dims[2] = n;
+                b3.strides[0] = (int64_t)kh * b->strides[0];
+                b3.strides[1] = b->strides[0];
+                b3.strides[2] = b->strides[1];
+                kx_tensor p3;
+                std::memset(&p3, 0, sizeof(p3));
+                p3.data = part;
+                p3.storage_len = 2 * hr * n;
+                p3.rank = 3;
+                p3.dims[0] = 2;
+                p3.dims[1] = hr;
+                p3.dims[2] = n;
+                p3.strides[0] = (int64_t)(hr * n);
+                p3.strides[1] = (int64_t)n;
+                p3.strides[2] = 1;
+                int rc = kx_matmul_f32(hh, &a3, &b3, &p3, err);
                 if (rc) return rc;
-                ce = cudaEventRecord(h->aux_ev[1 + half], h->aux);
-                if (ce == cudaSuccess) ce = cudaStreamWaitEvent(h->stream, h->aux_ev[1 + half], 0);
-                if (ce == cudaSuccess) {
-                    const uint64_t total = hr * n;
-                    uint64_t blocks = (total / 4 + 255) / 256;
-                    blocks = std::max<uint64_t>(1, std::min<uint64_t>(blocks, 4ull * h->sm_count));
-                    tail_add_kernel<<<(unsigned)blocks, 256, 0, h->stream>>>(c + gr * n, part + half * hr * n, total);
-                    ++h->launches;
-                    ce = cudaGetLastError();
-                }
+                const uint64_t total = hr * n;
+                uint64_t blocks = (total / 4 + 255) / 256;
+                blocks = std::max<uint64_t>(1, std::min<uint64_t>(blocks, 4ull * h->sm_count));
+                tail_sum_kernel<<<(unsigned)blocks, 256, 0, h->stream>>>(c + gr * n, part, part + total, total);
+                ++h->launches;
+                const cudaError_t ce = cudaGetLastError();
                 if (ce != cudaSuccess) {
                     h->cuda_fail(ce);
                     return cuda_err(err, h, kOp);
