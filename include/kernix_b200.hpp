@@ -11,6 +11,13 @@
 //   kernix::DeviceTensor<T>        Tensor<T, Kahen, Buffer> with an opaque device buffer
 //                                  and an affine layout (dims, signed strides, origin)
 //   kernix::OpsError               crates/kernix-ops/src/ops/error.rs:8-140
+//   kernix::CudaConfig / Context   the [cuda] table of kernix::config (config.rs:28-40, 133-137)
+//   CudaExecutor::{softmax, softmax_temperature, attention, tensordot,
+//                  matmul_backward, conv2d_backward, matmul_into}
+//                                  math.rs:531-536, math_extra.rs:544-557,
+//                                  linalg_extra.rs:164-276, autograd.rs:622-690,
+//                                  neural.rs:379-430, execution.rs:149-240
+//   kernix::shard_window / row_piece   the work split across the GPUs of a node
 // Errors are exceptions carrying the C ABI's kx_error record; hooks return bool
 // exactly like the reference (false => nothing written).
 #pragma once
@@ -55,12 +62,22 @@ template <> struct Fns<float> {
     static constexpr auto strided = kx_try_strided_matmul_f32;
     static constexpr auto matmul = kx_matmul_f32;
     static constexpr auto conv2d = kx_conv2d_f32;
+    static constexpr auto softmax = kx_softmax_f32;
+    static constexpr auto softmax_temperature = kx_softmax_temperature_f32;
+    static constexpr auto tensordot = kx_tensordot_f32;
+    static constexpr auto matmul_backward = kx_matmul_backward_f32;
+    static constexpr auto conv2d_backward = kx_conv2d_backward_f32;
 };
 template <> struct Fns<double> {
     static constexpr auto dense = kx_try_dense_matmul_f64;
     static constexpr auto strided = kx_try_strided_matmul_f64;
     static constexpr auto matmul = kx_matmul_f64;
     static constexpr auto conv2d = kx_conv2d_f64;
+    static constexpr auto softmax = kx_softmax_f64;
+    static constexpr auto softmax_temperature = kx_softmax_temperature_f64;
+    static constexpr auto tensordot = kx_tensordot_f64;
+    static constexpr auto matmul_backward = kx_matmul_backward_f64;
+    static constexpr auto conv2d_backward = kx_conv2d_backward_f64;
 };
 }  // namespace detail
 
@@ -89,6 +106,13 @@ class MatrixInput {
     kx_matrix m_;
 };
 
+// The [cuda] table of a configuration (kx_cuda_config); defaults as an
+// absent table: device 0, automatic kernel families, native products.
+struct CudaConfig {
+    kx_cuda_config c;
+    CudaConfig() { kx_cuda_config_default(&c); }
+};
+
 // One handle per device; movable, not copyable.
 class Handle {
   public:
@@ -96,15 +120,38 @@ class Handle {
         kx_error e{};
         check(kx_create(device, &h_, &e), e);
     }
+    // Context::new for the [cuda] table: every key is validated before any
+    // device work (OpsError with KX_E_PARAM naming the key).
+    explicit Handle(const CudaConfig &cfg) {
+        kx_error e{};
+        check(kx_context_create(&cfg.c, &h_, &e), e);
+    }
     ~Handle() { kx_destroy(h_); }
     Handle(const Handle &) = delete;
     Handle &operator=(const Handle &) = delete;
     Handle(Handle &&o) noexcept : h_(std::exchange(o.h_, nullptr)) {}
     kx_handle *get() const { return h_; }
+    CudaConfig config() const {
+        CudaConfig cfg;
+        kx_handle_config(h_, &cfg.c);
+        return cfg;
+    }
 
   private:
     kx_handle *h_ = nullptr;
 };
+
+// Work split across the GPUs of one node (kx_shard_window, kx_row_piece).
+inline std::pair<uint64_t, uint64_t> shard_window(uint64_t total, uint32_t rank, uint32_t world) {
+    uint64_t start = 0, count = 0;
+    check(kx_shard_window(total, rank, world, &start, &count), kx_error{});
+    return {start, count};
+}
+inline std::pair<uint64_t, uint64_t> row_piece(uint64_t m, uint32_t world, uint64_t target) {
+    uint64_t piece = 0, pieces = 0;
+    check(kx_row_piece(m, world, target, &piece, &pieces), kx_error{});
+    return {piece, pieces};
+}
 
 // MatmulElement hooks on HOST buffers.  The handle is the device the product
 // runs on; false means nothing was written.
@@ -198,6 +245,9 @@ class DeviceTensor {
 class CudaExecutor {
   public:
     explicit CudaExecutor(int device = 0) : h_(device), device_(device) {}
+    // A context's executor: the [cuda] table's device, kernel families and
+    // ordered mode (Context::new, config.rs:133-137).
+    explicit CudaExecutor(const CudaConfig &cfg) : h_(cfg), device_(cfg.c.device) {}
     const char *name() const { return "cuda"; }
     int device() const { return device_; }
     kx_handle *handle() const { return h_.get(); }
@@ -233,6 +283,20 @@ class CudaExecutor {
         kx_error e{};
         check(kx_synchronize(h_.get(), &e), e);
     }
+    // A fresh C-order device tensor of `dims` (Kernix allocates every result so).
+    template <typename T>
+    DeviceTensor<T> empty(std::vector<uint64_t> dims) const {
+        size_t n = 1;
+        for (auto d : dims) n *= d;
+        auto buf = std::make_shared<DeviceBuffer<T>>(h_.get(), n ? n : 1);
+        std::vector<int64_t> strides(dims.size());
+        int64_t acc = 1;
+        for (size_t i = dims.size(); i-- > 0;) {
+            strides[i] = acc;
+            acc *= (int64_t)(dims[i] ? dims[i] : 1);
+        }
+        return DeviceTensor<T>(buf, std::move(dims), std::move(strides), 0);
+    }
     // MatmulDevice::matmul: NumPy matmul semantics into a fresh C-order tensor.
     template <typename T>
     DeviceTensor<T> matmul(const DeviceTensor<T> &a, const DeviceTensor<T> &b) const {
@@ -242,21 +306,97 @@ class CudaExecutor {
         check(kx_matmul_shape(a.dims().data(), (uint32_t)a.dims().size(), b.dims().data(),
                               (uint32_t)b.dims().size(), &rank, od, &e),
               e);
-        std::vector<uint64_t> dims(od, od + rank);
-        size_t n = 1;
-        for (auto d : dims) n *= d;
-        auto buf = std::make_shared<DeviceBuffer<T>>(h_.get(), n ? n : 1);
-        std::vector<int64_t> strides(rank);
-        int64_t acc = 1;
-        for (size_t i = rank; i-- > 0;) {
-            strides[i] = acc;
-            acc *= (int64_t)(dims[i] ? dims[i] : 1);
-        }
-        DeviceTensor<T> out(buf, dims, strides, 0);
-        kx_tensor da = a.desc(), db = b.desc(), dc = out.desc();
-        dc.storage_len = n;
-        check(detail::Fns<T>::matmul(h_.get(), &da, &db, &dc, &e), e);
+        auto out = empty<T>(std::vector<uint64_t>(od, od + rank));
+        matmul_into(a, b, out);
         return out;
+    }
+    // CpuExecutor::matmul_into's contract: the caller's C-contiguous output is
+    // reused, nothing allocated (execution.rs:149-240).
+    template <typename T>
+    void matmul_into(const DeviceTensor<T> &a, const DeviceTensor<T> &b, const DeviceTensor<T> &out) const {
+        kx_error e{};
+        kx_tensor da = a.desc(), db = b.desc(), dc = out.desc();
+        check(detail::Fns<T>::matmul(h_.get(), &da, &db, &dc, &e), e);
+    }
+    // softmax (math.rs:531-536) and softmax_temperature (math_extra.rs:544-557).
+    template <typename T>
+    DeviceTensor<T> softmax(const DeviceTensor<T> &src, int64_t axis) const {
+        auto out = empty<T>(src.dims());
+        kx_error e{};
+        kx_tensor ds = src.desc(), dout = out.desc();
+        check(detail::Fns<T>::softmax(h_.get(), &ds, axis, &dout, &e), e);
+        return out;
+    }
+    template <typename T>
+    DeviceTensor<T> softmax_temperature(const DeviceTensor<T> &src, int64_t axis, T temperature) const {
+        auto out = empty<T>(src.dims());
+        kx_error e{};
+        kx_tensor ds = src.desc(), dout = out.desc();
+        check(detail::Fns<T>::softmax_temperature(h_.get(), &ds, axis, temperature, &dout, &e), e);
+        return out;
+    }
+    // matmul(softmax_temperature(matmul(q, kt), -1, t), v) in one call (f32).
+    DeviceTensor<float> attention(const DeviceTensor<float> &q, const DeviceTensor<float> &kt,
+                                  const DeviceTensor<float> &v, float temperature) const {
+        kx_error e{};
+        uint32_t r1 = 0, r2 = 0;
+        uint64_t sd[KX_MAX_RANK], od[KX_MAX_RANK];
+        check(kx_matmul_shape(q.dims().data(), (uint32_t)q.dims().size(), kt.dims().data(),
+                              (uint32_t)kt.dims().size(), &r1, sd, &e),
+              e);
+        check(kx_matmul_shape(sd, r1, v.dims().data(), (uint32_t)v.dims().size(), &r2, od, &e), e);
+        auto out = empty<float>(std::vector<uint64_t>(od, od + r2));
+        kx_tensor dq = q.desc(), dk = kt.desc(), dv = v.desc(), dout = out.desc();
+        check(kx_attention_f32(h_.get(), &dq, &dk, &dv, temperature, &dout, &e), e);
+        return out;
+    }
+    // tensordot (linalg_extra.rs:164-276): a's free axes, then b's.
+    template <typename T>
+    DeviceTensor<T> tensordot(const DeviceTensor<T> &a, const DeviceTensor<T> &b, const std::vector<int64_t> &a_axes,
+                              const std::vector<int64_t> &b_axes) const {
+        std::vector<bool> ca(a.dims().size()), cb(b.dims().size());
+        for (auto x : a_axes) {
+            const int64_t i = x < 0 ? x + (int64_t)ca.size() : x;
+            if (i >= 0 && i < (int64_t)ca.size()) ca[i] = true;
+        }
+        for (auto x : b_axes) {
+            const int64_t i = x < 0 ? x + (int64_t)cb.size() : x;
+            if (i >= 0 && i < (int64_t)cb.size()) cb[i] = true;
+        }
+        std::vector<uint64_t> dims;
+        for (size_t i = 0; i < ca.size(); ++i)
+            if (!ca[i]) dims.push_back(a.dims()[i]);
+        for (size_t i = 0; i < cb.size(); ++i)
+            if (!cb[i]) dims.push_back(b.dims()[i]);
+        auto out = empty<T>(dims.size() <= KX_MAX_RANK ? dims : std::vector<uint64_t>{});
+        kx_error e{};
+        kx_tensor da = a.desc(), db = b.desc(), dout = out.desc();
+        check(detail::Fns<T>::tensordot(h_.get(), &da, &db, a_axes.data(), (uint32_t)a_axes.size(), b_axes.data(),
+                                        (uint32_t)b_axes.size(), &dout, &e),
+              e);
+        return out;
+    }
+    // Tape::matmul's VJP (autograd.rs:622-690): (grad b^T, a^T grad) with
+    // broadcast batches summed back.
+    template <typename T>
+    std::pair<DeviceTensor<T>, DeviceTensor<T>> matmul_backward(const DeviceTensor<T> &a, const DeviceTensor<T> &b,
+                                                                const DeviceTensor<T> &grad) const {
+        auto ga = empty<T>(a.dims()), gb = empty<T>(b.dims());
+        kx_error e{};
+        kx_tensor da = a.desc(), db = b.desc(), dg = grad.desc(), dga = ga.desc(), dgb = gb.desc();
+        check(detail::Fns<T>::matmul_backward(h_.get(), &da, &db, &dg, &dga, &dgb, &e), e);
+        return {ga, gb};
+    }
+    // conv2d_backward (neural.rs:379-430): input and weight gradients.
+    template <typename T>
+    std::pair<DeviceTensor<T>, DeviceTensor<T>> conv2d_backward(const DeviceTensor<T> &x, const DeviceTensor<T> &w,
+                                                                const DeviceTensor<T> &grad,
+                                                                const kx_conv2d_options &opts) const {
+        auto gx = empty<T>(x.dims()), gw = empty<T>(w.dims());
+        kx_error e{};
+        kx_tensor dx = x.desc(), dw = w.desc(), dg = grad.desc(), dgx = gx.desc(), dgw = gw.desc();
+        check(detail::Fns<T>::conv2d_backward(h_.get(), &dx, &dw, &dg, &opts, &dgx, &dgw, &e), e);
+        return {gx, gw};
     }
 
   private:

@@ -1,8 +1,11 @@
 // Exercises the C++ host mirror (include/kernix_b200.hpp) the way Kernix's own
 // tests exercise the Rust API.  `--host` needs no GPU; `--gpu` runs on device 0.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
+#include <string>
+#include <utility>
 #include <vector>
 
 #include "kernix_b200.hpp"
@@ -37,6 +40,21 @@ static void host_checks() {
     std::vector<float> out(64, 7.0f), x(16, 1.0f), y(63, 2.0f);
     EXPECT(kx_try_dense_matmul_f32(nullptr, x.data(), 16, y.data(), 63, out.data(), 64, 4, 4, 16) == KX_DECLINED);
     for (float v : out) EXPECT(v == 7.0f);
+    // the [cuda] table is validated key by key before any device work
+    kernix::CudaConfig bad;
+    bad.c.f32_variant = 9;
+    threw = false;
+    try {
+        kernix::Handle h(bad);
+    } catch (const kernix::OpsError &e) {
+        threw = e.status() == KX_E_PARAM && std::string(e.record().parameter) == "cuda.f32_variant is not a kernel family";
+    }
+    EXPECT(threw);
+    // work split across the GPUs of a node
+    using U2 = std::pair<uint64_t, uint64_t>;
+    EXPECT((kernix::shard_window(16, 0, 3) == U2(0, 6)));
+    EXPECT((kernix::shard_window(16, 2, 3) == U2(11, 5)));
+    EXPECT((kernix::row_piece(8192, 8, 512) == U2(512, 2)));
 }
 
 static void gpu_checks() {
@@ -84,6 +102,66 @@ static void gpu_checks() {
     // ordered mode is available and reported
     cuda.with_ordered_matmul(true);
     EXPECT(cuda.ordered_matmul());
+    cuda.with_ordered_matmul(false);
+    // tensordot (ops_completeness_03.rs:224-237)
+    auto tx = cuda.upload<double>({1, 2, 3, 4, 5, 6}, {2, 3});
+    auto ty = cuda.upload<double>({1, 0, 0, 0, 1, 0, 0, 0, 1, 1, 1, 1}, {4, 3});
+    auto tz = cuda.download(cuda.tensordot(tx, ty, {1}, {1}));
+    EXPECT(tz == std::vector<double>({1, 2, 3, 6, 4, 5, 6, 15}));
+    // softmax of [0, ln 3]: [1/4, 3/4] (math.rs:531-536)
+    auto sm = cuda.download(cuda.softmax(cuda.upload<double>({0.0, std::log(3.0)}, {1, 2}), -1));
+    EXPECT(std::fabs(sm[0] - 0.25) < 1e-15 && std::fabs(sm[1] - 0.75) < 1e-15);
+    // matmul VJP with grad = ones: dA rows are B's row sums, dB columns A's column sums (exact)
+    auto va = cuda.upload<double>({1, 2, 3, 4, 5, 6}, {2, 3});
+    auto vb = cuda.upload<double>({0.5, -1, 2, 0.25, 1, 1}, {3, 2});
+    auto g = cuda.matmul_backward(va, vb, cuda.upload<double>({1, 1, 1, 1}, {2, 2}));
+    EXPECT(cuda.download(g.first) == std::vector<double>({-0.5, 2.25, 2, -0.5, 2.25, 2}));
+    EXPECT(cuda.download(g.second) == std::vector<double>({5, 5, 7, 7, 9, 9}));
+    // attention products against the host: out = softmax(q k^T / T) v
+    const int sq = 5, sk = 7, d = 128;
+    std::vector<float> q(sq * d), kk(sk * d), v(sk * d);
+    for (int i = 0; i < sq * d; ++i) q[i] = (float)((i * 37 % 101) - 50) / 64.0f;
+    for (int i = 0; i < sk * d; ++i) kk[i] = (float)((i * 53 % 97) - 48) / 64.0f;
+    for (int i = 0; i < sk * d; ++i) v[i] = (float)((i * 29 % 89) - 44) / 32.0f;
+    const float temp = 11.3137085f;
+    auto dq = cuda.upload<float>(q, {1, (uint64_t)sq, (uint64_t)d});
+    auto dkt = cuda.upload<float>(kk, {1, (uint64_t)sk, (uint64_t)d}).swap_axes(1, 2);
+    auto dv = cuda.upload<float>(v, {1, (uint64_t)sk, (uint64_t)d});
+    auto att = cuda.download(cuda.attention(dq, dkt, dv, temp));
+    for (int i = 0; i < sq; ++i) {
+        std::vector<double> s(sk), pr(sk);
+        double mx = -1e300, sum = 0;
+        for (int j = 0; j < sk; ++j) {
+            for (int c = 0; c < d; ++c) s[j] += (double)q[i * d + c] * kk[j * d + c];
+            mx = std::max(mx, s[j]);
+        }
+        for (int j = 0; j < sk; ++j) sum += (pr[j] = std::exp((s[j] - mx) / temp));
+        for (int c = 0; c < d; ++c) {
+            double o = 0, ab = 0;
+            for (int j = 0; j < sk; ++j) {
+                o += pr[j] / sum * v[j * d + c];
+                ab += pr[j] / sum * std::fabs(v[j * d + c]);
+            }
+            EXPECT(std::fabs(att[i * d + c] - o) <= 1e-4 * ab + 1e-12);
+        }
+    }
+    // a context from the [cuda] table: ordered products (bit for bit the ordered sums)
+    kernix::CudaConfig cfg;
+    cfg.c.ordered_matmul = 1;
+    kernix::CudaExecutor ordered(cfg);
+    EXPECT(ordered.ordered_matmul());
+    kernix::Handle hc(cfg);
+    EXPECT(hc.config().c.ordered_matmul == 1 && hc.config().c.device == 0);
+    auto oa = ordered.upload<float>({0.1f, 0.2f, 0.3f}, {1, 3});
+    auto ob = ordered.upload<float>({0.7f, 0.11f, 0.13f}, {3, 1});
+    auto ov1 = ordered.download(ordered.matmul(oa, ob));
+    float acc = 0.0f;
+    const float ta[3] = {0.1f, 0.2f, 0.3f}, tb[3] = {0.7f, 0.11f, 0.13f};
+    for (int i = 0; i < 3; ++i) {
+        volatile float prod = ta[i] * tb[i];        // separately rounded, as matmul_reference
+        acc = acc + prod;
+    }
+    EXPECT(ov1.size() == 1 && ov1[0] == acc);
 }
 
 int main(int argc, char **argv) {
