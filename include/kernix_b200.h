@@ -400,8 +400,13 @@ int kx_row_piece(uint64_t m, uint32_t world, uint64_t target_piece, uint64_t *pi
  * engines while the next piece multiplies, and the last piece either through
  * `out_mc`, the NVLink multicast address of `out`'s storage (one store, the
  * NVSwitch delivers it to every rank), or, when that is null, by a kernel on
- * all SMs.  Every rank's `out` has the same layout.  Returns once the work is
- * enqueued on the handle's stream; when every rank's call has completed on its
+ * all SMs.  Up to 4 GPUs, when the last piece's fan-out ((world - 1) x piece
+ * rows) is at least 32 MB and the piece a multiple of 256 rows, the last
+ * piece runs as two row halves, each one GEMM batched over its two K halves
+ * into the handle's scratch plus a summing kernel, and the first half is
+ * pushed while the second multiplies.  Every rank's `out` has the same
+ * layout.  Returns once the work is enqueued on the handle's stream; when
+ * every rank's call has completed on its
  * device (the caller orders that: a collective after the call, or
  * kx_synchronize on every rank and a host barrier), every rank's `out` holds
  * the whole product.  peer_out NULL: only this rank's rows are written. */
