@@ -1,0 +1,120 @@
+"""More of the reference's own tests on the device path.
+
+* batched_forward_matmul (kernix/tests/api_ergonomics.rs:25-31);
+* explicit_layout_policy_and_reusable_output (api_ergonomics.rs:105-117):
+  ordered matmul_into into a reused output, through a context made from
+  ``[cpu] ordered_matmul = true``;
+* matmul_and_dense_shared_parameter_gradients and
+  convolution_and_pooling_gradients (kernix/tests/autograd_tests.rs:142-167):
+  the backward products against central differences of sum(y * seed), seed_i =
+  0.3 + 0.11 i, h = 1e-6, |analytic - numeric| < 2e-6 (1 + |a| + |n|)
+  (autograd_tests.rs:7-12, 55-100);
+* the reconstruction check of cholesky_layouts_scales_branch_boundaries
+  (kernix-ops/tests/factorization_regressions.rs:39-61): matmul_reference(L,
+  L^T view) at scales 1e-200, 1, 1e200 -- bit for bit the oracle's ordered
+  product, and within 1e-12 * scale of the original matrix.
+"""
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(torch, arr):
+    return torch.from_numpy(np.array(arr, order="C")).cuda()
+
+
+def test_batched_forward_matmul(kx, torch_cuda):
+    torch = torch_cuda
+    c = kx.matmul(torch.ones(2, 2, 3, device="cuda"), torch.ones(3, 2, device="cuda"))
+    assert tuple(c.shape) == (2, 2, 2) and c.cpu().numpy().reshape(-1).tolist() == [3.0] * 8
+
+
+def test_ordered_matmul_into_reuses_the_output(kx, torch_cuda):
+    torch = torch_cuda
+    column_major = np.array([1.0, 3.0, 2.0, 4.0]).reshape(2, 2).T      # Order::F [[1, 2], [3, 4]]
+    a = dev(torch, np.ascontiguousarray(column_major))
+    out = torch.zeros(2, 2, dtype=torch.float64, device="cuda")
+    pointer = out.data_ptr()
+    ctx = kx.Context.new(kx.Config.from_toml("[cpu]\nordered_matmul = true"))
+    ctx.cuda().matmul_into(a, a, out)
+    assert out.cpu().numpy().reshape(-1).tolist() == [7.0, 10.0, 15.0, 22.0]
+    assert out.data_ptr() == pointer
+
+
+def _seed(n):
+    return 0.3 + 0.11 * np.arange(n)
+
+
+def _near(a, b):
+    assert abs(a - b) < 2e-6 * (1.0 + abs(a) + abs(b)), (a, b)
+
+
+def _check_binary(forward, backward, left, right):
+    """binary (autograd_tests.rs:55-100): the analytic gradients of
+    sum(forward(l, r) * seed) against central differences."""
+    out = forward(left, right)
+    seed = _seed(out.size).reshape(out.shape)
+    gl, gr = backward(left, right, seed)
+
+    def evaluate(l, r):
+        return float((forward(l, r).reshape(-1) * _seed(out.size)).sum())
+    h = 1e-6
+    for which, (inp, grad) in enumerate(((left, gl), (right, gr))):
+        for i in range(inp.size):
+            hi, lo = inp.copy().reshape(-1), inp.copy().reshape(-1)
+            hi[i] += h
+            lo[i] -= h
+            hi, lo = hi.reshape(inp.shape), lo.reshape(inp.shape)
+            num = (evaluate(hi, right) - evaluate(lo, right)) if which == 0 else \
+                (evaluate(left, hi) - evaluate(left, lo))
+            _near(float(grad.reshape(-1)[i]), num / (2 * h))
+
+
+def test_matmul_gradients_against_central_differences(kx, torch_cuda):
+    torch = torch_cuda
+    left = np.array([0.2, 0.4, 0.6, 0.8, 1.0, 1.2]).reshape(2, 3)
+    right = np.array([0.1, 0.3, 0.5, 0.7, 0.9, 1.1]).reshape(3, 2)
+
+    def forward(a, b):
+        return kx.matmul(dev(torch, a), dev(torch, b)).cpu().numpy()
+
+    def backward(a, b, g):
+        ga, gb = kx.matmul_backward(dev(torch, a), dev(torch, b), dev(torch, g))
+        return ga.cpu().numpy(), gb.cpu().numpy()
+    _check_binary(forward, backward, left, right)
+
+
+def test_conv2d_gradients_against_central_differences(kx, torch_cuda):
+    torch = torch_cuda
+    x = np.array([0.1, 0.3, 0.7, 0.4, 0.2, 0.8, 0.9, 0.6, 0.5]).reshape(1, 1, 3, 3)
+    w = np.array([0.2, 0.4, 0.7, 0.9]).reshape(1, 1, 2, 2)
+
+    def forward(a, b):
+        return kx.conv2d(dev(torch, a), dev(torch, b)).cpu().numpy()
+
+    def backward(a, b, g):
+        gx, gw = kx.conv2d_backward(dev(torch, a), dev(torch, b), dev(torch, g))
+        return gx.cpu().numpy(), gw.cpu().numpy()
+    _check_binary(forward, backward, x, w)
+
+
+def _spd(n, scale, seed):
+    rs = np.random.default_rng(seed)
+    m = rs.uniform(-1, 1, (n, n))
+    return (m @ m.T + n * np.eye(n)) * scale
+
+
+@pytest.mark.parametrize("n", [1, 7, 31, 64, 96, 97, 128])
+@pytest.mark.parametrize("scale", [1e-200, 1.0, 1e200])
+def test_cholesky_reconstruction_in_ordered_mode(kx, torch_cuda, n, scale):
+    torch = torch_cuda
+    a = _spd(n, scale, n)
+    low = np.linalg.cholesky(a)
+    want = oracle.matmul_reference(oracle.View.of(low), oracle.View(low, (n, n), (1, n)))
+    dl = dev(torch, low)
+    got = kx.matmul_reference(dl, dl.transpose(0, 1)).cpu().numpy()
+    assert np.array_equal(got, want)
+    assert (np.abs((got - a) / scale) < 1e-12 * n).all()
