@@ -12,7 +12,9 @@
 * the reconstruction check of cholesky_layouts_scales_branch_boundaries
   (kernix-ops/tests/factorization_regressions.rs:39-61): matmul_reference(L,
   L^T view) at scales 1e-200, 1, 1e200 -- bit for bit the oracle's ordered
-  product, and within 1e-12 * scale of the original matrix.
+  product, and within 1e-12 * scale of the original matrix;
+* the dense arm of Matrix::matmul with signed-stride vectors and views
+  (kernix-ops/tests/sparse_tests.rs:134-200), against matmul_reference.
 """
 import numpy as np
 import pytest
@@ -118,3 +120,49 @@ def test_cholesky_reconstruction_in_ordered_mode(kx, torch_cuda, n, scale):
     got = kx.matmul_reference(dl, dl.transpose(0, 1)).cpu().numpy()
     assert np.array_equal(got, want)
     assert (np.abs((got - a) / scale) < 1e-12 * n).all()
+
+
+def _sparse_matrix(m, n, shift):
+    """matrix (kernix-ops/tests/sparse_tests.rs:5-19)."""
+    p = np.arange(m * n)
+    return np.where((p * 7 + shift) % 11 < 2, (p % 13) / 8.0 - 0.5, 0.0).reshape(m, n)
+
+
+def _close(x, y):
+    """assert_close (sparse_tests.rs:20-25)."""
+    assert x.shape == y.shape
+    assert (np.abs(x - y) < 2e-12 * (1.0 + np.abs(y))).all()
+
+
+@pytest.mark.parametrize("m,k,n", [(0, 3, 4), (3, 0, 4), (3, 4, 0), (1, 1, 1), (3, 5, 4), (7, 9, 13),
+                                   (17, 31, 9), (65, 33, 7)])
+def test_dense_matrix_products_and_reversed_vectors(kx, torch_cuda, m, k, n):
+    """The dense arm of Matrix::matmul and the signed-stride vector products of
+    all_four_storage_products_and_signed_stride_vectors_match_independent_oracles
+    (sparse_tests.rs:134-179), against matmul_reference."""
+    torch = torch_cuda
+    a, b = _sparse_matrix(m, k, 1), _sparse_matrix(k, n, 2)
+    want = oracle.matmul_reference(oracle.View.of(a), oracle.View.of(b))
+    _close(kx.matmul(dev(torch, a), dev(torch, b)).cpu().numpy(), want)
+    v = np.arange(k) / 16.0 - 0.5
+    buf = dev(torch, v)
+    rev = kx.TensorView(buf, (k,), (-1,), max(k - 1, 0))                 # reverse_axis(0)
+    want_v = oracle.matmul_reference(oracle.View.of(a), oracle.View(v, (k,), (-1,), max(k - 1, 0)))
+    _close(kx.matmul(dev(torch, a), rev).cpu().numpy(), want_v)
+
+
+def test_transposed_and_reversed_dense_operands(kx, torch_cuda):
+    """transpose_csc_and_reversed_dense_rhs_remain_zero_copy_and_correct
+    (sparse_tests.rs:181-200), dense operands: a^T times b with axis 0
+    reversed, and a times b with axis 1 reversed, as views."""
+    torch = torch_cuda
+    a = _sparse_matrix(7, 9, 3)
+    b = _sparse_matrix(7, 5, 4)
+    at = kx.TensorView(dev(torch, a).reshape(-1), (9, 7), (1, 9), 0)
+    brev = kx.TensorView(dev(torch, b).reshape(-1), (7, 5), (-5, 1), 6 * 5)
+    want = oracle.matmul_reference(oracle.View(a, (9, 7), (1, 9)), oracle.View(b, (7, 5), (-5, 1), 30))
+    _close(kx.matmul(at, brev).cpu().numpy(), want)
+    b2 = _sparse_matrix(9, 5, 2)
+    b2rev = kx.TensorView(dev(torch, b2).reshape(-1), (9, 5), (5, -1), 4)
+    want2 = oracle.matmul_reference(oracle.View.of(a), oracle.View(b2, (9, 5), (5, -1), 4))
+    _close(kx.matmul(dev(torch, a), b2rev).cpu().numpy(), want2)
