@@ -104,6 +104,9 @@ def test_conv_medium_igemm_vs_compensated(kx, torch_cuda):
 # softmax_temperature
 # ---------------------------------------------------------------------------
 def test_softmax_known_answers(kx, torch_cuda):
+    """softmax_temperature_preserves_extreme_logits (kernix-ops/tests/numeric_dispatch_04.rs:172-190)
+    and large_temperature_preserves_finite_logit_differences
+    (kernix-ops/tests/qa_extreme_numerics.rs:10-24)."""
     x = to_dev(np.array([[1000.0, 1001.0]]), torch_cuda)
     y = kx.softmax_temperature(x, -1, 2.0).cpu().numpy()
     assert abs(y[0, 1] - 1.0 / (1.0 + math.exp(-0.5))) < 1e-15

@@ -14,7 +14,13 @@
   L^T view) at scales 1e-200, 1, 1e200 -- bit for bit the oracle's ordered
   product, and within 1e-12 * scale of the original matrix;
 * the dense arm of Matrix::matmul with signed-stride vectors and views
-  (kernix-ops/tests/sparse_tests.rs:134-200), against matmul_reference.
+  (kernix-ops/tests/sparse_tests.rs:134-200), against matmul_reference;
+* the matmul cases of kernix/tests/autograd_tensor_tests.rs:35-217: vector,
+  matrix and broadcast-batch VJPs against central differences, exactly zero
+  gradients of zero extents, a shared operand on both sides, reversed and
+  transposed views with a constant side;
+* the direct-memory and reversed-axis products of
+  kernix-ops/tests/numeric_dispatch_04.rs:116-152.
 """
 import numpy as np
 import pytest
@@ -166,3 +172,125 @@ def test_transposed_and_reversed_dense_operands(kx, torch_cuda):
     b2rev = kx.TensorView(dev(torch, b2).reshape(-1), (9, 5), (5, -1), 4)
     want2 = oracle.matmul_reference(oracle.View.of(a), oracle.View(b2, (9, 5), (5, -1), 4))
     _close(kx.matmul(dev(torch, a), b2rev).cpu().numpy(), want2)
+
+
+def _values(dims, offset):
+    """values (kernix/tests/autograd_tensor_tests.rs:7-16)."""
+    count = int(np.prod(dims, dtype=np.int64))
+    return (((np.arange(count) * 7 + offset) % 19) / 13.0 - 0.6).reshape(dims)
+
+
+def _near_tape(a, b):
+    """near (autograd_tensor_tests.rs:20-25)."""
+    assert abs(a - b) <= 3e-7 * (1.0 + abs(a) + abs(b)), (a, b)
+
+
+@pytest.mark.parametrize("ad,bd,out", [
+    ((3,), (3,), ()), ((3,), (3, 2), (2,)), ((2, 3), (3,), (2,)), ((3,), (2, 3, 2), (2, 2)),
+    ((2, 2, 3), (3,), (2, 2)), ((2, 1, 2, 3), (1, 3, 3, 2), (2, 3, 2, 2)),
+    ((2, 1, 2, 3), (3, 3, 2), (2, 3, 2, 2)), ((2, 3), (4, 3, 2), (4, 2, 2)),
+    ((4, 2, 3), (3, 2), (4, 2, 2)), ((1, 1, 1, 2, 3), (2, 3, 2), (1, 1, 2, 2, 2)),
+], ids=lambda v: "x".join(map(str, v)) or "scalar")
+def test_matmul_vjp_vector_and_broadcast_batch_finite_differences(kx, torch_cuda, ad, bd, out):
+    """matmul_fd over matmul_vector_matrix_and_broadcast_batch_finite_differences
+    (autograd_tensor_tests.rs:35-88): the VJP of sum(y * seed) against central
+    differences (h = 1e-6) of the device forward product, f64."""
+    torch = torch_cuda
+    a, b, seed = _values(ad, 1), _values(bd, 5), _values(out, 3)
+
+    def objective(l, r):
+        y = kx.matmul(dev(torch, l), dev(torch, r)).cpu().numpy()
+        assert y.shape == out
+        return float((y.reshape(-1) * seed.reshape(-1)).sum())
+    da, db = kx.matmul_backward(dev(torch, a), dev(torch, b), dev(torch, seed))
+    h = 1e-6
+    for side, (inp, grad) in enumerate(((a, da.cpu().numpy()), (b, db.cpu().numpy()))):
+        assert grad.shape == inp.shape
+        for i in range(inp.size):
+            hi, lo = inp.copy().reshape(-1), inp.copy().reshape(-1)
+            hi[i] += h
+            lo[i] -= h
+            hi, lo = hi.reshape(inp.shape), lo.reshape(inp.shape)
+            num = objective(a, hi) - objective(a, lo) if side else objective(hi, b) - objective(lo, b)
+            _near_tape(float(grad.reshape(-1)[i]), num / (2 * h))
+
+
+@pytest.mark.parametrize("ad,bd,out", [
+    ((1, 2, 3), (0, 3, 4), (0, 2, 4)), ((0, 2, 3), (1, 3, 4), (0, 2, 4)), ((3,), (0, 3, 4), (0, 4)),
+    ((0, 2, 3), (3,), (0, 2)), ((2, 0), (0, 3), (2, 3)), ((0, 3), (3, 2), (0, 2)),
+    ((2, 3), (3, 0), (2, 0)), ((0,), (0,), ()), ((0,), (2, 0, 3), (2, 3)), ((2, 3, 0), (0,), (2, 3)),
+], ids=lambda v: "x".join(map(str, v)) or "scalar")
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_matmul_zero_extents_have_exact_shaped_zero_gradients(kx, torch_cuda, ad, bd, out, dtype):
+    """matmul_zero_extents_have_exact_shaped_zero_gradients
+    (autograd_tensor_tests.rs:89-116): the gradients of sum(y) keep their
+    operands' shapes and are exactly zero."""
+    torch = torch_cuda
+    a, b = _values(ad, 1).astype(dtype), _values(bd, 2).astype(dtype)
+    y = kx.matmul(dev(torch, a), dev(torch, b))
+    assert tuple(y.shape) == out
+    da, db = kx.matmul_backward(dev(torch, a), dev(torch, b), dev(torch, np.ones(out, dtype)))
+    for g, dims in ((da, ad), (db, bd)):
+        g = g.cpu().numpy()
+        assert g.shape == dims and (g == 0).all()
+
+
+def test_matmul_shared_operand_and_seeded_dot(kx, torch_cuda):
+    """matmul_shared_dag_repeated_backward_and_seeded_dot
+    (autograd_tensor_tests.rs:117-155): d sum(x.x + x.x) / dx is the sum of both
+    VJP sides with seed 2, equal to 2 (row j of x summed + column i of x
+    summed) per batch, and the same on a repeated pass; d (v.v) / dv with seed
+    2 is 4 v."""
+    torch = torch_cuda
+    x = _values((2, 2, 2), 1)
+    dx = dev(torch, x)
+    g = dev(torch, np.full((2, 2, 2), 2.0))
+    first = sum(t.cpu().numpy() for t in kx.matmul_backward(dx, dx, g))
+    second = sum(t.cpu().numpy() for t in kx.matmul_backward(dx, dx, g))
+    for batch in range(2):
+        a = x[batch].reshape(-1)
+        for i in range(2):
+            for j in range(2):
+                _near_tape(first[batch, i, j], 2.0 * (a[j * 2] + a[j * 2 + 1] + a[i] + a[2 + i]))
+    assert np.array_equal(first, second)
+    v = dev(torch, np.array([1.0, 2.0, 3.0]))
+    gv = sum(t.cpu().numpy() for t in kx.matmul_backward(v, v, dev(torch, np.array(2.0))))
+    assert gv.tolist() == [4.0, 8.0, 12.0]
+
+
+def test_matmul_transposed_reversed_inputs_and_constant_side(kx, torch_cuda):
+    """matmul_transposed_reversed_inputs_and_constants
+    (autograd_tensor_tests.rs:178-217): a [2,2,3] with axis 2 reversed times
+    b [2,4,3] with axes 1 and 2 swapped, both zero-copy views; the product
+    against matmul_reference, and d sum(permute(y)) / da = ones[2,2,4] . b
+    with the constant side's gradient not computed."""
+    torch = torch_cuda
+    a, b = _values((2, 2, 3), 1), _values((2, 4, 3), 2)
+    av = kx.TensorView(dev(torch, a).reshape(-1), (2, 2, 3), (6, 3, -1), 2)
+    bv = kx.TensorView(dev(torch, b).reshape(-1), (2, 3, 4), (12, 1, 3), 0)
+    oa, ob = oracle.View(a, (2, 2, 3), (6, 3, -1), 2), oracle.View(b, (2, 3, 4), (12, 1, 3), 0)
+    y = kx.matmul(av, bv).cpu().numpy()
+    want = oracle.matmul_reference(oa, ob)
+    for p, q in zip(y.reshape(-1), want.reshape(-1)):
+        _near_tape(float(p), float(q))
+    da, db = kx.matmul_backward(av, bv, dev(torch, np.ones((2, 2, 4))), need_b=False)
+    assert db is None
+    want_da = oracle.matmul_reference(oracle.View.of(np.ones((2, 2, 4))), oracle.View.of(b))
+    for p, q in zip(da.cpu().numpy().reshape(-1), want_da.reshape(-1)):
+        _near_tape(float(p), float(q))
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_direct_memory_and_reversed_matrix_products(kx, torch_cuda, dtype):
+    """contiguous_matrix_mult_uses_direct_memory, contiguous_dot_uses_direct_memory
+    and noncontiguous_matrix_falls_back_to_checked_indexing
+    (kernix-ops/tests/numeric_dispatch_04.rs:116-152): exact small-integer
+    answers for the contiguous, the dot and the axis-1-reversed operand."""
+    torch = torch_cuda
+    a = np.arange(1, 7, dtype=dtype).reshape(2, 3)
+    b = np.arange(7, 13, dtype=dtype).reshape(3, 2)
+    assert kx.matmul(dev(torch, a), dev(torch, b)).cpu().numpy().reshape(-1).tolist() == [58, 64, 139, 154]
+    d = kx.matmul(dev(torch, np.array([1, 2, 3], dtype)), dev(torch, np.array([4, 5, 6], dtype)))
+    assert tuple(d.shape) == () and float(d.cpu()) == 32.0
+    rev = kx.TensorView(dev(torch, a).reshape(-1), (2, 3), (3, -1), 2)
+    assert kx.matmul(rev, dev(torch, b)).cpu().numpy().reshape(-1).tolist() == [50, 56, 131, 146]
