@@ -60,6 +60,7 @@ class Handle:
         err = KxError()
         raise_for(lib.kx_create(device, C.byref(ptr), C.byref(err)), err)
         self._h = ptr
+        self._stream = 0            # the raw stream the library handle orders work on
 
     @classmethod
     def adopt(cls, ptr: C.c_void_p, device: int) -> "Handle":
@@ -67,6 +68,7 @@ class Handle:
         h = cls.__new__(cls)
         h.device = device
         h._h = ptr
+        h._stream = 0
         return h
 
     @property
@@ -86,8 +88,10 @@ class Handle:
 
     def set_stream(self, stream) -> None:
         """Order later work on ``stream`` (a torch.cuda.Stream or raw cudaStream_t)."""
-        raw = getattr(stream, "cuda_stream", stream)
-        lib.kx_set_stream(self._h, C.c_void_p(int(raw) if raw else 0))
+        raw = int(getattr(stream, "cuda_stream", stream) or 0)
+        if raw != self._stream:     # every call binds the current stream: skip the unchanged case
+            lib.kx_set_stream(self._h, C.c_void_p(raw))
+            self._stream = raw
 
     def set_f32_variant(self, variant: int) -> None:
         raise_for(lib.kx_set_f32_variant(self._h, int(variant)), None)
@@ -192,21 +196,21 @@ def _descriptor(t) -> KxTensor:
         d.data = buf.data_ptr()
         d.storage_len = buf.numel()
         d.origin = int(t.origin)
-        dims, strides = list(t.dims), list(t.strides)
+        dims, strides = [int(n) for n in t.dims], [int(s) for s in t.strides]
     else:
         st = t.untyped_storage()
         d.data = st.data_ptr()
         d.storage_len = st.nbytes() // t.element_size()
         d.origin = t.storage_offset()
-        dims, strides = list(t.shape), list(t.stride())
-    if len(dims) != len(strides):
+        dims, strides = t.shape, t.stride()
+    rank = len(dims)
+    if rank != len(strides):
         raise LayoutError("stride rank mismatch", kind="StrideRankMismatch")
-    if len(dims) > MAX_RANK:
-        raise Unsupported(f"rank {len(dims)} above {MAX_RANK}")
-    d.rank = len(dims)
-    for i, (n, s) in enumerate(zip(dims, strides)):
-        d.dims[i] = int(n)
-        d.strides[i] = int(s)
+    if rank > MAX_RANK:
+        raise Unsupported(f"rank {rank} above {MAX_RANK}")
+    d.rank = rank
+    d.dims[:rank] = dims            # one slice store per array: the call path's largest host cost
+    d.strides[:rank] = strides
     return d
 
 
@@ -217,11 +221,18 @@ def _device_index(t) -> int:
     return dev.index if dev.index is not None else 0
 
 
-def _bind(t) -> Handle:
+def _current_stream(dev: int) -> int:
+    """torch's current stream on ``dev`` as a raw cudaStream_t (the raw query
+    when this torch build has it: no Stream object per call)."""
     import torch
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    return int(raw(dev)) if raw is not None else int(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _bind(t) -> Handle:
     dev = _device_index(t)
     h = getattr(_active, "handles", {}).get(dev) or handle(dev)
-    h.set_stream(torch.cuda.current_stream(dev))
+    h.set_stream(_current_stream(dev))
     return h
 
 
@@ -258,7 +269,7 @@ def matmul_shape(a_dims: Sequence[int], b_dims: Sequence[int]) -> tuple[int, ...
     rc = lib.kx_matmul_shape(u64_array(a_dims), len(a_dims), u64_array(b_dims), len(b_dims), C.byref(rank), out,
                              C.byref(err))
     raise_for(rc, err)
-    return tuple(int(out[i]) for i in range(rank.value))
+    return tuple(out[:rank.value])
 
 
 def matmul(a, b):

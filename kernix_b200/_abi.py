@@ -349,8 +349,5 @@ def raise_for(rc: int, err: KxError | None) -> None:
 
 
 def u64_array(values) -> C.Array:
-    vals = list(values)
-    arr = (C.c_uint64 * max(len(vals), MAX_RANK))()
-    for i, x in enumerate(vals):
-        arr[i] = int(x)
-    return arr
+    vals = [int(x) for x in values]
+    return (C.c_uint64 * max(len(vals), MAX_RANK))(*vals)
