@@ -265,6 +265,31 @@ def test_small_products_split_k_on_the_tensor_cores(kx, torch_cuda, m, k, n):
     assert (np.abs(c.astype(np.float64) - want) <= 2e-6 * absum + 1e-30).all()
 
 
+def test_split_k_back_to_back_and_guarded_output(kx, torch_cuda):
+    """K-sliced tensor-core products back to back with new data on the same
+    handle (the shared slice workspace reused) match the oracle, and a product
+    into an output inside a larger buffer is bitwise the same with the guard
+    elements on both sides untouched."""
+    torch = torch_cuda
+    h = kx.handle(0)
+    h.set_f32_variant(0)
+    rs = np.random.default_rng(11)
+    m = k = n = 512
+    for trial in range(3):
+        a = rs.uniform(-1, 1, (m, k)).astype(np.float32)
+        b = rs.uniform(-1, 1, (k, n)).astype(np.float32)
+        da, db = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+        c = kx.matmul(da, db)
+        assert h.last_kernel == "tc_3xtf32_splitk", h.last_kernel
+        want, absum = oracle.gemm_dot2(oracle.View.of(a.astype(np.float64)), oracle.View.of(b.astype(np.float64)))
+        assert (np.abs(c.cpu().numpy().astype(np.float64) - want) <= 2e-6 * absum + 1e-30).all()
+        buf = torch.full((m * n + 8,), -7.0, device="cuda")
+        kx.matmul_into(da, db, kx.TensorView(buf, (m, n), (n, 1), 4))
+        assert h.last_kernel == "tc_3xtf32_splitk"
+        assert (buf[:4] == -7.0).all() and (buf[4 + m * n:] == -7.0).all()
+        assert torch.equal(buf[4:4 + m * n].reshape(m, n), c)
+
+
 def test_split_k_nonfinite_and_uneven_k(kx, torch_cuda):
     """inf and NaN in A propagate through the split slices as through one
     f32 accumulation; a K the slices cannot divide evenly keeps the SIMT
