@@ -221,3 +221,32 @@ def test_python_errors_compare_like_rust_values():
     with pytest.raises(kx.InvalidRank) as e:
         kx.matmul_shape([], [2])
     assert (e.value.minimum, e.value.actual) == (1, 0)
+
+
+def test_descriptors_carry_layout_exactly():
+    """The kx_tensor descriptors the Python mirror builds (host only): torch
+    views keep their storage origin and strides, TensorView keeps signed and
+    zero strides and numpy integers, rank 0 fills nothing, and a rank above
+    KX_MAX_RANK or a stride list of the wrong length is refused before any
+    call."""
+    import torch
+    base = torch.zeros(6, 8, dtype=torch.float64)
+    t = base[1:, 2:].transpose(0, 1)
+    d = kx._descriptor(t)
+    assert (d.rank, d.origin, d.storage_len) == (2, 10, 48)
+    assert list(d.dims)[:2] == [6, 5] and list(d.strides)[:2] == [1, 8]
+    assert list(d.dims)[2:] == [0] * (kx.MAX_RANK - 2)
+    assert d.data == base.untyped_storage().data_ptr()
+    buf = torch.zeros(12)
+    v = kx.TensorView(buf, (np.int64(3), 4), (-4, np.int64(0)), np.int64(8))
+    d = kx._descriptor(v)
+    assert (d.rank, d.origin, d.storage_len) == (2, 8, 12)
+    assert list(d.dims)[:2] == [3, 4] and list(d.strides)[:2] == [-4, 0]
+    d = kx._descriptor(torch.tensor(2.5))
+    assert d.rank == 0 and list(d.dims) == [0] * kx.MAX_RANK
+    d = kx._descriptor(kx.TensorView(buf, (USIZE_MAX, 0), (1, 1)))
+    assert list(d.dims)[:2] == [USIZE_MAX, 0]
+    with pytest.raises(kx.Unsupported):
+        kx._descriptor(kx.TensorView(buf, (1,) * (kx.MAX_RANK + 1), (1,) * (kx.MAX_RANK + 1)))
+    with pytest.raises(kx.LayoutError):
+        kx._descriptor(kx.TensorView(buf, (3, 4), (4,)))
