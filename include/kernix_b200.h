@@ -413,6 +413,23 @@ int kx_row_piece(uint64_t m, uint32_t world, uint64_t target_piece, uint64_t *pi
 int kx_matmul_rows_sharded_f32(kx_handle *h, const kx_tensor *a_local, const kx_tensor *b, const kx_tensor *out,
                                uint32_t rank, uint32_t world, uint64_t piece, void *const *peer_out, void *out_mc,
                                kx_error *err);
+/* The row-sharded f32 product driven from ONE process over `ngpu` (1..8)
+ * handles, one per GPU (handles may share a device), for callers without one
+ * process per GPU.  `a`, `b` and `out` are arrays of ngpu descriptors:
+ * handle r multiplies a[r] (the rows of window r of A, as kx_shard_window(M,
+ * r, ngpu) gives them, on its device) by b[r] ([K, N], its replica) into the
+ * same rows of out[r] (a C-contiguous [M, N] output on its device).  With
+ * gather_out != 0 every window is then copied into every other handle's output
+ * by the copy engines (peer access between the devices is enabled on first
+ * use), after whatever that handle's stream had queued before the call; the
+ * outputs must not overlap.  With gather_out == 0 out[r] receives only its own
+ * rows.  Every argument is checked before anything is enqueued.  Returns once
+ * the work is enqueued: each handle's stream completes after all windows have
+ * reached its output (kx_synchronize on each handle).  Reference counterpart:
+ * the row chunks of CpuExecutor::matmul_into (execution.rs:188-233), one per
+ * worker sharing one output. */
+int kx_gemm_sharded_f32(kx_handle *const *handles, uint32_t ngpu, const kx_tensor *a, const kx_tensor *b,
+                        const kx_tensor *out, int gather_out, kx_error *err);
 
 /* ---- introspection ------------------------------------------------------ */
 /* Number of kernel launches this handle has issued since creation. */

@@ -169,6 +169,8 @@ _SIGNATURES = {
     "kx_row_piece": (C.c_int, [_u64, C.c_uint32, _u64, _P(_u64), _P(_u64)]),
     "kx_matmul_rows_sharded_f32": (C.c_int, [_vp, _P(KxTensor), _P(KxTensor), _P(KxTensor), C.c_uint32, C.c_uint32,
                                              _u64, _P(_vp), _vp, _P(KxError)]),
+    "kx_gemm_sharded_f32": (C.c_int, [_P(_vp), C.c_uint32, _P(KxTensor), _P(KxTensor), _P(KxTensor), C.c_int,
+                                      _P(KxError)]),
     "kx_launch_count": (C.c_uint64, [_vp]),
     "kx_last_kernel": (C.c_char_p, [_vp]),
     "kx_status_name": (C.c_char_p, [C.c_int]),

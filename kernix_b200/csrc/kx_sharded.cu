@@ -13,6 +13,10 @@
 //     global row block i * world + rank of `piece` rows is rank's piece i, so
 //     each rank's pieces interleave and piece i of all ranks fills one
 //     contiguous band of the output.
+//   * kx_gemm_sharded_f32: the same row split driven from ONE process over
+//     several handles (one per GPU): each handle multiplies its window of
+//     rows, then the copy engines copy every window into every other
+//     handle's output (peer access enabled between the devices).
 //   * kx_matmul_rows_sharded_f32: one rank's share of the row-sharded product,
 //     each piece pushed into every peer's output as soon as it is computed:
 //     copy engines (one stream per peer) while the next piece multiplies, and
@@ -20,6 +24,7 @@
 //     through an NVLink multicast address (the NVSwitch fans it out) or a
 //     kernel on all SMs writing to every peer.
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 
 #include "kx_internal.hpp"
@@ -72,6 +77,28 @@ __global__ void tail_sum_kernel(float *__restrict__ c, const float *__restrict__
 // 770 GB/s of one GPU's NVLink, against the split's two sums.
 constexpr uint64_t kTailSplitBytes = 32ull << 20;
 
+// Peer access from `dev` to `peer` for this process, enabled once per pair
+// (copies between the devices then go over NVLink directly; without it the
+// runtime stages them, still correct).
+void enable_peer(int dev, int peer) {
+    static std::atomic<uint64_t> done[kMaxWorld * 8] = {};
+    if (dev == peer || dev < 0 || peer < 0) return;
+    const int word = dev % (kMaxWorld * 8);
+    const uint64_t bit = 1ull << (peer % 64);
+    if (done[word].load() & bit) return;
+    int can = 0;
+    if (cudaDeviceCanAccessPeer(&can, dev, peer) == cudaSuccess && can) {
+        int prev = -1;
+        cudaGetDevice(&prev);
+        cudaSetDevice(dev);
+        // already enabled is no error for the caller, and a refusal leaves the
+        // copies staged: either way nothing is left for a later error check
+        if (cudaDeviceEnablePeerAccess(peer, 0) != cudaSuccess) cudaGetLastError();
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+    done[word].fetch_or(bit);
+}
+
 }  // namespace
 }  // namespace kx
 
@@ -115,7 +142,7 @@ int kx_matmul_rows_sharded_f32(kx_handle *hh, const kx_tensor *a_local, const kx
         return set_err(err, KX_E_PARAM, kOp, "piece rows must tile M over the ranks", m, piece);
     const uint64_t pieces = m / ((uint64_t)world * piece);
     if (a_local->dims[0] != pieces * piece)
-        return set_err(err, KX_E_LAYOUT, kOp, "local A must hold this rank's rows", a_local->dims[0], pieces * piece);
+        return set_err(err, KX_E_PARAM, kOp, "local A must hold this rank's rows", a_local->dims[0], pieces * piece);
     if (!is_c_contiguous(out))
         return set_err(err, KX_E_LAYOUT, kOp, "output must be C-contiguous", KX_LAYOUT_OUTPUT_NOT_C_CONTIGUOUS);
     DeviceGuard g(h->device);
@@ -245,6 +272,114 @@ int kx_matmul_rows_sharded_f32(kx_handle *hh, const kx_tensor *a_local, const kx
             if (ce != cudaSuccess) {
                 h->cuda_fail(ce);
                 return cuda_err(err, h, kOp);
+            }
+        }
+    }
+    return KX_OK;
+}
+
+int kx_gemm_sharded_f32(kx_handle *const *handles, uint32_t ngpu, const kx_tensor *a, const kx_tensor *b,
+                        const kx_tensor *out, int gather_out, kx_error *err) {
+    static const char *kOp = "gemm_sharded";
+    if (!handles || !a || !b || !out) return set_err(err, KX_E_PARAM, kOp, "null argument");
+    if (ngpu == 0 || ngpu > (uint32_t)kMaxWorld) return set_err(err, KX_E_PARAM, kOp, "ngpu (1..8)", ngpu);
+    for (uint32_t r = 0; r < ngpu; ++r)
+        if (!handles[r]) return set_err(err, KX_E_PARAM, kOp, "null handle", r);
+    // Every argument is checked before any work is enqueued.
+    if (out[0].rank != 2) return set_err(err, KX_E_PARAM, kOp, "rank-two outputs");
+    const uint64_t m = out[0].dims[0], n = out[0].dims[1];
+    if (a[0].rank != 2) return set_err(err, KX_E_PARAM, kOp, "rank-two blocks of A");
+    const uint64_t k = a[0].dims[1];
+    Span so[kMaxWorld];
+    for (uint32_t r = 0; r < ngpu; ++r) {
+        Span sa, sb;
+        int rc = validate_tensor(a + r, 4, &sa, err);
+        if (!rc) rc = validate_tensor(b + r, 4, &sb, err);
+        if (!rc) rc = validate_tensor(out + r, 4, &so[r], err);
+        if (rc) return rc;
+        uint64_t start = 0, count = 0;
+        kx_shard_window(m, r, ngpu, &start, &count);
+        if (a[r].rank != 2 || a[r].dims[0] != count || a[r].dims[1] != k)
+            return set_err(err, KX_E_PARAM, kOp, "a[r] must be [rows of window r, K]", r, count);
+        if (b[r].rank != 2 || b[r].dims[0] != k || b[r].dims[1] != n)
+            return set_err(err, KX_E_PARAM, kOp, "b[r] must be [K, N]", r);
+        if (out[r].rank != 2 || out[r].dims[0] != m || out[r].dims[1] != n)
+            return set_err(err, KX_E_LAYOUT, kOp, "every output [M, N]", KX_LAYOUT_OUTPUT_SHAPE_MISMATCH);
+        if (!is_c_contiguous(out + r))
+            return set_err(err, KX_E_LAYOUT, kOp, "output must be C-contiguous", KX_LAYOUT_OUTPUT_NOT_C_CONTIGUOUS);
+        if (spans_overlap(out[r].data, so[r], a[r].data, sa, 4) || spans_overlap(out[r].data, so[r], b[r].data, sb, 4))
+            return set_err(err, KX_E_ALIAS, kOp, "output overlaps an input");
+    }
+    if (gather_out)
+        for (uint32_t r = 0; r < ngpu; ++r)
+            for (uint32_t q = r + 1; q < ngpu; ++q)
+                if (spans_overlap(out[r].data, so[r], out[q].data, so[q], 4))
+                    return set_err(err, KX_E_ALIAS, kOp, "gathered outputs overlap", r, q);
+    if (m == 0 || n == 0) return KX_OK;
+    // Rows of window r in output q: one contiguous byte range.
+    auto rows_at = [&](uint32_t q, uint64_t start) {
+        return static_cast<char *>(out[q].data) + (out[q].origin + start * n) * sizeof(float);
+    };
+    const bool gather = gather_out && ngpu > 1;
+    if (gather) {
+        for (uint32_t r = 0; r < ngpu; ++r) {
+            Handle *h = &handles[r]->impl;
+            DeviceGuard g(h->device);
+            if (!g.ok) return set_err(err, KX_E_NO_DEVICE, kOp, "cannot select device", r);
+            if (!push_streams(h)) return set_err(err, KX_E_CUDA, kOp, "cannot create the gather events");
+            for (uint32_t q = 0; q < ngpu; ++q) enable_peer(h->device, handles[q]->impl.device);
+            // the point after which output r may be written by the other handles
+            const cudaError_t ce = cudaEventRecord(h->peer_done[0], h->stream);
+            if (ce != cudaSuccess) {
+                h->cuda_fail(ce);
+                return cuda_err(err, h, kOp);
+            }
+        }
+    }
+    for (uint32_t r = 0; r < ngpu; ++r) {
+        Handle *h = &handles[r]->impl;
+        uint64_t start = 0, count = 0;
+        kx_shard_window(m, r, ngpu, &start, &count);
+        if (count == 0) continue;
+        kx_tensor cp = out[r];
+        cp.dims[0] = count;
+        cp.origin = out[r].origin + start * n;
+        int rc = kx_matmul_f32(handles[r], a + r, b + r, &cp, err);
+        if (rc) return rc;
+        if (!gather) continue;
+        DeviceGuard g(h->device);
+        cudaError_t ce = cudaSuccess;
+        for (uint32_t q = 0; q < ngpu && ce == cudaSuccess; ++q) {
+            if (q == r) continue;
+            const Handle *hq = &handles[q]->impl;
+            ce = cudaStreamWaitEvent(h->stream, hq->peer_done[0], 0);
+            if (ce != cudaSuccess) break;
+            const uint64_t bytes = count * n * sizeof(float);
+            ce = hq->device == h->device
+                     ? cudaMemcpyAsync(rows_at(q, start), rows_at(r, start), bytes, cudaMemcpyDeviceToDevice, h->stream)
+                     : cudaMemcpyPeerAsync(rows_at(q, start), hq->device, rows_at(r, start), h->device, bytes,
+                                           h->stream);
+        }
+        if (ce == cudaSuccess) ce = cudaEventRecord(h->peer_ready, h->stream);
+        if (ce != cudaSuccess) {
+            h->cuda_fail(ce);
+            return cuda_err(err, h, kOp);
+        }
+    }
+    if (gather) {
+        // each handle's stream completes only after every window has reached its output
+        for (uint32_t q = 0; q < ngpu; ++q) {
+            Handle *h = &handles[q]->impl;
+            DeviceGuard g(h->device);
+            for (uint32_t r = 0; r < ngpu; ++r) {
+                uint64_t start = 0, count = 0;
+                kx_shard_window(m, r, ngpu, &start, &count);
+                if (r == q || count == 0) continue;
+                const cudaError_t ce = cudaStreamWaitEvent(h->stream, handles[r]->impl.peer_ready, 0);
+                if (ce != cudaSuccess) {
+                    h->cuda_fail(ce);
+                    return cuda_err(err, h, kOp);
+                }
             }
         }
     }

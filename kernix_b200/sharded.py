@@ -110,6 +110,28 @@ def rows_sharded(a_local, b, out, plan: RowPlan, rank: int, peer_ptrs=None, out_
     _abi.raise_for(rc, err)
 
 
+def gemm_sharded(handles, a_windows, b_replicas, outs, gather_out: bool = True) -> None:
+    """``kx_gemm_sharded_f32``: the row-sharded product from one process over
+    several handles (one per GPU).  ``a_windows[r]`` holds the rows
+    ``shard_window(M, r, len(handles))`` of A on handle r's device,
+    ``b_replicas[r]`` B there, ``outs[r]`` a C-contiguous [M, N] output there;
+    with ``gather_out`` every output ends with the whole product once each
+    handle's stream has completed (``Handle.synchronize``)."""
+    import ctypes as C
+
+    from . import _abi, _descriptor
+    n = len(handles)
+    if not (len(a_windows) == len(b_replicas) == len(outs) == n):
+        raise ValueError("one A window, B replica and output per handle")
+    hs = (C.c_void_p * n)(*[h.ptr for h in handles])
+    da = (_abi.KxTensor * n)(*[_descriptor(t) for t in a_windows])
+    db = (_abi.KxTensor * n)(*[_descriptor(t) for t in b_replicas])
+    do = (_abi.KxTensor * n)(*[_descriptor(t) for t in outs])
+    err = _abi.KxError()
+    rc = _abi.lib.kx_gemm_sharded_f32(hs, n, da, db, do, int(bool(gather_out)), C.byref(err))
+    _abi.raise_for(rc, err)
+
+
 def sharded_matmul(a_pieces, b, c, plan: RowPlan, rank: int, group=None,
                    matmul_into: Callable | None = None, streams=None, scratch=None) -> None:
     """Compute this rank's pieces and all-gather them into ``c`` (M x N).

@@ -250,3 +250,41 @@ def test_descriptors_carry_layout_exactly():
         kx._descriptor(kx.TensorView(buf, (1,) * (kx.MAX_RANK + 1), (1,) * (kx.MAX_RANK + 1)))
     with pytest.raises(kx.LayoutError):
         kx._descriptor(kx.TensorView(buf, (3, 4), (4,)))
+
+
+def test_gemm_sharded_checks_every_argument_before_any_work():
+    """kx_gemm_sharded_f32 (host side): null and count errors, then per handle
+    the window rows of A, B's shape, the outputs' shape, contiguity and
+    aliasing -- all before anything is enqueued, so a handle is never touched
+    (the stand-in handles here are zeroed host memory)."""
+    fake = (C.c_uint8 * 65536)()
+    hs = (C.c_void_p * 2)(C.addressof(fake), C.addressof(fake))
+    m, k, n = 5, 3, 4
+
+    def call(a, b, out, gather=1, ngpu=2):
+        err = _abi.KxError()
+        rc = _abi.lib.kx_gemm_sharded_f32(hs, ngpu, (_abi.KxTensor * 2)(*a), (_abi.KxTensor * 2)(*b),
+                                          (_abi.KxTensor * 2)(*out), gather, C.byref(err))
+        return rc, err
+
+    # windows of 5 rows over 2 handles: 3 and 2 rows
+    a = [_tensor([3, k], [k, 1], 0, 3 * k, 0x10000), _tensor([2, k], [k, 1], 0, 2 * k, 0x20000)]
+    b = [_tensor([k, n], [n, 1], 0, k * n, 0x30000), _tensor([k, n], [n, 1], 0, k * n, 0x40000)]
+    out = [_tensor([m, n], [n, 1], 0, m * n, 0x50000), _tensor([m, n], [n, 1], 0, m * n, 0x60000)]
+    rc, err = call(a, b, [_tensor([m * n], [1], 0, m * n, 0x50000)] * 2)
+    assert rc == _abi.KX_E_PARAM and err.parameter == b"rank-two outputs"
+    rc, err = call([a[1], a[0]], b, out)
+    assert rc == _abi.KX_E_PARAM and (err.values[0], err.values[1]) == (0, 3)
+    rc, err = call(a, [b[0], _tensor([k, n + 1], [n + 1, 1], 0, k * (n + 1), 0x40000)], out)
+    assert rc == _abi.KX_E_PARAM and err.parameter == b"b[r] must be [K, N]" and err.values[0] == 1
+    rc, err = call(a, b, [out[0], _tensor([m, n + 1], [n + 1, 1], 0, m * (n + 1), 0x60000)])
+    assert rc == _abi.KX_E_LAYOUT and _abi.LAYOUT_ERRORS[err.values[0]] == "OutputShapeMismatch"
+    rc, err = call(a, b, [out[0], _tensor([m, n], [1, m], 0, m * n, 0x60000)])
+    assert rc == _abi.KX_E_LAYOUT and _abi.LAYOUT_ERRORS[err.values[0]] == "OutputNotCContiguous"
+    rc, err = call(a, b, [out[0], _tensor([m, n], [n, 1], 0, m * n, 0x20000)])      # over a[1]
+    assert rc == _abi.KX_E_ALIAS
+    rc, err = call(a, b, [out[0], out[0]])
+    assert rc == _abi.KX_E_ALIAS and err.parameter == b"gathered outputs overlap"
+    empty = [_tensor([0, k], [k, 1], 0, 0, 0x10000)] * 2
+    zero_out = [_tensor([0, n], [n, 1], 0, 0, 0x50000), _tensor([0, n], [n, 1], 0, 0, 0x60000)]
+    assert call(empty, b, zero_out)[0] == _abi.KX_OK               # nothing to compute or copy
