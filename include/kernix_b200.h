@@ -18,6 +18,7 @@
  *   - softmax                           crates/kernix-ops/src/ops/math.rs:398-465,531-536
  *   - tensordot                         crates/kernix-ops/src/ops/linalg_extra.rs:164-276
  *   - CpuExecutor::matmul_into          crates/kernix-ops/src/execution.rs:149-240
+ *     (its row chunks per worker, execution.rs:188-233: the sharded entries)
  *   - Config / Context::new ([cuda])    crates/kernix/src/config.rs:28-40,84-95,133-137
  *   - Tape::matmul backward (VJP)       crates/kernix/src/autograd.rs:622-690
  *   - conv2d_backward                   crates/kernix-ops/src/neural.rs:379-430
