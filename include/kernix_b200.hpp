@@ -18,6 +18,7 @@
 //                                  linalg_extra.rs:164-276, autograd.rs:622-690,
 //                                  neural.rs:379-430, execution.rs:149-240
 //   kernix::shard_window / row_piece   the work split across the GPUs of a node
+//   kernix::gemm_sharded           one process over several GPUs (kx_gemm_sharded_f32)
 // Errors are exceptions carrying the C ABI's kx_error record; hooks return bool
 // exactly like the reference (false => nothing written).
 #pragma once
@@ -403,5 +404,29 @@ class CudaExecutor {
     Handle h_;
     int device_;
 };
+
+// The row-sharded f32 product from one process over several executors, one
+// per GPU (kx_gemm_sharded_f32): executor r multiplies a_windows[r] (window r
+// of A's rows, shard_window(M, r, n)) by b[r] into the same rows of out[r];
+// with `gather` every output holds the whole product once each executor has
+// synchronized.  Reference counterpart: CpuExecutor::matmul_into's row chunks
+// per worker (execution.rs:188-233).
+inline void gemm_sharded(const std::vector<const CudaExecutor *> &execs,
+                         const std::vector<DeviceTensor<float>> &a_windows, const std::vector<DeviceTensor<float>> &b,
+                         const std::vector<DeviceTensor<float>> &out, bool gather = true) {
+    const size_t n = execs.size();
+    if (a_windows.size() != n || b.size() != n || out.size() != n) throw OpsError(KX_E_PARAM);
+    std::vector<kx_handle *> hs(n);
+    std::vector<kx_tensor> da(n), db(n), dout(n);
+    for (size_t r = 0; r < n; ++r) {
+        if (!execs[r]) throw OpsError(KX_E_PARAM);
+        hs[r] = execs[r]->handle();
+        da[r] = a_windows[r].desc();
+        db[r] = b[r].desc();
+        dout[r] = out[r].desc();
+    }
+    kx_error e{};
+    check(kx_gemm_sharded_f32(hs.data(), (uint32_t)n, da.data(), db.data(), dout.data(), gather ? 1 : 0, &e), e);
+}
 
 }  // namespace kernix

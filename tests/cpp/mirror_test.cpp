@@ -55,6 +55,14 @@ static void host_checks() {
     EXPECT((kernix::shard_window(16, 0, 3) == U2(0, 6)));
     EXPECT((kernix::shard_window(16, 2, 3) == U2(11, 5)));
     EXPECT((kernix::row_piece(8192, 8, 512) == U2(512, 2)));
+    // no executors: refused before anything runs
+    threw = false;
+    try {
+        kernix::gemm_sharded({}, {}, {}, {});
+    } catch (const kernix::OpsError &e) {
+        threw = e.status() == KX_E_PARAM;
+    }
+    EXPECT(threw);
 }
 
 static void gpu_checks() {
@@ -162,6 +170,38 @@ static void gpu_checks() {
         acc = acc + prod;
     }
     EXPECT(ov1.size() == 1 && ov1[0] == acc);
+    // one process over two executors (both on device 0 here): windows of 3
+    // and 2 rows, every output gathered to the whole product
+    {
+        const uint64_t m = 5, k = 7, n = 6;
+        std::vector<float> av(m * k), bv(k * n);
+        for (size_t i = 0; i < av.size(); ++i) av[i] = (float)((int)(i % 9) - 4) / 4.0f;
+        for (size_t i = 0; i < bv.size(); ++i) bv[i] = (float)((int)(i % 5) - 2) / 2.0f;
+        kernix::CudaExecutor e0(0), e1(0);
+        std::vector<const kernix::CudaExecutor *> ex = {&e0, &e1};
+        std::vector<kernix::DeviceTensor<float>> aw, br, outs;
+        for (uint32_t r = 0; r < 2; ++r) {
+            auto w = kernix::shard_window(m, r, 2);
+            const kernix::CudaExecutor &x = *ex[r];
+            aw.push_back(x.upload<float>(std::vector<float>(av.begin() + w.first * k,
+                                                            av.begin() + (w.first + w.second) * k),
+                                         {w.second, k}));
+            br.push_back(x.upload<float>(bv, {k, n}));
+            outs.push_back(x.upload<float>(std::vector<float>(m * n, -1.0f), {m, n}));
+        }
+        kernix::gemm_sharded(ex, aw, br, outs, true);
+        e0.synchronize();
+        e1.synchronize();
+        auto o0 = e0.download(outs[0]), o1 = e1.download(outs[1]);
+        bool exact = o0 == o1;
+        for (uint64_t i = 0; i < m; ++i)
+            for (uint64_t j = 0; j < n; ++j) {
+                double s = 0;       // dyadic data: every product and sum is exact in f32
+                for (uint64_t q = 0; q < k; ++q) s += (double)av[i * k + q] * bv[q * n + j];
+                exact = exact && (double)o0[i * n + j] == s;
+            }
+        EXPECT(exact);
+    }
 }
 
 int main(int argc, char **argv) {
