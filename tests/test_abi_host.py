@@ -288,3 +288,11 @@ def test_gemm_sharded_checks_every_argument_before_any_work():
     empty = [_tensor([0, k], [k, 1], 0, 0, 0x10000)] * 2
     zero_out = [_tensor([0, n], [n, 1], 0, 0, 0x50000), _tensor([0, n], [n, 1], 0, 0, 0x60000)]
     assert call(empty, b, zero_out)[0] == _abi.KX_OK               # nothing to compute or copy
+
+
+def test_gemm_sharded_wrapper_needs_one_of_each_per_handle():
+    """kernix_b200.sharded.gemm_sharded: one A window, B replica and output per
+    handle, refused on the host before the library is called."""
+    from kernix_b200.sharded import gemm_sharded
+    with pytest.raises(ValueError):
+        gemm_sharded([object(), object()], [None], [None, None], [None, None])

@@ -248,6 +248,43 @@ def test_matmul_backward_oracle_known_answers():
         assert np.array_equal(db, np.broadcast_to(a.sum(axis=0)[:, None], (k, n)))
 
 
+def _tape_values(dims, offset):
+    """values (kernix/tests/autograd_tensor_tests.rs:7-16)."""
+    count = int(np.prod(dims, dtype=np.int64))
+    return (((np.arange(count) * 7 + offset) % 19) / 13.0 - 0.6).reshape(dims)
+
+
+@pytest.mark.parametrize("ad,bd,out", [
+    ((3,), (3,), ()), ((3,), (3, 2), (2,)), ((2, 3), (3,), (2,)), ((3,), (2, 3, 2), (2, 2)),
+    ((2, 2, 3), (3,), (2, 2)), ((2, 1, 2, 3), (1, 3, 3, 2), (2, 3, 2, 2)),
+    ((2, 1, 2, 3), (3, 3, 2), (2, 3, 2, 2)), ((2, 3), (4, 3, 2), (4, 2, 2)),
+    ((4, 2, 3), (3, 2), (4, 2, 2)), ((1, 1, 1, 2, 3), (2, 3, 2), (1, 1, 2, 2, 2)),
+], ids=lambda v: "x".join(map(str, v)) or "scalar")
+def test_matmul_backward_oracle_central_differences(ad, bd, out):
+    """matmul_fd over matmul_vector_matrix_and_broadcast_batch_finite_differences
+    (autograd_tensor_tests.rs:35-88) on the oracle: its VJP of sum(y * seed)
+    against central differences of its ordered forward product (h = 1e-6,
+    |a - n| <= 3e-7 (1 + |a| + |n|))."""
+    a, b, seed = _tape_values(ad, 1), _tape_values(bd, 5), _tape_values(out, 3)
+
+    def objective(l, r):
+        y = oracle.matmul_reference(oracle.View.of(l), oracle.View.of(r))
+        assert y.shape == out
+        return float((np.asarray(y).reshape(-1) * seed.reshape(-1)).sum())
+    da, db = oracle.matmul_backward(a, b, seed)
+    h = 1e-6
+    for side, (inp, grad) in enumerate(((a, da), (b, db))):
+        assert grad.shape == inp.shape
+        for i in range(inp.size):
+            hi, lo = inp.copy().reshape(-1), inp.copy().reshape(-1)
+            hi[i] += h
+            lo[i] -= h
+            hi, lo = hi.reshape(inp.shape), lo.reshape(inp.shape)
+            num = objective(a, hi) - objective(a, lo) if side else objective(hi, b) - objective(lo, b)
+            g, n = float(grad.reshape(-1)[i]), num / (2 * h)
+            assert abs(g - n) <= 3e-7 * (1 + abs(g) + abs(n)), (side, i, g, n)
+
+
 def test_tensordot_oracle_known_answers_and_errors():
     """tensordot_contracts_arbitrary_axes_and_empty_k and
     tensordot_scalar_outer_and_zero_result_shapes (ops_completeness_03.rs:
