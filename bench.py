@@ -715,6 +715,13 @@ def _im2col(x: np.ndarray, kh: int, kw: int, pad: int) -> np.ndarray:
     return cols.reshape(c * kh * kw, n * oh * ow)
 
 
+def _cpu_line(flops, seconds, cores, sample):
+    """The host-CPU restatement of the reference's path for one configuration,
+    timed on a bounded sample (kind "port": the oracle's C restatements)."""
+    return {"value": round(flops / max(seconds, 1e-9) / 1e12, 6), "unit": "TFLOP/s", "cores": int(cores),
+            "kind": "port", "sample": sample}
+
+
 def run_workload(w, steps, warmup, rank=0, world=1, local=0, batch=0, size=0):
     """Measure one of c1..c4 and check the timed output against the oracle.
 
@@ -764,7 +771,12 @@ def run_workload(w, steps, warmup, rank=0, world=1, local=0, batch=0, size=0):
         va, vb = oracle.View.of(a_np), oracle.View.of(b_np)
         exp, ab = oracle.gemm_dot2(va, vb)
         ours = err_metrics(c.cpu().numpy(), exp, ab)
-        eng = err_metrics(oracle.engine_gemm(va, vb, threads=1), exp, ab)
+        t0 = time.perf_counter()
+        eng_c = oracle.engine_gemm(va, vb, threads=1)
+        res["cpu_baseline"] = _cpu_line(flops, time.perf_counter() - t0, 1,
+                                        "the whole product, blocked fp32 engine restatement on one thread "
+                                        "(Kernix's default Parallelism::None; stand-in for gemm-f32)")
+        eng = err_metrics(eng_c, exp, ab)
         check = {"outputs_checked": 512 * 512, **ours, "bound": 2e-6, "normwise_bound": 1e-5,
                  "elementwise_target": 1e-5, "cpu_fp32_engine": eng,
                  "pass": ours["max_err_over_sum_abs"] <= 2e-6 and ours["normwise"] <= 1e-5}
@@ -787,7 +799,12 @@ def run_workload(w, steps, warmup, rank=0, world=1, local=0, batch=0, size=0):
         va, vb = oracle.View.of(sub), oracle.View(bt_np, (n, n), (1, n))
         exp, ab = oracle.gemm_dot2(va, vb)
         ours = err_metrics(c[rows].cpu().numpy(), exp, ab)
-        eng = err_metrics(oracle.engine_gemm(va, vb, threads=threads), exp, ab)
+        t0 = time.perf_counter()
+        eng_c = oracle.engine_gemm(va, vb, threads=threads)
+        res["cpu_baseline"] = _cpu_line(2.0 * len(rows) * n * n, time.perf_counter() - t0, threads,
+                                        f"{len(rows)} rows of C, blocked f64 engine restatement with B read "
+                                        "through its transposed view (stand-in for matrixmultiply)")
+        eng = err_metrics(eng_c, exp, ab)
         check = {"rows_checked": len(rows), **ours, "bound": 1e-13, "elementwise_target": 1e-12,
                  "cpu_f64_engine": eng,
                  "pass": ours["max_err_over_sum_abs"] <= 1e-13 and ours["max_rel_err_elementwise"] <= 1e-12}
@@ -851,6 +868,25 @@ def run_workload(w, steps, warmup, rank=0, world=1, local=0, batch=0, size=0):
             eng.append(err_metrics(e32[None], truth, absv))
         del oc
 
+        if rank == 0:
+            # the reference's path for one (batch, head) pair, timed and scaled
+            # to the whole job: S through the ordered general fallback (K^T is
+            # a view), softmax_temperature, P V through the blocked engine
+            try:
+                qh, kh, vh = (x[0, 0].cpu().numpy() for x in (q, k_, v_))
+                t0 = time.perf_counter()
+                s_ref = oracle.matmul_reference(oracle.View.of(qh), oracle.View(kh, (128, 2048), (1, 128)))
+                p_ref = oracle.softmax_temperature(s_ref, -1, t)
+                oracle.engine_gemm(oracle.View.of(p_ref), oracle.View.of(vh), threads=1)
+                pair_s = time.perf_counter() - t0
+                res["cpu_baseline"] = _cpu_line(
+                    flops, pair_s * total * 32, 1,
+                    f"one (batch, head) pair in {pair_s:.2f} s, extrapolated x{total * 32}: S by the ordered "
+                    "general-fallback restatement (linalg.rs:176-213), softmax_temperature, P V by the blocked "
+                    "engine (stand-in for gemm-f32)")
+            except Exception as e:      # a baseline, never a reason to lose the line
+                res["cpu_baseline"] = {"unavailable": f"{type(e).__name__}: {e}"}
+
         def worst(lst):
             return {kk: max(e[kk] for e in lst) for kk in lst[0]}
         wo, wc, we = worst(ours), worst(comp), worst(eng)
@@ -900,8 +936,12 @@ def run_workload(w, steps, warmup, rank=0, world=1, local=0, batch=0, size=0):
         got = y[imgs].cpu().numpy()
         ours = err_metrics(got, d2, ab)
         # the reference's lowering on the CPU: im2col, then the blocked engine
+        t0 = time.perf_counter()
         cols = _im2col(xs, 3, 3, 1)
         eng = oracle.engine_gemm(oracle.View.of(w_np.reshape(256, 1152)), oracle.View.of(cols), threads=threads)
+        res["cpu_baseline"] = _cpu_line(2.0 * 256 * 1152 * len(imgs) * 56 * 56, time.perf_counter() - t0, threads,
+                                        f"{len(imgs)} images: im2col then the blocked fp32 engine restatement "
+                                        "(neural.rs:212-302 lowering; stand-in for gemm-f32)")
         eng = eng.reshape(256, len(imgs), 56, 56).transpose(1, 0, 2, 3)
         eng_err = err_metrics(eng, d2, ab)
         vals = _max_over_ranks([ours[k] for k in ours], world, dev)
@@ -1017,7 +1057,7 @@ def main():
                 if r is not None:
                     per[w] = {k: r[k] for k in ("value", "unit", "ms_per_step", "steps", "warmup", "dtype", "kernel",
                                                 "gpu_launches", "check", "roofline", "clocks", "config")}
-                    for extra in ("parts", "cuda_graph"):
+                    for extra in ("parts", "cuda_graph", "cpu_baseline"):
                         if extra in r:
                             per[w][extra] = r[extra]
             if res is not None:
