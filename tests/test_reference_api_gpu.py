@@ -20,7 +20,9 @@
   gradients of zero extents, a shared operand on both sides, reversed and
   transposed views with a constant side;
 * the direct-memory and reversed-axis products of
-  kernix-ops/tests/numeric_dispatch_04.rs:116-152.
+  kernix-ops/tests/numeric_dispatch_04.rs:116-152;
+* the reconstruction products of kernix-ops/tests/linalg_tests.rs:13-57,
+  100-137 (LU, inverse, QR, least squares) with host-computed factors.
 """
 import numpy as np
 import pytest
@@ -294,3 +296,48 @@ def test_direct_memory_and_reversed_matrix_products(kx, torch_cuda, dtype):
     assert tuple(d.shape) == () and float(d.cpu()) == 32.0
     rev = kx.TensorView(dev(torch, a).reshape(-1), (2, 3), (3, -1), 2)
     assert kx.matmul(rev, dev(torch, b)).cpu().numpy().reshape(-1).tolist() == [50, 56, 131, 146]
+
+
+def _near12(a, b):
+    """near (kernix-ops/tests/linalg_tests.rs:7-12)."""
+    assert abs(a - b) <= 2e-12 * (1.0 + abs(a) + abs(b)), (a, b)
+
+
+def test_decomposition_reconstruction_products(kx, torch_cuda):
+    """The matmul checks of linalg_tests.rs:13-57 and 100-137 on the device,
+    with the factors computed on the host: P A = L U, A inverse(A) = I, Q R = A
+    for a tall and a wide matrix, Q^T Q = I through Q's transposed view, and
+    the least-squares normal equations A^T (A x - b) = 0 with A^T a view."""
+    import scipy.linalg as sl
+    torch = torch_cuda
+
+    def mm(x, y):
+        return kx.matmul(x if isinstance(x, kx.TensorView) else dev(torch, x),
+                         y if isinstance(y, kx.TensorView) else dev(torch, y)).cpu().numpy()
+    a = np.array([0.0, 2.0, 1.0, 1.0, 1.0, 0.0, 2.0, 0.0, 1.0]).reshape(3, 3)
+    p, low, up = sl.lu(a)                              # a = p @ low @ up
+    prod = mm(low, up)
+    pa = p.T @ a
+    for i in range(3):
+        for j in range(3):
+            _near12(prod[i, j], pa[i, j])
+    ident = mm(a, np.linalg.inv(a))
+    for i in range(3):
+        for j in range(3):
+            _near12(ident[i, j], 1.0 if i == j else 0.0)
+    tall = np.array([1.0, 0.0, 1.0, 1.0, 1.0, 2.0]).reshape(3, 2)
+    for mat in (tall, np.arange(1.0, 7.0).reshape(2, 3)):
+        q, r = np.linalg.qr(mat)
+        for x, y in zip(mm(q, r).reshape(-1), mat.reshape(-1)):
+            _near12(x, y)
+    q, r = np.linalg.qr(tall)
+    qbuf = dev(torch, q).reshape(-1)
+    qt = kx.TensorView(qbuf, (2, 3), (1, 2), 0)         # q.transpose(), zero-copy
+    for x, y in zip(mm(qt, kx.TensorView(qbuf, (3, 2), (2, 1), 0)).reshape(-1), [1.0, 0.0, 0.0, 1.0]):
+        _near12(x, y)
+    x_ls = np.array([7.0 / 6.0, 0.5])
+    b = np.array([1.0, 2.0, 2.0])
+    residual = mm(tall, x_ls) - b
+    _near12(float(np.linalg.norm(residual)), (1.0 / 6.0) ** 0.5)
+    at = kx.TensorView(dev(torch, tall).reshape(-1), (2, 3), (1, 2), 0)
+    _near12(float(np.linalg.norm(mm(at, residual))), 0.0)
