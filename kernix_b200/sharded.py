@@ -11,23 +11,25 @@ communication stream while piece ``i + 1`` is being multiplied.
 
 Three ways to gather on GPUs:
 
-* ``ReplicatedOutput`` + ``sharded_matmul_replicated`` (the default when the
-  node has NVLink multicast, NVLS): C lives in symmetric memory bound to an
-  NVLink multicast object; the GEMM's epilogue stores every output element
-  once through the multicast address and the NVSwitch delivers it to every
-  rank's C.  Each rank sends its rows once instead of once per peer, the
-  gather overlaps the GEMM's later tiles, and one small all-reduce closes the
-  step.
 * ``PeerOutput`` + ``sharded_matmul_push`` (or symmetric memory +
-  ``sharded_matmul_push_mc``): C lives in library-allocated memory that every
-  rank maps into every other rank (CUDA IPC over NVLink).  The library's
-  ``kx_matmul_rows_sharded_f32`` computes the rank's pieces and pushes each
-  into the same rows of every peer's C: with the copy engines, one stream per
-  peer, while the next piece multiplies, and the last piece with an all-SM
-  kernel (or one NVLink multicast store); one 4-byte NCCL all-reduce at the
-  end of the step tells every rank that all pushes into its C have landed.
+  ``sharded_matmul_push_mc``, the bench's default where the node has NVLink
+  multicast, NVLS): C lives in memory that every rank maps into every other
+  rank (CUDA IPC over NVLink).  The library's ``kx_matmul_rows_sharded_f32``
+  computes the rank's pieces and pushes each into the same rows of every
+  peer's C: with the copy engines, one stream per peer, while the next piece
+  multiplies, and the last piece with one NVLink multicast store (or an
+  all-SM kernel); one 4-byte NCCL all-reduce at the end of the step tells
+  every rank that all pushes into its C have landed.
+* ``ReplicatedOutput`` + ``sharded_matmul_replicated``: C lives in symmetric
+  memory bound to an NVLink multicast object; the GEMM's epilogue stores
+  every output element once through the multicast address and the NVSwitch
+  delivers it to every rank's C, and one small all-reduce closes the step.
 * ``sharded_matmul`` with ``all_gather_into_tensor`` per piece (NCCL; also the
   gloo path the CPU tests use).
+
+``gemm_sharded`` is the single-process form (``kx_gemm_sharded_f32``): one
+handle per GPU in one process, a contiguous window of rows per handle, the
+windows copied between the outputs by the copy engines.
 
 This is the multi-worker counterpart of ``CpuExecutor::matmul_into``'s row
 chunking (crates/kernix-ops/src/execution.rs:188-233), lifted from threads in
