@@ -12,8 +12,9 @@ NVLink, so ``scaling`` is strong (fixed total work).
 N > 1 runs under ``python -m torch.distributed.run --nproc-per-node N``.  Rank 0
 prints one JSON line.  After the headline, the line carries ``per_config``: c1
 and c2 (one GPU only: replicas) and c3 and c4 (their batch split over the
-ranks), each timed on device-resident seeded inputs with its own clock record
-and a parity check of the timed output against the oracle.
+ranks), each timed on device-resident seeded inputs with its own clock record,
+a parity check of the timed output against the oracle and a CPU baseline of
+the reference's path on a bounded sample.
 ``--workload c1|c2|c3|c4`` measures one of them alone and prints its own line.
 """
 from __future__ import annotations
